@@ -1,0 +1,282 @@
+/*
+ * tmllm.h — C ABI of the B200 (sm_100a) KV-cache decode path.
+ *
+ * This is the drop-in boundary for Lee-Dongwook/RustLLM's per-layer KV-cache decode
+ * path: the KV-cache append, concat_sequence, repeat_kv and the GQA attention chain
+ * (QK^T -> scale/mask -> softmax -> PV).  A Rust `build.rs` links `libtmllm_b200.so`
+ * and binds these functions with `extern "C"`; INTEGRATION.md shows the binding.
+ *
+ * Conventions
+ *  - Every function returns an `int` status (tmllm_status).  0 is success.  Non-zero
+ *    codes map one-to-one onto the reference's `TinyError` variants (src/error.rs:3-43)
+ *    plus three codes the new runtime needs.  tmllm_last_error() returns a
+ *    human-readable message for the calling thread's last failure.
+ *  - Arguments are validated on the host BEFORE anything is enqueued or mutated; a
+ *    rejected call leaves every buffer and every cache length unchanged (the reference's
+ *    rule, src/model/kv_cache.rs:18-53 and its test at :295-306).
+ *  - Tensor arguments are device pointers to dense row-major data in the given dtype.
+ *  - Work is enqueued on `stream` (NULL = the legacy default stream) and is asynchronous.
+ *    Nothing here synchronises the device except tmllm_sync and the setup-time bulk
+ *    copies documented on tmllm_cache_reserve.
+ *  - A cache handle is not thread-safe (the reference's MetalContext is !Sync,
+ *    src/metal/context.rs:14-17).
+ *  - There is no CPU fallback: on a machine without a usable sm_100 device every call
+ *    that needs the GPU returns TMLLM_DEVICE_ERROR.
+ */
+#ifndef TMLLM_H
+#define TMLLM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without pulling in the CUDA headers. */
+typedef struct CUstream_st* tmllm_stream;
+
+typedef enum tmllm_status {
+    TMLLM_OK = 0,
+    TMLLM_INVALID_ARGUMENT = 1,      /* TinyError::InvalidArgument      src/error.rs:4 */
+    TMLLM_INVALID_SHAPE = 2,         /* TinyError::InvalidShape         src/error.rs:5 */
+    TMLLM_SHAPE_MISMATCH = 3,        /* TinyError::ShapeMismatch        src/error.rs:6-9 */
+    TMLLM_INVALID_DIMENSION = 4,     /* TinyError::InvalidDimension     src/error.rs:10 */
+    TMLLM_UNSUPPORTED_DTYPE = 5,     /* TinyError::UnsupportedDType     src/error.rs:17 */
+    TMLLM_NON_CONTIGUOUS = 6,        /* TinyError::NonContiguousTensor  src/error.rs:18 */
+    TMLLM_POSITION_OUT_OF_RANGE = 7, /* TinyError::PositionOutOfRange   src/error.rs:19-23 */
+    TMLLM_MODEL_FORMAT = 8,          /* TinyError::ModelFormat          src/error.rs:31 */
+    TMLLM_DEVICE_ERROR = 9,          /* TinyError::Metal -> a CUDA runtime error */
+    TMLLM_OUT_OF_BLOCKS = 10,        /* new: the paged block pool is exhausted */
+    TMLLM_TIMEOUT = 11,              /* new: a bounded device-side wait expired */
+    TMLLM_NOT_RESERVED = 12          /* new: a write targets a position with no block */
+} tmllm_status;
+
+/* src/tensor (DType::{F32, F16}) */
+typedef enum tmllm_dtype { TMLLM_F32 = 0, TMLLM_F16 = 1 } tmllm_dtype;
+
+/* ---------------------------------------------------------------------------------- */
+/* Library                                                                             */
+/* ---------------------------------------------------------------------------------- */
+
+/* ABI version (major*10000 + minor*100 + patch). */
+int tmllm_version(void);
+/* Static name of a status code ("TMLLM_INVALID_SHAPE", ...). */
+const char* tmllm_status_name(int status);
+/* Message of the calling thread's most recent failure ("" if none). */
+const char* tmllm_last_error(void);
+/* Blocks until all work on `stream` is done (MetalExecution::finish's wait,
+ * src/metal/execution.rs:30-36). */
+int tmllm_sync(tmllm_stream stream);
+
+/* ---------------------------------------------------------------------------------- */
+/* Op-level entry points (stateless; contiguous device tensors)                        */
+/* ---------------------------------------------------------------------------------- */
+
+/* Replaces kv_cache_write_f32/_f16[_encode] (src/ops/kv_cache_write.rs:9-141):
+ * cache [num_heads, max_seq, head_dim] (a LayerKvCache buffer, batch 1),
+ * source [num_heads, source_seq, head_dim]; writes positions [start, start+source_seq).
+ * Errors: POSITION_OUT_OF_RANGE when start+source_seq > max_seq (:577-586). */
+int tmllm_kv_cache_write(tmllm_dtype dtype, void* cache, const void* source, size_t num_heads,
+                         size_t max_seq, size_t head_dim, size_t start, size_t source_seq,
+                         tmllm_stream stream);
+
+/* Replaces concat_sequence_f32 (src/ops/concat_sequence.rs:13-115), extended to F16:
+ * out [B,H,Sl+Sr,D] = left [B,H,Sl,D] ++ right [B,H,Sr,D] along the sequence axis. */
+int tmllm_concat_sequence(tmllm_dtype dtype, const void* left, const void* right, void* out,
+                          size_t batch, size_t num_heads, size_t left_seq, size_t right_seq,
+                          size_t head_dim, tmllm_stream stream);
+
+/* Replaces Tensor::repeat_kv / repeat_kv (src/tensor/repeat_kv.rs:13-81,
+ * src/tensor/tensor.rs:686-688): out [B,Hkv*r,S,D][b,qh] = in [B,Hkv,S,D][b,qh/r].
+ * repeats == 1 copies the input (the reference returns the same tensor, :27-29). */
+int tmllm_repeat_kv(tmllm_dtype dtype, const void* in, void* out, size_t batch,
+                    size_t kv_heads, size_t seq_len, size_t head_dim, size_t repeats,
+                    tmllm_stream stream);
+
+/* Replaces gqa_qk_matmul[_encode] (src/tensor/gqa_matmul.rs:16-62): scores
+ * [B,Hq,Sq,L] = Q [B,Hq,Sq,D] . K^T where K is read as [B,Hkv,kv_capacity,D] for its
+ * first kv_len rows (the `narrow` view of a cache, gqa_matmul.rs:59).  F16 stores
+ * half(sum) of an F32 sum over d in increasing order (gqa_matmul.metal:319). */
+int tmllm_gqa_qk(tmllm_dtype dtype, const void* q, const void* k, void* out, size_t batch,
+                 size_t q_heads, size_t kv_heads, size_t q_len, size_t kv_len,
+                 size_t head_dim, size_t kv_capacity, tmllm_stream stream);
+
+/* Replaces gqa_pv_matmul[_encode] (src/tensor/gqa_matmul.rs:65-105): out [B,Hq,Sq,D] =
+ * P [B,Hq,Sq,L] . V with V read as [B,Hkv,kv_capacity,D]. */
+int tmllm_gqa_pv(tmllm_dtype dtype, const void* probs, const void* v, void* out,
+                 size_t batch, size_t q_heads, size_t kv_heads, size_t q_len, size_t kv_len,
+                 size_t head_dim, size_t kv_capacity, tmllm_stream stream);
+
+/* Replaces Tensor::attention_scale_mask (src/tensor/tensor.rs:604-668,
+ * src/ops/attention_scale_mask.rs:10-216): scores [..., query_len, key_len];
+ * key > start + q ? -inf : x*scale.  Errors mirror attention_scale_mask.rs:120-160. */
+int tmllm_attention_scale_mask(tmllm_dtype dtype, const void* in, void* out, size_t numel,
+                               size_t query_len, size_t key_len, size_t query_start_pos,
+                               float scale, tmllm_stream stream);
+
+/* Replaces Tensor::softmax_last_dim (src/tensor/tensor.rs:458-495, src/ops/softmax.rs):
+ * stable row softmax over `width`; F16 rows that are entirely -inf become zeros. */
+int tmllm_softmax_last_dim(tmllm_dtype dtype, const void* in, void* out, size_t rows,
+                           size_t width, tmllm_stream stream);
+
+/* Replaces Tensor::batched_matmul (src/tensor/tensor.rs:497-602,
+ * src/ops/batched_matmul.rs): out [batch,m,n] = a [batch,m,k] . b [batch,k,n]. */
+int tmllm_batched_matmul(tmllm_dtype dtype, const void* a, const void* b, void* out,
+                         size_t batch, size_t m, size_t k, size_t n, tmllm_stream stream);
+
+/* Replaces RotaryEmbedding::new's table build (src/nn/rope.rs:44-62).  Fills HOST
+ * arrays cos/sin [max_seq_len, head_dim/2] in F32, as the reference does on the CPU. */
+int tmllm_rope_tables(float* cos_table, float* sin_table, size_t head_dim,
+                      size_t max_seq_len, float theta);
+
+/* Replaces rope / rope_encode (src/ops/rope.rs:277-370): in/out [rows, seq_len, head_dim]
+ * (rows = batch*heads), device tables [table_len, head_dim/2] F32; half-split pairs
+ * (i, i+D/2) at positions start_pos + s. */
+int tmllm_rope(tmllm_dtype dtype, const void* in, void* out, const float* cos_table,
+               const float* sin_table, size_t table_len, size_t rows, size_t seq_len,
+               size_t head_dim, size_t start_pos, tmllm_stream stream);
+
+/* ---------------------------------------------------------------------------------- */
+/* Fused paged decode attention (the hot path)                                         */
+/* ---------------------------------------------------------------------------------- */
+
+/* A block-paged KV store for one layer.  Each arena is
+ *   [num_blocks, num_kv_heads, block_size, head_dim]  (dtype),
+ * so element (h, pos, d) of sequence s is at
+ *   ((block_table[s*max_blocks_per_seq + pos/block_size]*num_kv_heads + h)*block_size
+ *     + pos%block_size)*head_dim + d.
+ * With block_size == capacity and one block per sequence this is exactly the
+ * reference's LayerKvCache buffer [1, Hkv, max_seq, D] (src/model/kv_cache.rs:66). */
+typedef struct tmllm_paged_kv {
+    void* k_cache;
+    void* v_cache;
+    const int32_t* block_table; /* device, [num_seqs, max_blocks_per_seq] */
+    const int32_t* seq_lens;    /* device, [num_seqs]: tokens cached before this call */
+    int64_t num_blocks;
+    int32_t num_seqs;
+    int32_t num_kv_heads;
+    int32_t head_dim;
+    int32_t block_size;
+    int32_t max_blocks_per_seq;
+    int32_t dtype;              /* tmllm_dtype */
+} tmllm_paged_kv;
+
+/* Optional inputs of tmllm_gqa_decode. */
+typedef struct tmllm_decode_opts {
+    float scale;            /* logit scale; <= 0 means 1/sqrt(head_dim) (attention.rs:236) */
+    int32_t num_splits;     /* sequence splits per (seq, kv head); 0 = automatic */
+    int32_t out_dtype;      /* tmllm_dtype of `out` (F32 is used for cross-GPU partials) */
+    const float* rope_cos;  /* optional device RoPE tables [rope_len, head_dim/2]; when   */
+    const float* rope_sin;  /* given, q and k_new are rotated at position               */
+    int32_t rope_len;       /* seq_lens[s] + rope_pos_offset (attention.rs:202-207)     */
+    int32_t rope_pos_offset;
+    int64_t max_len_hint;   /* longest sequence this call sees, for the split choice;  */
+                            /* 0 = the capacity.  Affects speed only, never results.   */
+} tmllm_decode_opts;
+
+/* Bytes of scratch tmllm_gqa_decode needs for `num_splits` splits (0 = enough for any
+ * automatic choice for this shape on this device).  Zero it once (tmllm_decode_workspace_init)
+ * before its first use; every successful call leaves it ready for the next. */
+size_t tmllm_decode_workspace_bytes(int32_t num_seqs, int32_t q_heads, int32_t kv_heads,
+                                    int32_t head_dim, int32_t num_splits);
+int tmllm_decode_workspace_init(void* workspace, size_t bytes, tmllm_stream stream);
+/* The split count tmllm_gqa_decode chooses when opts->num_splits == 0. */
+int32_t tmllm_decode_auto_splits(int32_t num_seqs, int32_t kv_heads, int64_t max_len);
+
+/* Fused KV-append + GQA decode attention for one query token per sequence.
+ * Replaces, for q_len == 1, the chain SelfAttention::forward_with_cache_encode runs
+ * (src/nn/attention.rs:303-313): LayerKvCache::append_encode (kv_cache.rs:112-142,
+ * kv_cache_write.metal) followed by attention_core_encode (attention.rs:216-247:
+ * gqa_qk / batched_matmul, attention_scale_mask, softmax, gqa_pv / batched_matmul).
+ *   q      [num_seqs, q_heads, head_dim]        (kv dtype)
+ *   k_new  [num_seqs, num_kv_heads, head_dim]   appended at position seq_lens[s];
+ *   v_new  [num_seqs, num_kv_heads, head_dim]   both NULL = attend the cache only
+ *   out    [num_seqs, q_heads, head_dim]        (opts->out_dtype)
+ *   lse    [num_seqs, q_heads] F32, natural-log log-sum-exp of the scaled logits (NULL ok)
+ * Each sequence attends keys [0, seq_lens[s] + (k_new != NULL)).  The block for the new
+ * position must already be in the block table.  seq_lens is NOT advanced.
+ * q_heads must be a multiple of num_kv_heads (gqa_matmul.rs:163-170). */
+int tmllm_gqa_decode(const tmllm_paged_kv* kv, const void* q, const void* k_new,
+                     const void* v_new, void* out, float* lse, int32_t q_heads,
+                     const tmllm_decode_opts* opts, void* workspace, size_t workspace_bytes,
+                     tmllm_stream stream);
+
+/* Log-sum-exp merge of partial attention results (the combine step of a sequence split
+ * across GPUs).  Part p's normalised output rows are at parts_o + p*o_stride ([rows,
+ * head_dim] F32) and its log-sum-exp values at parts_lse + p*lse_stride ([rows] F32);
+ * strides are in floats, 0 = packed (rows*head_dim and rows).  Writes out [rows,
+ * head_dim] (out_dtype) and out_lse [rows] (NULL ok). */
+int tmllm_merge_lse(const float* parts_o, const float* parts_lse, int32_t num_parts,
+                    int32_t rows, int32_t head_dim, int64_t o_stride, int64_t lse_stride,
+                    void* out, int32_t out_dtype, float* out_lse, tmllm_stream stream);
+
+/* ---------------------------------------------------------------------------------- */
+/* Paged KV cache runtime                                                              */
+/* ---------------------------------------------------------------------------------- */
+
+typedef struct tmllm_cache tmllm_cache;
+
+typedef struct tmllm_cache_config {
+    int32_t device;         /* CUDA device ordinal */
+    int32_t num_layers;     /* one K and one V arena per layer, one block table for all */
+    int32_t num_seqs;
+    int32_t max_seq_len;    /* per-sequence capacity (LayerKvCache max, kv_cache.rs:57) */
+    int32_t block_size;     /* tokens per block; == max_seq_len gives the reference layout */
+    int32_t num_kv_heads;
+    int32_t head_dim;
+    int32_t dtype;          /* tmllm_dtype */
+    int64_t num_blocks;     /* pool size; 0 = num_seqs * ceil(max_seq_len / block_size) */
+    uint64_t shuffle_seed;  /* 0 = blocks handed out in pool order; else a seeded shuffle */
+} tmllm_cache_config;
+
+/* Replaces LayerKvCache::new (src/model/kv_cache.rs:54-75) and KvCache::new (:150-164).
+ * Errors: INVALID_SHAPE for zero dimensions (:61-65). */
+int tmllm_cache_create(const tmllm_cache_config* config, tmllm_cache** out);
+int tmllm_cache_destroy(tmllm_cache* cache);
+/* LayerKvCache::len (kv_cache.rs:76-78), per sequence. */
+int tmllm_cache_len(const tmllm_cache* cache, int32_t seq, int64_t* out);
+/* LayerKvCache::capacity (kv_cache.rs:83-85). */
+int tmllm_cache_capacity(const tmllm_cache* cache, int64_t* out);
+/* LayerKvCache::storage_bytes / KvCache::storage_bytes (kv_cache.rs:87-89,176-178):
+ * bytes of all K and V arenas. */
+int tmllm_cache_storage_bytes(const tmllm_cache* cache, int64_t* out);
+/* LayerKvCache::reset / KvCache::reset (kv_cache.rs:92-94,179-183): length 0, blocks
+ * back to the pool; device memory is not cleared.  seq < 0 resets every sequence. */
+int tmllm_cache_reset(tmllm_cache* cache, int32_t seq, tmllm_stream stream);
+/* New: give sequence `seq` blocks for positions [len, len+n).  Validates first
+ * (POSITION_OUT_OF_RANGE past capacity, OUT_OF_BLOCKS when the pool is empty) and
+ * changes nothing on failure.  Table updates of up to 32 entries are enqueued on
+ * `stream`; larger ones (prefill-sized) are copied synchronously. */
+int tmllm_cache_reserve(tmllm_cache* cache, int32_t seq, int64_t n, tmllm_stream stream);
+/* Replaces LayerKvCache::append_encode's write half (kv_cache.rs:112-138): k, v
+ * [num_kv_heads, n, head_dim] (dtype) written at positions [len, len+n) of `seq` in
+ * `layer`, reserving blocks as needed.  The length is NOT advanced (every layer of a
+ * step writes the same positions); see tmllm_cache_advance. */
+int tmllm_cache_append(tmllm_cache* cache, int32_t layer, int32_t seq, const void* k,
+                       const void* v, int64_t n, int32_t dtype, tmllm_stream stream);
+/* The `self.len = new_len` of append_encode (kv_cache.rs:140): len += n for `seq`
+ * (every sequence when seq < 0), on the host and on the device copy of the lengths. */
+int tmllm_cache_advance(tmllm_cache* cache, int32_t seq, int64_t n, tmllm_stream stream);
+/* Device pointers of one layer's store, for tmllm_gqa_decode. */
+int tmllm_cache_view(const tmllm_cache* cache, int32_t layer, tmllm_paged_kv* out);
+/* Host copy of a sequence's block table (the first ceil(len/block_size) entries and any
+ * reserved beyond); *n receives the number of valid entries. */
+int tmllm_cache_block_table(const tmllm_cache* cache, int32_t seq, int32_t* out,
+                            int64_t capacity, int64_t* n);
+/* Replaces LayerKvCache::key()/value() (kv_cache.rs:98-103) followed by contiguous():
+ * dense copies [num_kv_heads, len, head_dim] of positions [0, len) (either may be NULL). */
+int tmllm_cache_gather(const tmllm_cache* cache, int32_t layer, int32_t seq, void* k_out,
+                       void* v_out, tmllm_stream stream);
+/* Fused append + decode attention over every sequence of the cache for `layer` (see
+ * tmllm_gqa_decode), with a workspace the cache owns.  Blocks for the new positions are
+ * reserved first.  The first call for a given (q_heads, splits) shape allocates that
+ * workspace; make it before any stream capture.  Lengths are not advanced. */
+int tmllm_cache_decode(tmllm_cache* cache, int32_t layer, const void* q, const void* k_new,
+                       const void* v_new, void* out, float* lse, int32_t q_heads,
+                       const tmllm_decode_opts* opts, tmllm_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TMLLM_H */

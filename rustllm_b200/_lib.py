@@ -1,0 +1,191 @@
+"""ctypes binding of ``libtmllm_b200.so`` (the C ABI declared in ``include/tmllm.h``).
+
+There is no fallback: if the library is missing or a call fails, an exception is raised.
+Status codes map onto the reference's ``TinyError`` variants (src/error.rs:3-43).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libtmllm_b200.so")
+
+F32 = 0
+F16 = 1
+
+vp = C.c_void_p
+i32 = C.c_int32
+i64 = C.c_int64
+sz = C.c_size_t
+
+
+class TinyError(Exception):
+    """Mirror of the reference's ``TinyError`` (src/error.rs:3-43)."""
+
+    status = -1
+
+    def __init__(self, message: str, status: int | None = None):
+        super().__init__(message)
+        if status is not None:
+            self.status = status
+
+
+class InvalidArgument(TinyError):
+    status = 1
+
+
+class InvalidShape(TinyError):
+    status = 2
+
+
+class ShapeMismatch(TinyError):
+    status = 3
+
+
+class InvalidDimension(TinyError):
+    status = 4
+
+
+class UnsupportedDType(TinyError):
+    status = 5
+
+
+class NonContiguousTensor(TinyError):
+    status = 6
+
+
+class PositionOutOfRange(TinyError):
+    status = 7
+
+
+class ModelFormat(TinyError):
+    status = 8
+
+
+class DeviceError(TinyError):
+    """CUDA runtime failure (the reference's ``TinyError::Metal``)."""
+
+    status = 9
+
+
+class OutOfBlocks(TinyError):
+    status = 10
+
+
+class DeviceTimeout(TinyError):
+    status = 11
+
+
+class NotReserved(TinyError):
+    status = 12
+
+
+_BY_STATUS = {cls.status: cls for cls in (
+    InvalidArgument, InvalidShape, ShapeMismatch, InvalidDimension, UnsupportedDType,
+    NonContiguousTensor, PositionOutOfRange, ModelFormat, DeviceError, OutOfBlocks,
+    DeviceTimeout, NotReserved)}
+
+
+class PagedKV(C.Structure):
+    """``tmllm_paged_kv``: device pointers of one layer's block-paged store."""
+
+    _fields_ = [("k_cache", vp), ("v_cache", vp), ("block_table", vp), ("seq_lens", vp),
+                ("num_blocks", i64), ("num_seqs", i32), ("num_kv_heads", i32),
+                ("head_dim", i32), ("block_size", i32), ("max_blocks_per_seq", i32),
+                ("dtype", i32)]
+
+
+class DecodeOpts(C.Structure):
+    """``tmllm_decode_opts``."""
+
+    _fields_ = [("scale", C.c_float), ("num_splits", i32), ("out_dtype", i32),
+                ("rope_cos", vp), ("rope_sin", vp), ("rope_len", i32),
+                ("rope_pos_offset", i32), ("max_len_hint", i64)]
+
+
+class CacheConfig(C.Structure):
+    """``tmllm_cache_config``."""
+
+    _fields_ = [("device", i32), ("num_layers", i32), ("num_seqs", i32),
+                ("max_seq_len", i32), ("block_size", i32), ("num_kv_heads", i32),
+                ("head_dim", i32), ("dtype", i32), ("num_blocks", i64),
+                ("shuffle_seed", C.c_uint64)]
+
+
+_PROTOS = {
+    "tmllm_version": (C.c_int, []),
+    "tmllm_status_name": (C.c_char_p, [C.c_int]),
+    "tmllm_last_error": (C.c_char_p, []),
+    "tmllm_sync": (C.c_int, [vp]),
+    "tmllm_kv_cache_write": (C.c_int, [C.c_int, vp, vp, sz, sz, sz, sz, sz, vp]),
+    "tmllm_concat_sequence": (C.c_int, [C.c_int, vp, vp, vp, sz, sz, sz, sz, sz, vp]),
+    "tmllm_repeat_kv": (C.c_int, [C.c_int, vp, vp, sz, sz, sz, sz, sz, vp]),
+    "tmllm_gqa_qk": (C.c_int, [C.c_int, vp, vp, vp, sz, sz, sz, sz, sz, sz, sz, vp]),
+    "tmllm_gqa_pv": (C.c_int, [C.c_int, vp, vp, vp, sz, sz, sz, sz, sz, sz, sz, vp]),
+    "tmllm_attention_scale_mask": (C.c_int, [C.c_int, vp, vp, sz, sz, sz, sz, C.c_float, vp]),
+    "tmllm_softmax_last_dim": (C.c_int, [C.c_int, vp, vp, sz, sz, vp]),
+    "tmllm_batched_matmul": (C.c_int, [C.c_int, vp, vp, vp, sz, sz, sz, sz, vp]),
+    "tmllm_rope_tables": (C.c_int, [vp, vp, sz, sz, C.c_float]),
+    "tmllm_rope": (C.c_int, [C.c_int, vp, vp, vp, vp, sz, sz, sz, sz, sz, vp]),
+    "tmllm_decode_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
+    "tmllm_decode_workspace_init": (C.c_int, [vp, sz, vp]),
+    "tmllm_decode_auto_splits": (i32, [i32, i32, i64]),
+    "tmllm_gqa_decode": (C.c_int, [C.POINTER(PagedKV), vp, vp, vp, vp, vp, i32,
+                                   C.POINTER(DecodeOpts), vp, sz, vp]),
+    "tmllm_merge_lse": (C.c_int, [vp, vp, i32, i32, i32, i64, i64, vp, i32, vp, vp]),
+    "tmllm_cache_create": (C.c_int, [C.POINTER(CacheConfig), C.POINTER(vp)]),
+    "tmllm_cache_destroy": (C.c_int, [vp]),
+    "tmllm_cache_len": (C.c_int, [vp, i32, C.POINTER(i64)]),
+    "tmllm_cache_capacity": (C.c_int, [vp, C.POINTER(i64)]),
+    "tmllm_cache_storage_bytes": (C.c_int, [vp, C.POINTER(i64)]),
+    "tmllm_cache_reset": (C.c_int, [vp, i32, vp]),
+    "tmllm_cache_reserve": (C.c_int, [vp, i32, i64, vp]),
+    "tmllm_cache_append": (C.c_int, [vp, i32, i32, vp, vp, i64, i32, vp]),
+    "tmllm_cache_advance": (C.c_int, [vp, i32, i64, vp]),
+    "tmllm_cache_view": (C.c_int, [vp, i32, C.POINTER(PagedKV)]),
+    "tmllm_cache_block_table": (C.c_int, [vp, i32, vp, i64, C.POINTER(i64)]),
+    "tmllm_cache_gather": (C.c_int, [vp, i32, i32, vp, vp, vp]),
+    "tmllm_cache_decode": (C.c_int, [vp, i32, vp, vp, vp, vp, vp, i32, C.POINTER(DecodeOpts),
+                                     vp]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load():
+    """Loads the C-ABI library (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python -m rustllm_b200.build` "
+                "(there is no CPU fallback)")
+        lib = C.CDLL(LIB_PATH)
+        for name, (res, args) in _PROTOS.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def check(rc: int) -> None:
+    """Raises the TinyError subclass for a non-zero status."""
+    if rc == 0:
+        return
+    lib = load()
+    msg = lib.tmllm_last_error().decode(errors="replace")
+    name = lib.tmllm_status_name(rc).decode()
+    cls = _BY_STATUS.get(rc, TinyError)
+    raise cls(f"{name}: {msg}", rc)
+
+
+def call(name: str, *args) -> None:
+    check(getattr(load(), name)(*args))

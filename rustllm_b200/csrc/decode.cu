@@ -1,0 +1,890 @@
+// Fused KV-append + GQA decode attention over a block-paged cache (sm_100a).
+//
+// One query token per sequence.  The reference runs this as six dispatches with the score
+// tensor [Hq, L] travelling through memory four times and every KV head read once per
+// query head (src/nn/attention.rs:216-247, kernels/gqa_matmul.metal, softmax.metal,
+// attention_scale_mask.metal, kv_cache_write.metal).  Here it is one kernel:
+//
+//   grid (splits, kv_heads, seqs), 128 threads.  A CTA owns one KV head of one sequence
+//   and a contiguous chunk of its positions, and serves all G = Hq/Hkv query heads of that
+//   KV head, so every K/V byte is read from HBM exactly once.
+//   K/V tiles of TT positions stream through a STAGES-deep cp.async ring in shared
+//   memory (16-byte copies, rows XOR-swizzled so the per-token reads below hit 8 distinct
+//   bank groups).  QK^T: one thread per (token, slice of D), q held in shared memory as
+//   F32 [D][GP] and read by broadcast.  Online softmax in the log2 domain with
+//   warp-shuffle max/sum.  PV: each warp owns TT/4 tokens, each lane D/32 dims, F32
+//   accumulators in registers; all warps share the CTA's running max, so their partial
+//   outputs simply add at the end.
+//   The CTA whose chunk holds the new position rotates (optional RoPE) and writes k_new /
+//   v_new into their paged slot and uses them from shared memory (no read-after-write
+//   through memory).  With several splits, each CTA writes (O, m, l) partials and the
+//   last CTA of a (seq, kv head) -- found with an atomic ticket -- merges them.
+#include <cmath>
+
+#include "common.cuh"
+
+namespace tmllm {
+namespace {
+
+constexpr int kDecodeThreads = 128;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct DecodeArgs {
+    const void* q;
+    const void* k_new;
+    const void* v_new;
+    void* k_cache;
+    void* v_cache;
+    const int32_t* block_table;
+    const int32_t* seq_lens;
+    void* out;
+    float* lse;
+    int32_t* counters;  // [B * Hkv]
+    float* part_ml;     // [B, Hkv, max_splits, G, 2]
+    float* part_o;      // [B, Hkv, max_splits, G, D]
+    const float* rope_cos;
+    const float* rope_sin;
+    int64_t num_blocks;
+    int32_t q_heads, kv_heads, group, block_size, bs_shift, max_blocks, chunk;
+    int32_t rope_len, rope_off, out_f32;
+    float scale_log2;
+};
+
+// Physical slot of 16-byte chunk `c` of tile row `r` (XOR swizzle inside groups of 8).
+template <int C>
+__device__ __forceinline__ int swz(int r, int c) {
+    constexpr int M = (C >= 8 ? 8 : C) - 1;
+    return c ^ (r & M);
+}
+
+__device__ __forceinline__ int64_t block_of(const DecodeArgs& a, int b, int pos) {
+    int idx = a.bs_shift >= 0 ? (pos >> a.bs_shift) : (pos / a.block_size);
+    if (idx >= a.max_blocks) return -1;
+    int64_t blk = __ldg(&a.block_table[static_cast<int64_t>(b) * a.max_blocks + idx]);
+    return (blk >= 0 && blk < a.num_blocks) ? blk : -1;
+}
+
+__device__ __forceinline__ int offset_in_block(const DecodeArgs& a, int pos) {
+    return a.bs_shift >= 0 ? (pos & (a.block_size - 1)) : (pos % a.block_size);
+}
+
+// Rotates the pair (x1, x2) = (x[i], x[i + D/2]) at `pos`; identity when no table is given
+// or `pos` is outside it.  Same arithmetic as kernels/rope.metal:57-63 without contraction.
+__device__ __forceinline__ void rope_pair(const DecodeArgs& a, int pos, int i, int half,
+                                          float& x1, float& x2) {
+    if (a.rope_cos == nullptr || pos < 0 || pos >= a.rope_len) return;
+    float c = __ldg(&a.rope_cos[static_cast<int64_t>(pos) * half + i]);
+    float s = __ldg(&a.rope_sin[static_cast<int64_t>(pos) * half + i]);
+    float y1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+    float y2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+    x1 = y1;
+    x2 = y2;
+}
+
+template <typename T, int D, int GP, int TT, int STAGES>
+struct DecodeCfg {
+    static constexpr int EPC = 16 / sizeof(T);  // elements per 16-byte chunk
+    static constexpr int C = D / EPC;           // chunks per row
+    static constexpr int NH = kDecodeThreads / TT;  // D slices in QK
+    static constexpr int CPT = C / NH;          // chunks per thread in QK
+    static constexpr int DPL = D / 32;          // dims per lane in PV
+    static constexpr int TPW = TT / 4;          // tokens per warp in PV
+    static constexpr int ROW = D * static_cast<int>(sizeof(T));
+    static constexpr int TILE = TT * ROW;
+    static constexpr int LOADS = TT * C / kDecodeThreads;
+    static constexpr int RSTEP = kDecodeThreads / C;  // rows between a thread's loads
+    static_assert(C % NH == 0, "D slices must split the row into whole chunks");
+    static_assert((TT * C) % kDecodeThreads == 0 && kDecodeThreads % C == 0, "load mapping");
+    static_assert(D % 32 == 0 && TT % 32 == 0 && TT <= 128, "shape");
+    static_assert((DPL * sizeof(T)) == 4 || (DPL * sizeof(T)) == 8 || (DPL * sizeof(T)) == 16,
+                  "PV lane width");
+    // shared-memory carve-up (bytes)
+    static constexpr int OFF_Q = STAGES * 2 * TILE;
+    static constexpr int OFF_SPART = OFF_Q + D * GP * 4;
+    static constexpr int OFF_P = OFF_SPART + NH * TT * GP * 4;
+    static constexpr int OFF_ST = OFF_P + TT * GP * 4;  // alpha, m, l [GP] each + flag
+    static constexpr int OFF_NEW = OFF_ST + 4 * GP * 4 + 16;
+    static constexpr int BYTES = OFF_NEW + 2 * ROW;
+    static_assert(STAGES * 2 * TILE >= 4 * GP * D * 4, "reduction scratch fits in the ring");
+};
+
+template <int N> struct VecBytes;
+template <> struct VecBytes<4> { using type = uint32_t; };
+template <> struct VecBytes<8> { using type = uint2; };
+template <> struct VecBytes<16> { using type = uint4; };
+
+template <typename T, int N>
+__device__ __forceinline__ void unpack_n(const void* p, float* f) {
+    using V = typename VecBytes<N * sizeof(T)>::type;
+    V raw = *reinterpret_cast<const V*>(p);
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < N; ++i) f[i] = to_f32<T>(e[i]);
+}
+
+template <typename T, int D, int GP, int TT, int STAGES>
+__global__ void __launch_bounds__(kDecodeThreads, 2) decode_split_kernel(const DecodeArgs a) {
+    using Cfg = DecodeCfg<T, D, GP, TT, STAGES>;
+    constexpr int C = Cfg::C, EPC = Cfg::EPC, NH = Cfg::NH, CPT = Cfg::CPT, DPL = Cfg::DPL;
+    constexpr int TPW = Cfg::TPW, ROW = Cfg::ROW, TILE = Cfg::TILE;
+    extern __shared__ __align__(128) unsigned char smem[];
+    float* q_s = reinterpret_cast<float*>(smem + Cfg::OFF_Q);        // [D][GP]
+    float* s_part = reinterpret_cast<float*>(smem + Cfg::OFF_SPART);  // [NH][TT][GP]
+    float* p_s = reinterpret_cast<float*>(smem + Cfg::OFF_P);         // [TT][GP]
+    float* alpha_s = reinterpret_cast<float*>(smem + Cfg::OFF_ST);    // [GP]
+    float* m_s = alpha_s + GP;
+    float* l_s = m_s + GP;
+    int* flag_s = reinterpret_cast<int*>(l_s + GP);
+    T* knew_s = reinterpret_cast<T*>(smem + Cfg::OFF_NEW);            // [D]
+    T* vnew_s = knew_s + D;                                           // [D]
+
+    const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = a.group;
+    const int cached = a.seq_lens[b] < 0 ? 0 : a.seq_lens[b];
+    const bool has_new = a.k_new != nullptr;
+    const int L = cached + (has_new ? 1 : 0);
+    int splits_b = (L + a.chunk - 1) / a.chunk;
+    if (splits_b < 1) splits_b = 1;
+    if (splits_b > static_cast<int>(gridDim.x)) splits_b = gridDim.x;
+    if (split >= splits_b) return;
+    const int t0 = split * a.chunk;
+    const int t1 = (split == splits_b - 1) ? L : min(L, t0 + a.chunk);
+    const int ntiles = t1 > t0 ? (t1 - t0 + TT - 1) / TT : 0;
+    const bool owns_new = has_new && cached >= t0 && cached < t1;
+    const int half = D / 2;
+    const int qpos = cached + a.rope_off;
+
+    // ---- q (rotated, storage-rounded) into q_s; padded heads are zero
+    for (int idx = tid; idx < GP * half; idx += kDecodeThreads) {
+        int g = idx / half, i = idx - g * half;
+        float x1 = 0.f, x2 = 0.f;
+        if (g < G) {
+            const T* qr = static_cast<const T*>(a.q) +
+                          (static_cast<int64_t>(b) * a.q_heads + kvh * G + g) * D;
+            x1 = to_f32<T>(qr[i]);
+            x2 = to_f32<T>(qr[i + half]);
+            rope_pair(a, qpos, i, half, x1, x2);
+            x1 = round_store<T>(x1);
+            x2 = round_store<T>(x2);
+        }
+        q_s[i * GP + g] = x1;
+        q_s[(i + half) * GP + g] = x2;
+    }
+    for (int idx = tid; idx < TT * GP; idx += kDecodeThreads) p_s[idx] = 0.f;
+    if (tid < GP) {
+        alpha_s[tid] = 1.f;
+        m_s[tid] = -INFINITY;
+        l_s[tid] = 0.f;
+    }
+    // ---- the new token: rotate k, keep both rows in shared memory, write them to the cache
+    if (owns_new) {
+        const int64_t nrow = (static_cast<int64_t>(b) * a.kv_heads + kvh) * D;
+        const T* kn = static_cast<const T*>(a.k_new) + nrow;
+        const T* vn = static_cast<const T*>(a.v_new) + nrow;
+        for (int i = tid; i < half; i += kDecodeThreads) {
+            float x1 = to_f32<T>(kn[i]), x2 = to_f32<T>(kn[i + half]);
+            rope_pair(a, qpos, i, half, x1, x2);
+            knew_s[i] = from_f32<T>(x1);
+            knew_s[i + half] = from_f32<T>(x2);
+            vnew_s[i] = vn[i];
+            vnew_s[i + half] = vn[i + half];
+        }
+    }
+    __syncthreads();
+    if (owns_new) {
+        const int64_t blk = block_of(a, b, cached);
+        if (blk >= 0) {
+            const int64_t off =
+                ((blk * a.kv_heads + kvh) * a.block_size + offset_in_block(a, cached)) * D;
+            T* kd = static_cast<T*>(a.k_cache) + off;
+            T* vd = static_cast<T*>(a.v_cache) + off;
+            for (int i = tid; i < D; i += kDecodeThreads) {
+                kd[i] = knew_s[i];
+                vd[i] = vnew_s[i];
+            }
+        }
+    }
+
+    // ---- cp.async producer: thread `tid` copies chunk (tid % C) of rows tid/C + k*RSTEP
+    const int lc = tid % C;
+    const int lr0 = tid / C;
+    const unsigned char* kbase = static_cast<const unsigned char*>(a.k_cache);
+    const unsigned char* vbase = static_cast<const unsigned char*>(a.v_cache);
+    auto load_tile = [&](int tile, int stage) {
+        unsigned char* ks = smem + stage * 2 * TILE;
+        unsigned char* vs = ks + TILE;
+        const int base = t0 + tile * TT;
+#pragma unroll
+        for (int k = 0; k < Cfg::LOADS; ++k) {
+            const int r = lr0 + k * Cfg::RSTEP;
+            const int pos = base + r;
+            const unsigned char* ksrc = kbase;
+            const unsigned char* vsrc = vbase;
+            int bytes = 0;
+            if (pos < cached && pos < t1) {
+                const int64_t blk = block_of(a, b, pos);
+                if (blk >= 0) {
+                    const int64_t off =
+                        ((blk * a.kv_heads + kvh) * a.block_size + offset_in_block(a, pos)) *
+                            ROW +
+                        lc * 16;
+                    ksrc += off;
+                    vsrc += off;
+                    bytes = 16;
+                }
+            }
+            const int dst = r * ROW + swz<C>(r, lc) * 16;
+            cp_async16(ks + dst, ksrc, bytes);
+            cp_async16(vs + dst, vsrc, bytes);
+        }
+    };
+
+#pragma unroll
+    for (int s = 0; s < STAGES - 1; ++s) {
+        if (s < ntiles) load_tile(s, s);
+        cp_async_commit();
+    }
+
+    // consumer roles
+    const int tq = (warp % (TT / 32)) * 32 + lane;  // QK: token of this thread
+    const int hq = warp / (TT / 32);                 // QK: D slice of this thread
+    float acc_o[GP][DPL];
+#pragma unroll
+    for (int g = 0; g < GP; ++g)
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) acc_o[g][e] = 0.f;
+
+    for (int it = 0; it < ntiles; ++it) {
+        cp_async_wait<STAGES - 2>();
+        __syncthreads();
+        {
+            const int nt = it + STAGES - 1;
+            if (nt < ntiles) load_tile(nt, nt % STAGES);
+            cp_async_commit();
+        }
+        unsigned char* ks = smem + (it % STAGES) * 2 * TILE;
+        unsigned char* vs = ks + TILE;
+        const int base = t0 + it * TT;
+        if (owns_new && cached >= base && cached < base + TT) {
+            const int r = cached - base;
+            if (tid < C) {
+                *reinterpret_cast<uint4*>(ks + r * ROW + swz<C>(r, tid) * 16) =
+                    *reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned char*>(knew_s) + tid * 16);
+            } else if (tid < 2 * C) {
+                const int c = tid - C;
+                *reinterpret_cast<uint4*>(vs + r * ROW + swz<C>(r, c) * 16) =
+                    *reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned char*>(vnew_s) + c * 16);
+            }
+            __syncthreads();
+        }
+
+        // ---- QK^T partial over this thread's D slice
+        {
+            float acc[GP];
+#pragma unroll
+            for (int g = 0; g < GP; ++g) acc[g] = 0.f;
+            const unsigned char* krow = ks + tq * ROW;
+#pragma unroll
+            for (int j = 0; j < CPT; ++j) {
+                const int c = hq * CPT + j;
+                uint4 raw = *reinterpret_cast<const uint4*>(krow + swz<C>(tq, c) * 16);
+                float kf[EPC];
+                Chunk<T>::unpack(raw, kf);
+#pragma unroll
+                for (int e = 0; e < EPC; ++e) {
+                    const float* qd = q_s + (c * EPC + e) * GP;
+#pragma unroll
+                    for (int g4 = 0; g4 < GP; g4 += 4) {
+                        float4 qv = *reinterpret_cast<const float4*>(qd + g4);
+                        acc[g4 + 0] = fmaf(qv.x, kf[e], acc[g4 + 0]);
+                        acc[g4 + 1] = fmaf(qv.y, kf[e], acc[g4 + 1]);
+                        acc[g4 + 2] = fmaf(qv.z, kf[e], acc[g4 + 2]);
+                        acc[g4 + 3] = fmaf(qv.w, kf[e], acc[g4 + 3]);
+                    }
+                }
+            }
+            float* sp = s_part + (hq * TT + tq) * GP;
+#pragma unroll
+            for (int g4 = 0; g4 < GP; g4 += 4)
+                *reinterpret_cast<float4*>(sp + g4) =
+                    make_float4(acc[g4], acc[g4 + 1], acc[g4 + 2], acc[g4 + 3]);
+        }
+        __syncthreads();
+
+        // ---- online softmax, one warp per query head
+        for (int g = warp; g < G; g += 4) {
+            float sv[TT / 32];
+            float mx = -INFINITY;
+#pragma unroll
+            for (int k = 0; k < TT / 32; ++k) {
+                const int t = lane + 32 * k;
+                float v = 0.f;
+#pragma unroll
+                for (int h = 0; h < NH; ++h) v += s_part[(h * TT + t) * GP + g];
+                v = (base + t < t1) ? v * a.scale_log2 : -INFINITY;
+                sv[k] = v;
+                mx = fmaxf(mx, v);
+            }
+            mx = warp_max(mx);
+            const float m_old = m_s[g];
+            const float m_new = fmaxf(m_old, mx);
+            float alpha, sum = 0.f;
+            if (m_new == -INFINITY) {
+                alpha = 1.f;
+#pragma unroll
+                for (int k = 0; k < TT / 32; ++k) p_s[(lane + 32 * k) * GP + g] = 0.f;
+            } else {
+                alpha = exp2f(m_old - m_new);
+#pragma unroll
+                for (int k = 0; k < TT / 32; ++k) {
+                    float p = exp2f(sv[k] - m_new);
+                    p_s[(lane + 32 * k) * GP + g] = p;
+                    sum += p;
+                }
+            }
+            sum = warp_sum(sum);
+            if (lane == 0) {
+                alpha_s[g] = alpha;
+                m_s[g] = m_new;
+                l_s[g] = l_s[g] * alpha + sum;
+            }
+        }
+        __syncthreads();
+
+        // ---- PV: warp owns tokens [warp*TPW, +TPW), lane owns dims [lane*DPL, +DPL)
+        {
+#pragma unroll
+            for (int g = 0; g < GP; ++g) {
+                const float al = alpha_s[g];
+#pragma unroll
+                for (int e = 0; e < DPL; ++e) acc_o[g][e] *= al;
+            }
+            constexpr int LB = DPL * static_cast<int>(sizeof(T));  // bytes per lane
+            const int lbyte = lane * LB;
+            const int lch = lbyte / 16, lin = lbyte % 16;
+#pragma unroll 4
+            for (int i = 0; i < TPW; ++i) {
+                const int t = warp * TPW + i;
+                float vf[DPL];
+                unpack_n<T, DPL>(vs + t * ROW + swz<C>(t, lch) * 16 + lin, vf);
+                const float* pr = p_s + t * GP;
+#pragma unroll
+                for (int g4 = 0; g4 < GP; g4 += 4) {
+                    float4 pv = *reinterpret_cast<const float4*>(pr + g4);
+#pragma unroll
+                    for (int e = 0; e < DPL; ++e) {
+                        acc_o[g4 + 0][e] = fmaf(pv.x, vf[e], acc_o[g4 + 0][e]);
+                        acc_o[g4 + 1][e] = fmaf(pv.y, vf[e], acc_o[g4 + 1][e]);
+                        acc_o[g4 + 2][e] = fmaf(pv.z, vf[e], acc_o[g4 + 2][e]);
+                        acc_o[g4 + 3][e] = fmaf(pv.w, vf[e], acc_o[g4 + 3][e]);
+                    }
+                }
+            }
+        }
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+
+    // ---- sum the four warps' partial outputs (the ring is free now)
+    float* red = reinterpret_cast<float*>(smem);  // [4][GP][D]
+#pragma unroll
+    for (int g = 0; g < GP; ++g)
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) red[(warp * GP + g) * D + lane * DPL + e] = acc_o[g][e];
+    __syncthreads();
+
+    const int64_t qh0 = static_cast<int64_t>(b) * a.q_heads + static_cast<int64_t>(kvh) * G;
+    if (splits_b == 1) {
+        for (int idx = tid; idx < G * D; idx += kDecodeThreads) {
+            const int g = idx / D, d = idx - g * D;
+            float o = red[g * D + d] + red[(GP + g) * D + d] + red[(2 * GP + g) * D + d] +
+                      red[(3 * GP + g) * D + d];
+            const float l = l_s[g];
+            o = l > 0.f ? o / l : 0.f;
+            if (a.out_f32)
+                static_cast<float*>(a.out)[(qh0 + g) * D + d] = o;
+            else
+                static_cast<T*>(a.out)[(qh0 + g) * D + d] = from_f32<T>(o);
+            if (d == 0 && a.lse)
+                a.lse[qh0 + g] = l > 0.f ? (m_s[g] + log2f(l)) * kLn2 : -INFINITY;
+        }
+        return;
+    }
+
+    // ---- several splits: publish (O, m, l), last CTA of this (seq, kv head) merges
+    const int64_t pbase =
+        ((static_cast<int64_t>(b) * a.kv_heads + kvh) * gridDim.x) * G;  // part row of split 0
+    for (int idx = tid; idx < G * D; idx += kDecodeThreads) {
+        const int g = idx / D, d = idx - g * D;
+        float o = red[g * D + d] + red[(GP + g) * D + d] + red[(2 * GP + g) * D + d] +
+                  red[(3 * GP + g) * D + d];
+        a.part_o[(pbase + static_cast<int64_t>(split) * G + g) * D + d] = o;
+    }
+    if (tid < G) {
+        a.part_ml[(pbase + static_cast<int64_t>(split) * G + tid) * 2 + 0] = m_s[tid];
+        a.part_ml[(pbase + static_cast<int64_t>(split) * G + tid) * 2 + 1] = l_s[tid];
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const int ticket = atomicAdd(&a.counters[static_cast<int64_t>(b) * a.kv_heads + kvh], 1);
+        *flag_s = (ticket == splits_b - 1);
+    }
+    __syncthreads();
+    if (!*flag_s) return;
+    __threadfence();
+
+    // merge weights w[s][g] = 2^(m_s - M_g), kept in the free ring
+    float* wts = reinterpret_cast<float*>(smem);  // [splits_b][GP]
+    float* Ms = wts + static_cast<int64_t>(gridDim.x) * GP;
+    float* den = Ms + GP;
+    if (tid < G) {
+        float M = -INFINITY;
+        for (int s = 0; s < splits_b; ++s)
+            M = fmaxf(M, __ldcg(&a.part_ml[(pbase + static_cast<int64_t>(s) * G + tid) * 2]));
+        float dsum = 0.f;
+        for (int s = 0; s < splits_b; ++s) {
+            const float* ml = a.part_ml + (pbase + static_cast<int64_t>(s) * G + tid) * 2;
+            const float w = (M == -INFINITY) ? 0.f : exp2f(__ldcg(ml) - M);
+            wts[s * GP + tid] = w;
+            dsum += w * __ldcg(ml + 1);
+        }
+        Ms[tid] = M;
+        den[tid] = dsum;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < G * D; idx += kDecodeThreads) {
+        const int g = idx / D, d = idx - g * D;
+        float num = 0.f;
+        for (int s = 0; s < splits_b; ++s)
+            num += wts[s * GP + g] *
+                   __ldcg(&a.part_o[(pbase + static_cast<int64_t>(s) * G + g) * D + d]);
+        const float dn = den[g];
+        const float o = dn > 0.f ? num / dn : 0.f;
+        if (a.out_f32)
+            static_cast<float*>(a.out)[(qh0 + g) * D + d] = o;
+        else
+            static_cast<T*>(a.out)[(qh0 + g) * D + d] = from_f32<T>(o);
+        if (d == 0 && a.lse) a.lse[qh0 + g] = dn > 0.f ? (Ms[g] + log2f(dn)) * kLn2 : -INFINITY;
+    }
+    if (tid == 0) a.counters[static_cast<int64_t>(b) * a.kv_heads + kvh] = 0;
+}
+
+// Any even head_dim: one CTA per (seq, query head), tiles of 128 positions, one thread per
+// position for QK^T and one thread per dimension for PV.  Used for head sizes the tiled
+// kernel does not instantiate (the reference's unit tests use D = 2 and 4).
+template <typename T>
+__global__ void __launch_bounds__(128) decode_generic_kernel(const DecodeArgs a, int D) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    float* q_s = reinterpret_cast<float*>(smem);  // [D]
+    float* kn_s = q_s + D;                        // [D] rotated k_new
+    float* vn_s = kn_s + D;                       // [D]
+    float* p_s = vn_s + D;                        // [128]
+    float* red = p_s + 128;                       // [4]
+    const int qh = blockIdx.x, b = blockIdx.y;
+    const int kvh = qh / a.group, g = qh % a.group;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int cached = a.seq_lens[b] < 0 ? 0 : a.seq_lens[b];
+    const bool has_new = a.k_new != nullptr;
+    const int L = cached + (has_new ? 1 : 0);
+    const int half = D / 2;
+    const int qpos = cached + a.rope_off;
+    const T* qr = static_cast<const T*>(a.q) + (static_cast<int64_t>(b) * a.q_heads + qh) * D;
+    for (int i = tid; i < half; i += 128) {
+        float x1 = to_f32<T>(qr[i]), x2 = to_f32<T>(qr[i + half]);
+        rope_pair(a, qpos, i, half, x1, x2);
+        q_s[i] = round_store<T>(x1);
+        q_s[i + half] = round_store<T>(x2);
+    }
+    if (has_new) {
+        const int64_t nrow = (static_cast<int64_t>(b) * a.kv_heads + kvh) * D;
+        const T* kn = static_cast<const T*>(a.k_new) + nrow;
+        const T* vn = static_cast<const T*>(a.v_new) + nrow;
+        for (int i = tid; i < half; i += 128) {
+            float x1 = to_f32<T>(kn[i]), x2 = to_f32<T>(kn[i + half]);
+            rope_pair(a, qpos, i, half, x1, x2);
+            kn_s[i] = round_store<T>(x1);
+            kn_s[i + half] = round_store<T>(x2);
+            vn_s[i] = to_f32<T>(vn[i]);
+            vn_s[i + half] = to_f32<T>(vn[i + half]);
+        }
+    }
+    __syncthreads();
+    if (has_new && g == 0) {
+        const int64_t blk = block_of(a, b, cached);
+        if (blk >= 0) {
+            const int64_t off =
+                ((blk * a.kv_heads + kvh) * a.block_size + offset_in_block(a, cached)) * D;
+            for (int i = tid; i < D; i += 128) {
+                static_cast<T*>(a.k_cache)[off + i] = from_f32<T>(kn_s[i]);
+                static_cast<T*>(a.v_cache)[off + i] = from_f32<T>(vn_s[i]);
+            }
+        }
+    }
+    float m = -INFINITY, l = 0.f;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};  // dims tid, tid+128, ... (D <= 512)
+    const T* kc = static_cast<const T*>(a.k_cache);
+    const T* vc = static_cast<const T*>(a.v_cache);
+    for (int base = 0; base < L; base += 128) {
+        const int pos = base + tid;
+        float s = -INFINITY;
+        if (pos < L) {
+            float dot = 0.f;
+            if (pos == cached && has_new) {
+                for (int d = 0; d < D; ++d) dot = fmaf(q_s[d], kn_s[d], dot);
+                s = dot * a.scale_log2;
+            } else {
+                const int64_t blk = block_of(a, b, pos);
+                if (blk >= 0) {
+                    const T* kr = kc + ((blk * a.kv_heads + kvh) * a.block_size +
+                                        offset_in_block(a, pos)) * static_cast<int64_t>(D);
+                    for (int d = 0; d < D; ++d) dot = fmaf(q_s[d], to_f32<T>(kr[d]), dot);
+                    s = dot * a.scale_log2;
+                }
+            }
+        }
+        float mx = warp_max(s);
+        if (lane == 0) red[warp] = mx;
+        __syncthreads();
+        mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+        __syncthreads();
+        const float m_new = fmaxf(m, mx);
+        const float p = (m_new == -INFINITY || s == -INFINITY) ? 0.f : exp2f(s - m_new);
+        const float alpha = (m_new == -INFINITY) ? 1.f : exp2f(m - m_new);
+        p_s[tid] = p;
+        float ps = warp_sum(p);
+        if (lane == 0) red[warp] = ps;
+        __syncthreads();
+        ps = red[0] + red[1] + red[2] + red[3];
+        l = l * alpha + ps;
+        m = m_new;
+        const int n = min(128, L - base);
+        for (int k = 0; k < 4; ++k) {
+            const int d = tid + 128 * k;
+            if (d >= D) break;
+            float o = acc[k] * alpha;
+            for (int t = 0; t < n; ++t) {
+                const int ps_pos = base + t;
+                float vv;
+                if (ps_pos == cached && has_new) {
+                    vv = vn_s[d];
+                } else {
+                    const int64_t blk = block_of(a, b, ps_pos);
+                    vv = blk < 0 ? 0.f
+                                 : to_f32<T>(vc[((blk * a.kv_heads + kvh) * a.block_size +
+                                                 offset_in_block(a, ps_pos)) *
+                                                    static_cast<int64_t>(D) + d]);
+                }
+                o = fmaf(p_s[t], vv, o);
+            }
+            acc[k] = o;
+        }
+        __syncthreads();
+    }
+    const int64_t orow = (static_cast<int64_t>(b) * a.q_heads + qh) * D;
+    for (int k = 0; k < 4; ++k) {
+        const int d = tid + 128 * k;
+        if (d >= D) break;
+        const float o = l > 0.f ? acc[k] / l : 0.f;
+        if (a.out_f32)
+            static_cast<float*>(a.out)[orow + d] = o;
+        else
+            static_cast<T*>(a.out)[orow + d] = from_f32<T>(o);
+    }
+    if (tid == 0 && a.lse)
+        a.lse[static_cast<int64_t>(b) * a.q_heads + qh] = l > 0.f ? (m + log2f(l)) * kLn2 : -INFINITY;
+}
+
+// Log-sum-exp merge of normalised partials: one block per row, threads over D.
+template <typename OutT>
+__global__ void merge_lse_kernel(const float* __restrict__ po, const float* __restrict__ pl,
+                                 int n, int rows, int D, int64_t os, int64_t ls,
+                                 OutT* __restrict__ out, float* __restrict__ out_lse) {
+    const int r = blockIdx.x;
+    float M = -INFINITY;
+    for (int p = 0; p < n; ++p) M = fmaxf(M, pl[p * ls + r]);
+    float den = 0.f;
+    for (int p = 0; p < n; ++p) den += (M == -INFINITY) ? 0.f : expf(pl[p * ls + r] - M);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        float num = 0.f;
+        for (int p = 0; p < n; ++p) {
+            const float w = (M == -INFINITY) ? 0.f : expf(pl[p * ls + r] - M);
+            num += w * po[p * os + static_cast<int64_t>(r) * D + d];
+        }
+        out[static_cast<int64_t>(r) * D + d] = from_f32<OutT>(den > 0.f ? num / den : 0.f);
+    }
+    if (threadIdx.x == 0 && out_lse) out_lse[r] = den > 0.f ? M + logf(den) : -INFINITY;
+}
+
+// ---- launch plumbing -------------------------------------------------------------------
+
+struct WorkspaceLayout {
+    size_t counters, part_ml, part_o, total;
+};
+
+inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+WorkspaceLayout workspace_layout(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t S) {
+    WorkspaceLayout w;
+    w.counters = 0;
+    size_t c = align256(static_cast<size_t>(B * Hkv) * sizeof(int32_t));
+    w.part_ml = c;
+    size_t ml = align256(static_cast<size_t>(B * Hq * S * 2) * sizeof(float));
+    w.part_o = c + ml;
+    w.total = c + ml + align256(static_cast<size_t>(B * Hq * S * D) * sizeof(float));
+    return w;
+}
+
+template <typename T, int D, int GP, int TT, int STAGES>
+int launch_tiled(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
+    using Cfg = DecodeCfg<T, D, GP, TT, STAGES>;
+    auto* fn = decode_split_kernel<T, D, GP, TT, STAGES>;
+    const size_t bytes = static_cast<size_t>(Cfg::BYTES);
+    const size_t need_merge = (static_cast<size_t>(grid.x) + 2) * GP * 4;
+    if (need_merge > static_cast<size_t>(STAGES * 2 * Cfg::TILE))
+        return fail(TMLLM_INVALID_ARGUMENT, "too many splits (%u) for the merge scratch", grid.x);
+    TMLLM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(bytes)));
+    fn<<<grid, kDecodeThreads, bytes, s>>>(a);
+    TMLLM_LAUNCH_TRY();
+    return TMLLM_OK;
+}
+
+template <typename T, int D, int TT, int STAGES>
+int launch_gp(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
+    if (a.group <= 4) return launch_tiled<T, D, 4, TT, STAGES>(a, grid, s);
+    return launch_tiled<T, D, 8, TT, STAGES>(a, grid, s);
+}
+
+// Tiled configurations: (tile positions, ring depth) per (dtype, head_dim), each stage
+// 32 KB (K+V) so three stages fit two CTAs per SM.
+int launch_decode(int dtype, int D, const DecodeArgs& a, dim3 grid, cudaStream_t s, bool* done) {
+    *done = true;
+    if (dtype == TMLLM_F16) {
+        if (D == 64) return launch_gp<__half, 64, 128, 3>(a, grid, s);
+        if (D == 128) return launch_gp<__half, 128, 64, 3>(a, grid, s);
+        if (D == 256) return launch_gp<__half, 256, 32, 3>(a, grid, s);
+    } else {
+        if (D == 64) return launch_gp<float, 64, 64, 3>(a, grid, s);
+        if (D == 128) return launch_gp<float, 128, 32, 3>(a, grid, s);
+    }
+    *done = false;
+    return TMLLM_OK;
+}
+
+// Splits per (sequence, KV head): enough CTAs to fill every SM twice (two CTAs are
+// resident per SM), at least two for long sequences of a big batch so lengths balance,
+// and never chunks shorter than 256 positions.
+int32_t auto_splits(int64_t B, int64_t Hkv, int64_t max_len) {
+    const int64_t slots = static_cast<int64_t>(device_sm_count()) * 2;
+    int64_t bh = B * Hkv;
+    if (bh < 1) bh = 1;
+    int64_t s = (slots + bh - 1) / bh;
+    if (s < 2 && max_len > 1024) s = 2;
+    const int64_t by_len = (max_len + 255) / 256;
+    if (s > by_len) s = by_len;
+    if (s < 1) s = 1;
+    if (s > 1024) s = 1024;
+    return static_cast<int32_t>(s);
+}
+
+int32_t auto_splits_bound(int64_t B, int64_t Hkv) {
+    const int64_t slots = static_cast<int64_t>(device_sm_count()) * 2;
+    int64_t bh = B * Hkv;
+    if (bh < 1) bh = 1;
+    int64_t s = (slots + bh - 1) / bh;
+    if (s < 2) s = 2;
+    if (s > 1024) s = 1024;
+    return static_cast<int32_t>(s);
+}
+
+}  // namespace
+
+int decode_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, const void* v_new,
+                void* out, float* lse, int32_t q_heads, const tmllm_decode_opts* opts,
+                void* workspace, size_t workspace_bytes, int64_t max_len_hint,
+                cudaStream_t stream) {
+    if (!kv) return fail(TMLLM_INVALID_ARGUMENT, "null paged KV descriptor");
+    if (!valid_dtype(kv->dtype)) return fail(TMLLM_UNSUPPORTED_DTYPE, "unknown cache dtype");
+    const int D = kv->head_dim, Hkv = kv->num_kv_heads, B = kv->num_seqs;
+    if (B <= 0 || Hkv <= 0 || D <= 0 || kv->block_size <= 0 || kv->max_blocks_per_seq <= 0 ||
+        kv->num_blocks <= 0)
+        return fail(TMLLM_INVALID_SHAPE, "paged KV dimensions must be positive");
+    if (D % 2 != 0 || D > 512)
+        return fail(TMLLM_INVALID_SHAPE, "head_dim must be even and <= 512, got %d", D);
+    if (q_heads <= 0 || q_heads % Hkv != 0)
+        return fail(TMLLM_MODEL_FORMAT, "Q heads %d must be divisible by non-zero KV heads %d",
+                    q_heads, Hkv);
+    const int G = q_heads / Hkv;
+    if (G > 8) return fail(TMLLM_INVALID_SHAPE, "GQA group size %d exceeds 8", G);
+    if ((k_new == nullptr) != (v_new == nullptr))
+        return fail(TMLLM_INVALID_ARGUMENT, "k_new and v_new must both be given or both be NULL");
+    if (!q || !out || !kv->k_cache || !kv->v_cache || !kv->block_table || !kv->seq_lens)
+        return fail(TMLLM_INVALID_ARGUMENT, "null tensor pointer");
+    int64_t capacity;
+    if (!mul_ok(kv->block_size, kv->max_blocks_per_seq, &capacity) || capacity > INT32_MAX - 1)
+        return fail(TMLLM_INVALID_SHAPE, "sequence capacity exceeds i32");
+    tmllm_decode_opts o{};
+    if (opts) o = *opts;
+    if (o.out_dtype != TMLLM_F32 && o.out_dtype != kv->dtype)
+        return fail(TMLLM_UNSUPPORTED_DTYPE, "out dtype must be F32 or the cache dtype");
+    if (o.rope_cos && (!o.rope_sin || o.rope_len <= 0))
+        return fail(TMLLM_INVALID_ARGUMENT, "RoPE needs both tables and a positive length");
+    const float scale = o.scale > 0.f ? o.scale : 1.0f / sqrtf(static_cast<float>(D));
+    if (!std::isfinite(scale))
+        return fail(TMLLM_INVALID_SHAPE, "attention scale must be positive and finite");
+
+    int64_t hint = max_len_hint > 0 ? max_len_hint : capacity;
+    if (hint > capacity) hint = capacity;
+    int32_t splits = o.num_splits > 0 ? o.num_splits : auto_splits(B, Hkv, hint);
+    if (splits > 1024) splits = 1024;
+    int64_t chunk = (hint + splits - 1) / splits;
+    chunk = ((chunk + 127) / 128) * 128;
+    if (chunk < 128) chunk = 128;
+    if (chunk > INT32_MAX) chunk = INT32_MAX;
+
+    int bs_shift = -1;
+    if ((kv->block_size & (kv->block_size - 1)) == 0) {
+        bs_shift = 0;
+        while ((1 << bs_shift) < kv->block_size) ++bs_shift;
+    }
+
+    DecodeArgs a{};
+    a.q = q;
+    a.k_new = k_new;
+    a.v_new = v_new;
+    a.k_cache = kv->k_cache;
+    a.v_cache = kv->v_cache;
+    a.block_table = kv->block_table;
+    a.seq_lens = kv->seq_lens;
+    a.out = out;
+    a.lse = lse;
+    a.rope_cos = o.rope_cos;
+    a.rope_sin = o.rope_sin;
+    a.rope_len = o.rope_len;
+    a.rope_off = o.rope_pos_offset;
+    a.num_blocks = kv->num_blocks;
+    a.q_heads = q_heads;
+    a.kv_heads = Hkv;
+    a.group = G;
+    a.block_size = kv->block_size;
+    a.bs_shift = bs_shift;
+    a.max_blocks = kv->max_blocks_per_seq;
+    a.chunk = static_cast<int32_t>(chunk);
+    a.out_f32 = o.out_dtype == TMLLM_F32;
+    a.scale_log2 = scale * kLog2e;
+
+    const size_t es = dtype_size(kv->dtype);
+    auto misaligned = [es](const void* p) {
+        return p != nullptr && (reinterpret_cast<uintptr_t>(p) % es) != 0;
+    };
+    if (misaligned(kv->k_cache) || misaligned(kv->v_cache) || misaligned(q) ||
+        misaligned(k_new) || misaligned(v_new) || misaligned(out) ||
+        (reinterpret_cast<uintptr_t>(lse) & 3u) != 0)
+        return fail(TMLLM_INVALID_ARGUMENT, "tensor pointers must be aligned to their element size");
+    // The tiled kernel stages K/V with 16-byte copies: it needs 16-byte aligned arenas.
+    const int tiled_ok = (D == 64 || D == 128 || D == 256) &&
+                         !(kv->dtype == TMLLM_F32 && D == 256) && aligned16(kv->k_cache) &&
+                         aligned16(kv->v_cache);
+    if (tiled_ok) {
+        if (splits > 1) {
+            const WorkspaceLayout w = workspace_layout(B, q_heads, Hkv, D, splits);
+            if (!workspace || workspace_bytes < w.total)
+                return fail(TMLLM_INVALID_ARGUMENT,
+                            "decode workspace too small: need %zu bytes, got %zu", w.total,
+                            workspace_bytes);
+            unsigned char* base = static_cast<unsigned char*>(workspace);
+            a.counters = reinterpret_cast<int32_t*>(base + w.counters);
+            a.part_ml = reinterpret_cast<float*>(base + w.part_ml);
+            a.part_o = reinterpret_cast<float*>(base + w.part_o);
+        }
+        dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(Hkv),
+                  static_cast<unsigned>(B));
+        bool done = false;
+        int st = launch_decode(kv->dtype, D, a, grid, stream, &done);
+        if (done) return st;
+    }
+    // generic path: one CTA per (query head, sequence), no splits
+    const size_t smem = (3 * static_cast<size_t>(D) + 128 + 4) * sizeof(float);
+    dim3 grid(static_cast<unsigned>(q_heads), static_cast<unsigned>(B));
+    if (kv->dtype == TMLLM_F16)
+        decode_generic_kernel<__half><<<grid, 128, smem, stream>>>(a, D);
+    else
+        decode_generic_kernel<float><<<grid, 128, smem, stream>>>(a, D);
+    TMLLM_LAUNCH_TRY();
+    return TMLLM_OK;
+}
+
+size_t decode_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t splits) {
+    if (splits <= 1) return 256;
+    return workspace_layout(B, Hq, Hkv, D, splits).total;
+}
+
+int32_t decode_auto_splits(int64_t B, int64_t Hkv, int64_t max_len) {
+    return auto_splits(B, Hkv, max_len);
+}
+
+int32_t decode_auto_splits_bound(int64_t B, int64_t Hkv) { return auto_splits_bound(B, Hkv); }
+
+}  // namespace tmllm
+
+using namespace tmllm;
+
+extern "C" {
+
+size_t tmllm_decode_workspace_bytes(int32_t num_seqs, int32_t q_heads, int32_t kv_heads,
+                                    int32_t head_dim, int32_t num_splits) {
+    if (num_seqs <= 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0) return 0;
+    int64_t s = num_splits > 0 ? num_splits : auto_splits_bound(num_seqs, kv_heads);
+    return decode_workspace_bytes(num_seqs, q_heads, kv_heads, head_dim, s);
+}
+
+int tmllm_decode_workspace_init(void* workspace, size_t bytes, tmllm_stream stream) {
+    clear_error();
+    if (!workspace || bytes == 0) return fail(TMLLM_INVALID_ARGUMENT, "null workspace");
+    TMLLM_CUDA_TRY(cudaMemsetAsync(workspace, 0, bytes, reinterpret_cast<cudaStream_t>(stream)));
+    return TMLLM_OK;
+}
+
+int32_t tmllm_decode_auto_splits(int32_t num_seqs, int32_t kv_heads, int64_t max_len) {
+    return decode_auto_splits(num_seqs, kv_heads, max_len);
+}
+
+int tmllm_gqa_decode(const tmllm_paged_kv* kv, const void* q, const void* k_new,
+                     const void* v_new, void* out, float* lse, int32_t q_heads,
+                     const tmllm_decode_opts* opts, void* workspace, size_t workspace_bytes,
+                     tmllm_stream stream) {
+    clear_error();
+    return decode_impl(kv, q, k_new, v_new, out, lse, q_heads, opts, workspace, workspace_bytes,
+                       opts ? opts->max_len_hint : 0, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int tmllm_merge_lse(const float* parts_o, const float* parts_lse, int32_t num_parts,
+                    int32_t rows, int32_t head_dim, int64_t o_stride, int64_t lse_stride,
+                    void* out, int32_t out_dtype, float* out_lse, tmllm_stream stream) {
+    clear_error();
+    if (num_parts <= 0 || rows <= 0 || head_dim <= 0)
+        return fail(TMLLM_INVALID_SHAPE, "merge dimensions must be positive");
+    if (!valid_dtype(out_dtype)) return fail(TMLLM_UNSUPPORTED_DTYPE, "unknown dtype");
+    if (!parts_o || !parts_lse || !out) return fail(TMLLM_INVALID_ARGUMENT, "null pointer");
+    const int64_t os = o_stride > 0 ? o_stride : static_cast<int64_t>(rows) * head_dim;
+    const int64_t ls = lse_stride > 0 ? lse_stride : rows;
+    if (os < static_cast<int64_t>(rows) * head_dim || ls < rows)
+        return fail(TMLLM_INVALID_SHAPE, "merge strides overlap the parts");
+    auto s = reinterpret_cast<cudaStream_t>(stream);
+    const int threads = head_dim >= 128 ? 128 : 64;
+    if (out_dtype == TMLLM_F16)
+        merge_lse_kernel<__half><<<rows, threads, 0, s>>>(parts_o, parts_lse, num_parts, rows,
+                                                          head_dim, os, ls,
+                                                          static_cast<__half*>(out), out_lse);
+    else
+        merge_lse_kernel<float><<<rows, threads, 0, s>>>(parts_o, parts_lse, num_parts, rows,
+                                                         head_dim, os, ls,
+                                                         static_cast<float*>(out), out_lse);
+    TMLLM_LAUNCH_TRY();
+    return TMLLM_OK;
+}
+
+}  // extern "C"

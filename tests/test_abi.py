@@ -1,0 +1,104 @@
+"""The C-ABI library loads, exports every function include/tmllm.h declares, and rejects
+bad arguments on the host with the reference's error kinds -- all without a GPU (no call
+here reaches a kernel)."""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+import numpy as np
+import pytest
+
+from rustllm_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions() -> list[str]:
+    src = open(os.path.join(ROOT, "include", "tmllm.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(tmllm_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_functions()
+    assert len(names) >= 30
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    # and the Python binding covers all of them
+    assert set(names) <= set(_lib._PROTOS), set(names) - set(_lib._PROTOS)
+
+
+def test_status_names_and_version():
+    lib = _lib.load()
+    assert lib.tmllm_version() >= 100
+    for code, cls in _lib._BY_STATUS.items():
+        assert lib.tmllm_status_name(code).decode().startswith("TMLLM_")
+        assert cls.status == code
+    assert lib.tmllm_status_name(0) == b"TMLLM_OK"
+
+
+def rc(name, *args):
+    return getattr(_lib.load(), name)(*args)
+
+
+def test_host_validation_codes():
+    """Argument errors are reported before any device work (kv_cache_write.rs:577-586,
+    repeat_kv.rs:20-25, attention_scale_mask.rs validate, softmax.rs validate, ...)."""
+    dummy = C.c_void_p(16)
+    # start + source_seq > max_seq
+    assert rc("tmllm_kv_cache_write", 1, dummy, dummy, 2, 8, 4, 7, 2, None) == 7
+    assert rc("tmllm_kv_cache_write", 7, dummy, dummy, 2, 8, 4, 0, 1, None) == 5
+    assert rc("tmllm_repeat_kv", 0, dummy, dummy, 1, 2, 2, 2, 0, None) == 8
+    assert rc("tmllm_gqa_qk", 0, dummy, dummy, dummy, 1, 5, 2, 1, 4, 4, 4, None) == 8
+    assert rc("tmllm_gqa_qk", 0, dummy, dummy, dummy, 1, 4, 2, 1, 5, 4, 4, None) == 2
+    assert rc("tmllm_attention_scale_mask", 0, dummy, dummy, 9, 3, 3, 0, 0.0, None) == 2
+    assert rc("tmllm_attention_scale_mask", 0, dummy, dummy, 9, 3, 3, 1, 0.5, None) == 2
+    assert rc("tmllm_attention_scale_mask", 0, dummy, dummy, 8, 3, 3, 0, 0.5, None) == 2
+    assert rc("tmllm_softmax_last_dim", 0, dummy, dummy, 0, 4, None) == 2
+    assert rc("tmllm_rope", 0, dummy, dummy, dummy, dummy, 8, 1, 2, 3, 0, None) == 2
+    assert rc("tmllm_rope", 0, dummy, dummy, dummy, dummy, 8, 1, 4, 4, 5, None) == 2
+    assert b"position range is invalid" in _lib.load().tmllm_last_error()
+    cfg = _lib.CacheConfig(device=0, num_layers=1, num_seqs=1, max_seq_len=0, block_size=16,
+                           num_kv_heads=2, head_dim=4, dtype=1)
+    h = C.c_void_p()
+    assert rc("tmllm_cache_create", C.byref(cfg), C.byref(h)) == 2  # kv_cache.rs:61-65
+    assert h.value is None
+    opts = _lib.DecodeOpts()
+    kv = _lib.PagedKV(k_cache=16, v_cache=16, block_table=16, seq_lens=16, num_blocks=4,
+                      num_seqs=1, num_kv_heads=3, head_dim=64, block_size=16,
+                      max_blocks_per_seq=4, dtype=1)
+    assert rc("tmllm_gqa_decode", C.byref(kv), dummy, None, None, dummy, None, 8,
+              C.byref(opts), None, 0, None) == 8  # 8 q heads over 3 kv heads
+    assert rc("tmllm_gqa_decode", C.byref(kv), dummy, dummy, None, dummy, None, 9,
+              C.byref(opts), None, 0, None) == 1  # k_new without v_new
+
+
+def test_error_mapping_raises_reference_kinds():
+    with pytest.raises(_lib.PositionOutOfRange):
+        _lib.call("tmllm_kv_cache_write", 1, C.c_void_p(16), C.c_void_p(16), 2, 8, 4, 7, 2, None)
+    with pytest.raises(_lib.ModelFormat):
+        _lib.call("tmllm_repeat_kv", 0, C.c_void_p(16), C.c_void_p(16), 1, 2, 2, 2, 0, None)
+
+
+def test_rope_tables_bit_exact_with_oracle(orc):
+    """tmllm_rope_tables (host-side, as the reference builds them) equals the oracle."""
+    for d, n, theta in [(64, 300, 100000.0), (4, 8, 10000.0), (128, 64, 500000.0)]:
+        cos = np.empty((n, d // 2), np.float32)
+        sin = np.empty((n, d // 2), np.float32)
+        _lib.call("tmllm_rope_tables", cos.ctypes.data, sin.ctypes.data, d, n, theta)
+        oc, os_ = orc.rope_tables(d, n, theta)
+        assert np.array_equal(cos, oc) and np.array_equal(sin, os_)
+
+
+def test_workspace_size_arithmetic():
+    lib = _lib.load()
+    b, hq, hkv, d, s = 2, 32, 8, 128, 37
+    got = lib.tmllm_decode_workspace_bytes(b, hq, hkv, d, s)
+
+    def up(x):
+        return (x + 255) // 256 * 256
+    assert got == up(b * hkv * 4) + up(b * hq * s * 2 * 4) + up(b * hq * s * d * 4)
+    assert lib.tmllm_decode_workspace_bytes(0, hq, hkv, d, s) == 0
