@@ -220,8 +220,10 @@ def run_ours(args) -> None:
     from rustllm_b200.distributed import SequenceSplitAttention
 
     torch.manual_seed(1234 + rank)
-    sp = SequenceSplitAttention(CACHED, HQ, HKV, D, dtype=torch.float16, block_size=BS,
-                                shuffle_seed=77 + rank, device=dev)
+    cached = args.cached
+    sp = SequenceSplitAttention(cached, HQ, HKV, D, dtype=torch.float16, block_size=BS,
+                                shuffle_seed=77 + rank, device=dev, variant=args.variant,
+                                num_splits=args.splits)
     n_local = sp.hi - sp.lo
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     # fill in slabs to bound the temporary footprint
@@ -324,7 +326,7 @@ def run_ours(args) -> None:
 
     if rank == 0:
         peaks = load_peaks()
-        launch_bytes = algorithmic_bytes(cached=n_local if world > 1 else CACHED)
+        launch_bytes = algorithmic_bytes(cached=n_local if world > 1 else cached)
         if world > 1 and not sp.owner:
             launch_bytes = 2 * HKV * n_local * D * ESIZE + 2 * HQ * D * ESIZE
         achieved = launch_bytes / (k_ms * 1e-3) / 1e9
@@ -339,27 +341,31 @@ def run_ours(args) -> None:
                        "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "cached": CACHED,
                        "block_size": BS, "parallelism": f"seqsplit{world}" if world > 1 else "1gpu",
                        "l2": "inputs larger than L2 (537 MB K/V per step vs 126 MB L2)"},
-            "hbm_gbs": algorithmic_bytes() / (ms_step * 1e-3) / 1e9,
+            "hbm_gbs": algorithmic_bytes(cached=cached) / (ms_step * 1e-3) / 1e9,
             "gpu_launches": args.steps * (2 if world > 1 else 1),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                          "peak_source": peaks["source"], "traffic": args.traffic,
-                         "kernel": "decode_split_kernel<half,128,4,64,3>",
+                         "kernel": ("decode_split_kernel<__half,128,4,64,3>" if args.variant == 1
+                                    else "decode_mma_kernel<128,3>"),
                          "kernel_ms": k_ms, "bytes_per_launch": launch_bytes},
             "e2e": {"value": e2e_tok_s, "unit": "tok/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "clocks": clocks,
         }
+        if cached != CACHED:
+            line["config"]["cached"] = cached
+            line["config"]["workload"] += f" (reduced to {cached} cached for a capture)"
         if world == 1 and not args.no_cpu:
             import numpy as np
             kd, vd = sp.cache.gather(0, 0)
-            L = CACHED + 1
+            L = cached + 1
             kc = np.empty((1, HKV, L, D), np.float16)
             vc = np.empty((1, HKV, L, D), np.float16)
-            kc[0, :, :CACHED] = kd.cpu().numpy()
-            vc[0, :, :CACHED] = vd.cpu().numpy()
-            kc[0, :, CACHED] = kn[0].cpu().numpy()
-            vc[0, :, CACHED] = vn[0].cpu().numpy()
+            kc[0, :, :cached] = kd.cpu().numpy()
+            vc[0, :, :cached] = vd.cpu().numpy()
+            kc[0, :, cached] = kn[0].cpu().numpy()
+            vc[0, :, cached] = vn[0].cpu().numpy()
             threads = os.cpu_count() or 1
             steps, secs = cpu_time(args.cpu_budget, 1000, threads,
                                    (q[:, :, None].cpu().numpy(), kc, vc))
@@ -382,6 +388,11 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--ref-budget", type=float, default=60.0)
+    ap.add_argument("--variant", type=int, default=0,
+                    help="decode kernel: 0 auto (tensor-core for F16), 1 CUDA-core, 2 tensor-core")
+    ap.add_argument("--splits", type=int, default=0, help="split count (0 = automatic)")
+    ap.add_argument("--cached", type=int, default=CACHED,
+                    help="cached positions (smaller values only for profiling captures)")
     ap.add_argument("--traffic", type=float, default=None,
                     help="ncu DRAM bytes per launch of the decode kernel (from profiles/)")
     args = ap.parse_args()

@@ -173,6 +173,9 @@ typedef struct tmllm_decode_opts {
     int32_t rope_pos_offset;
     int64_t max_len_hint;   /* longest sequence this call sees, for the split choice;  */
                             /* 0 = the capacity.  Affects speed only, never results.   */
+    int32_t variant;        /* 0 = automatic; 1 = CUDA-core FMA kernel; 2 = tensor-core */
+                            /* (mma.sync) kernel, F16 with head_dim 64 or 128 only     */
+    int32_t reserved;
 } tmllm_decode_opts;
 
 /* Bytes of scratch tmllm_gqa_decode needs for `num_splits` splits (0 = enough for any

@@ -102,7 +102,8 @@ class DecodeOpts(C.Structure):
 
     _fields_ = [("scale", C.c_float), ("num_splits", i32), ("out_dtype", i32),
                 ("rope_cos", vp), ("rope_sin", vp), ("rope_len", i32),
-                ("rope_pos_offset", i32), ("max_len_hint", i64)]
+                ("rope_pos_offset", i32), ("max_len_hint", i64), ("variant", i32),
+                ("reserved", i32)]
 
 
 class CacheConfig(C.Structure):

@@ -42,7 +42,8 @@ def gqa_decode(kv: PagedKV, q: torch.Tensor, k_new: torch.Tensor | None,
                v_new: torch.Tensor | None, workspace: DecodeWorkspace, *,
                out: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
                lse: torch.Tensor | None = None, scale: float = 0.0, num_splits: int = 0,
-               max_len_hint: int = 0, rope=None, rope_pos_offset: int = 0) -> torch.Tensor:
+               max_len_hint: int = 0, rope=None, rope_pos_offset: int = 0,
+               variant: int = 0) -> torch.Tensor:
     """Fused KV-append + GQA decode attention (``tmllm_gqa_decode``).
 
     q [num_seqs, Hq, D]; k_new, v_new [num_seqs, Hkv, D] or both None; out
@@ -50,7 +51,8 @@ def gqa_decode(kv: PagedKV, q: torch.Tensor, k_new: torch.Tensor | None,
     if out is None:
         out = torch.empty(q.shape, dtype=out_dtype or q.dtype, device=q.device)
     opts = DecodeOpts(scale=scale, num_splits=num_splits, out_dtype=dtype_code(out.dtype),
-                      rope_pos_offset=rope_pos_offset, max_len_hint=max_len_hint)
+                      rope_pos_offset=rope_pos_offset, max_len_hint=max_len_hint,
+                      variant=variant)
     if rope is not None:
         cos, sin = rope
         opts.rope_cos, opts.rope_sin, opts.rope_len = cos.data_ptr(), sin.data_ptr(), cos.shape[0]

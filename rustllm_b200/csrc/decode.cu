@@ -472,6 +472,397 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_split_kernel(const D
     if (tid == 0) a.counters[static_cast<int64_t>(b) * a.kv_heads + kvh] = 0;
 }
 
+// ---- F16 tensor-core variant ----------------------------------------------------------
+//
+// Same contract as decode_split_kernel, for F16 caches with D in {64, 128} and G <= 16.
+// The two skinny contractions run on the warp-level tensor cores (mma.sync m16n8k16, F16
+// inputs, F32 accumulation): S[16 x 16] = Q[16 x D] K^T per 16-position sub-tile with the
+// query heads (padded to 16 rows) as M, and O[16 x D] += P[16 x 16] V with P taken straight
+// from S's accumulator registers (the C layout of S is the A layout of P).  Each of the 4
+// warps runs its own cp.async ring of 16-position sub-tiles (sub-tiles w, w+4, ... of the
+// CTA's chunk) and its own online softmax, so warps never wait on each other inside the
+// loop; the four (m, l, O) states are combined once at the end.
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                          uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+template <int D, int STAGES>
+struct MmaCfg {
+    static constexpr int C = D / 8;         // 16-byte chunks per row
+    static constexpr int ROW = D * 2;       // bytes per row
+    static constexpr int SUB = 16;          // positions per warp sub-tile
+    static constexpr int SUBB = SUB * ROW;  // bytes of one K (or V) sub-tile
+    static constexpr int WARP_RING = STAGES * 2 * SUBB;
+    static constexpr int QROW = D + 8;      // padded q row (halves)
+    static constexpr int OFF_Q = 4 * WARP_RING;
+    static constexpr int OFF_ST = OFF_Q + 16 * QROW * 2;  // m, l per warp x row + flag
+    static constexpr int OFF_NEW = OFF_ST + (2 * 4 * 16 + 16) * 4;
+    static constexpr int BYTES = OFF_NEW + 2 * ROW;
+    static constexpr int LOADS = SUB * C / 32;  // 16-byte copies per lane per K sub-tile
+    static constexpr int RSTEP = 32 / C;
+    static_assert(C == 8 || C == 16, "D must be 64 or 128");
+    static_assert(4 * WARP_RING >= 4 * 16 * D * 4, "warp-merge scratch fits in the rings");
+};
+
+template <int D, int STAGES>
+__global__ void __launch_bounds__(kDecodeThreads, 2) decode_mma_kernel(const DecodeArgs a) {
+    using Cfg = MmaCfg<D, STAGES>;
+    constexpr int C = Cfg::C, ROW = Cfg::ROW, SUBB = Cfg::SUBB, QROW = Cfg::QROW;
+    constexpr int KS = D / 16;  // k-steps of QK
+    constexpr int NT = D / 8;   // n-tiles of PV
+    extern __shared__ __align__(128) unsigned char smem[];
+    __half* q_s = reinterpret_cast<__half*>(smem + Cfg::OFF_Q);  // [16][QROW]
+    float* wm = reinterpret_cast<float*>(smem + Cfg::OFF_ST);    // [4][16]
+    float* wl = wm + 64;                                          // [4][16]
+    int* flag_s = reinterpret_cast<int*>(wl + 64);
+    __half* knew_s = reinterpret_cast<__half*>(smem + Cfg::OFF_NEW);
+    __half* vnew_s = knew_s + D;
+
+    const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = a.group;
+    const int cached = a.seq_lens[b] < 0 ? 0 : a.seq_lens[b];
+    const bool has_new = a.k_new != nullptr;
+    const int L = cached + (has_new ? 1 : 0);
+    int splits_b = (L + a.chunk - 1) / a.chunk;
+    if (splits_b < 1) splits_b = 1;
+    if (splits_b > static_cast<int>(gridDim.x)) splits_b = gridDim.x;
+    if (split >= splits_b) return;
+    const int t0 = split * a.chunk;
+    const int t1 = (split == splits_b - 1) ? L : min(L, t0 + a.chunk);
+    const int nsub = t1 > t0 ? (t1 - t0 + 15) / 16 : 0;
+    const bool owns_new = has_new && cached >= t0 && cached < t1;
+    const int half = D / 2;
+    const int qpos = cached + a.rope_off;
+
+    // ---- q rows (rotated, rounded to F16) into q_s; rows >= G are zero
+    for (int idx = tid; idx < 16 * half; idx += kDecodeThreads) {
+        const int g = idx / half, i = idx - g * half;
+        float x1 = 0.f, x2 = 0.f;
+        if (g < G) {
+            const __half* qr = static_cast<const __half*>(a.q) +
+                               (static_cast<int64_t>(b) * a.q_heads + kvh * G + g) * D;
+            x1 = __half2float(qr[i]);
+            x2 = __half2float(qr[i + half]);
+            rope_pair(a, qpos, i, half, x1, x2);
+        }
+        q_s[g * QROW + i] = __float2half_rn(x1);
+        q_s[g * QROW + i + half] = __float2half_rn(x2);
+    }
+    if (owns_new) {
+        const int64_t nrow = (static_cast<int64_t>(b) * a.kv_heads + kvh) * D;
+        const __half* kn = static_cast<const __half*>(a.k_new) + nrow;
+        const __half* vn = static_cast<const __half*>(a.v_new) + nrow;
+        for (int i = tid; i < half; i += kDecodeThreads) {
+            float x1 = __half2float(kn[i]), x2 = __half2float(kn[i + half]);
+            rope_pair(a, qpos, i, half, x1, x2);
+            knew_s[i] = __float2half_rn(x1);
+            knew_s[i + half] = __float2half_rn(x2);
+            vnew_s[i] = vn[i];
+            vnew_s[i + half] = vn[i + half];
+        }
+    }
+    __syncthreads();
+    if (owns_new) {
+        const int64_t blk = block_of(a, b, cached);
+        if (blk >= 0) {
+            const int64_t off =
+                ((blk * a.kv_heads + kvh) * a.block_size + offset_in_block(a, cached)) * D;
+            __half* kd = static_cast<__half*>(a.k_cache) + off;
+            __half* vd = static_cast<__half*>(a.v_cache) + off;
+            for (int i = tid; i < D; i += kDecodeThreads) {
+                kd[i] = knew_s[i];
+                vd[i] = vnew_s[i];
+            }
+        }
+    }
+
+    // ---- Q fragments (A operand, 16 rows x D) into registers
+    uint32_t qa[KS][4];
+    {
+        const int mi = lane >> 3, r = (mi & 1) * 8 + (lane & 7);
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            const int col = ks * 16 + (mi >> 1) * 8;
+            ldsm_x4(smem_u32(q_s + r * QROW + col), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+        }
+    }
+
+    // ---- this warp's cp.async ring: sub-tiles warp, warp+4, ... of the chunk
+    unsigned char* ring = smem + warp * Cfg::WARP_RING;
+    const int nmine = nsub > warp ? (nsub - warp + 3) / 4 : 0;
+    const unsigned char* kbase = static_cast<const unsigned char*>(a.k_cache);
+    const unsigned char* vbase = static_cast<const unsigned char*>(a.v_cache);
+    const int lc = lane % C, lr0 = lane / C;
+    const bool whole_blocks = (a.block_size % 16) == 0;
+    auto load_sub = [&](int j, int stage) {
+        unsigned char* ks = ring + stage * 2 * SUBB;
+        unsigned char* vs = ks + SUBB;
+        const int base = t0 + (warp + 4 * j) * 16;
+        int64_t row0 = -1;  // arena row of position `base` when the sub-tile is one block
+        if (whole_blocks) {
+            const int64_t blk = block_of(a, b, base);
+            if (blk >= 0)
+                row0 = (blk * a.kv_heads + kvh) * a.block_size + offset_in_block(a, base);
+        }
+#pragma unroll
+        for (int k = 0; k < Cfg::LOADS; ++k) {
+            const int r = lr0 + k * Cfg::RSTEP;
+            const int pos = base + r;
+            const unsigned char* ksrc = kbase;
+            const unsigned char* vsrc = vbase;
+            int bytes = 0;
+            if (pos < cached && pos < t1) {
+                int64_t arow = -1;
+                if (whole_blocks) {
+                    if (row0 >= 0) arow = row0 + r;
+                } else {
+                    const int64_t blk = block_of(a, b, pos);
+                    if (blk >= 0)
+                        arow = (blk * a.kv_heads + kvh) * a.block_size + offset_in_block(a, pos);
+                }
+                if (arow >= 0) {
+                    const int64_t off = arow * ROW + lc * 16;
+                    ksrc += off;
+                    vsrc += off;
+                    bytes = 16;
+                }
+            }
+            const int dst = r * ROW + swz<C>(r, lc) * 16;
+            cp_async16(ks + dst, ksrc, bytes);
+            cp_async16(vs + dst, vsrc, bytes);
+        }
+    };
+#pragma unroll
+    for (int s = 0; s < STAGES - 1; ++s) {
+        if (s < nmine) load_sub(s, s);
+        cp_async_commit();
+    }
+
+    float o[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+    const int g4 = lane >> 2, t4 = lane & 3;
+
+    for (int it = 0; it < nmine; ++it) {
+        cp_async_wait<STAGES - 2>();
+        __syncwarp();
+        {
+            const int nt = it + STAGES - 1;
+            if (nt < nmine) load_sub(nt, nt % STAGES);
+            cp_async_commit();
+        }
+        unsigned char* ks = ring + (it % STAGES) * 2 * SUBB;
+        unsigned char* vs = ks + SUBB;
+        const int base = t0 + (warp + 4 * it) * 16;
+        if (owns_new && cached >= base && cached < base + 16) {
+            const int r = cached - base;
+            if (lane < C) {
+                *reinterpret_cast<uint4*>(ks + r * ROW + swz<C>(r, lane) * 16) =
+                    reinterpret_cast<const uint4*>(knew_s)[lane];
+                *reinterpret_cast<uint4*>(vs + r * ROW + swz<C>(r, lane) * 16) =
+                    reinterpret_cast<const uint4*>(vnew_s)[lane];
+            }
+            __syncwarp();
+        }
+        // S = Q K^T: two n-tiles of 8 positions
+        float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        {
+            const int mi = lane >> 3, r = (mi >> 1) * 8 + (lane & 7);
+            const uint32_t rbase = smem_u32(ks + r * ROW);
+#pragma unroll
+            for (int kstep = 0; kstep < KS; ++kstep) {
+                const int c = kstep * 2 + (mi & 1);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(rbase + swz<C>(r, c) * 16, b0, b1, b2, b3);
+                mma16816(sc[0], qa[kstep][0], qa[kstep][1], qa[kstep][2], qa[kstep][3], b0, b1);
+                mma16816(sc[1], qa[kstep][0], qa[kstep][1], qa[kstep][2], qa[kstep][3], b2, b3);
+            }
+        }
+        // online softmax over the 16 positions, rows g4 and g4 + 8
+        float alpha[2];
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+            float mx = -INFINITY;
+#pragma unroll
+            for (int n = 0; n < 2; ++n)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int pos = base + n * 8 + t4 * 2 + e;
+                    float v = pos < t1 ? sc[n][rr * 2 + e] * a.scale_log2 : -INFINITY;
+                    sc[n][rr * 2 + e] = v;
+                    mx = fmaxf(mx, v);
+                }
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            const float m_new = fmaxf(m_r[rr], mx);
+            alpha[rr] = (m_new == -INFINITY) ? 1.f : exp2f(m_r[rr] - m_new);
+            float sum = 0.f;
+#pragma unroll
+            for (int n = 0; n < 2; ++n)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const float p =
+                        (m_new == -INFINITY) ? 0.f : exp2f(sc[n][rr * 2 + e] - m_new);
+                    sc[n][rr * 2 + e] = p;
+                    sum += p;
+                }
+            l_r[rr] = l_r[rr] * alpha[rr] + sum;
+            m_r[rr] = m_new;
+        }
+        if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                o[j][0] *= alpha[0];
+                o[j][1] *= alpha[0];
+                o[j][2] *= alpha[1];
+                o[j][3] *= alpha[1];
+            }
+        }
+        // O += P V: P's A fragment is S's accumulator layout
+        const uint32_t pa0 = pack_half2(sc[0][0], sc[0][1]);
+        const uint32_t pa1 = pack_half2(sc[0][2], sc[0][3]);
+        const uint32_t pa2 = pack_half2(sc[1][0], sc[1][1]);
+        const uint32_t pa3 = pack_half2(sc[1][2], sc[1][3]);
+        {
+            const int mi = lane >> 3, r = (mi & 1) * 8 + (lane & 7);
+            const uint32_t rbase = smem_u32(vs + r * ROW);
+#pragma unroll
+            for (int jj = 0; jj < NT / 2; ++jj) {
+                const int c = jj * 2 + (mi >> 1);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_t(rbase + swz<C>(r, c) * 16, b0, b1, b2, b3);
+                mma16816(o[2 * jj], pa0, pa1, pa2, pa3, b0, b1);
+                mma16816(o[2 * jj + 1], pa0, pa1, pa2, pa3, b2, b3);
+            }
+        }
+    }
+    cp_async_wait<0>();
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+        l_r[rr] += __shfl_xor_sync(0xffffffffu, l_r[rr], 1);
+        l_r[rr] += __shfl_xor_sync(0xffffffffu, l_r[rr], 2);
+    }
+    __syncthreads();
+
+    // ---- combine the four warps: red[w][16][D] (rings are free now)
+    float* red = reinterpret_cast<float*>(smem);
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+        const int d = j * 8 + t4 * 2;
+        red[(warp * 16 + g4) * D + d] = o[j][0];
+        red[(warp * 16 + g4) * D + d + 1] = o[j][1];
+        red[(warp * 16 + g4 + 8) * D + d] = o[j][2];
+        red[(warp * 16 + g4 + 8) * D + d + 1] = o[j][3];
+    }
+    if (t4 == 0) {
+        wm[warp * 16 + g4] = m_r[0];
+        wm[warp * 16 + g4 + 8] = m_r[1];
+        wl[warp * 16 + g4] = l_r[0];
+        wl[warp * 16 + g4 + 8] = l_r[1];
+    }
+    __syncthreads();
+    // per row g: M = max_w m_w, weights 2^(m_w - M)
+    const int64_t qh0 = static_cast<int64_t>(b) * a.q_heads + static_cast<int64_t>(kvh) * G;
+    const int64_t pbase = ((static_cast<int64_t>(b) * a.kv_heads + kvh) * gridDim.x) * G;
+    for (int idx = tid; idx < G * D; idx += kDecodeThreads) {
+        const int g = idx / D, d = idx - g * D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w * 16 + g]);
+        float num = 0.f, den = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const float wt = (M == -INFINITY) ? 0.f : exp2f(wm[w * 16 + g] - M);
+            num += wt * red[(w * 16 + g) * D + d];
+            den += wt * wl[w * 16 + g];
+        }
+        if (splits_b == 1) {
+            const float ov = den > 0.f ? num / den : 0.f;
+            if (a.out_f32)
+                static_cast<float*>(a.out)[(qh0 + g) * D + d] = ov;
+            else
+                static_cast<__half*>(a.out)[(qh0 + g) * D + d] = __float2half_rn(ov);
+            if (d == 0 && a.lse) a.lse[qh0 + g] = den > 0.f ? (M + log2f(den)) * kLn2 : -INFINITY;
+        } else {
+            a.part_o[(pbase + static_cast<int64_t>(split) * G + g) * D + d] = num;
+            if (d == 0) {
+                a.part_ml[(pbase + static_cast<int64_t>(split) * G + g) * 2 + 0] = M;
+                a.part_ml[(pbase + static_cast<int64_t>(split) * G + g) * 2 + 1] = den;
+            }
+        }
+    }
+    if (splits_b == 1) return;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const int ticket = atomicAdd(&a.counters[static_cast<int64_t>(b) * a.kv_heads + kvh], 1);
+        *flag_s = (ticket == splits_b - 1);
+    }
+    __syncthreads();
+    if (!*flag_s) return;
+    __threadfence();
+    float* wts = reinterpret_cast<float*>(smem);  // [splits_b][16] (red is consumed)
+    float* Ms = wts + static_cast<int64_t>(gridDim.x) * 16;
+    float* dens = Ms + 16;
+    if (tid < G) {
+        float M = -INFINITY;
+        for (int s2 = 0; s2 < splits_b; ++s2)
+            M = fmaxf(M, __ldcg(&a.part_ml[(pbase + static_cast<int64_t>(s2) * G + tid) * 2]));
+        float dsum = 0.f;
+        for (int s2 = 0; s2 < splits_b; ++s2) {
+            const float* ml = a.part_ml + (pbase + static_cast<int64_t>(s2) * G + tid) * 2;
+            const float w = (M == -INFINITY) ? 0.f : exp2f(__ldcg(ml) - M);
+            wts[s2 * 16 + tid] = w;
+            dsum += w * __ldcg(ml + 1);
+        }
+        Ms[tid] = M;
+        dens[tid] = dsum;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < G * D; idx += kDecodeThreads) {
+        const int g = idx / D, d = idx - g * D;
+        float num = 0.f;
+        for (int s2 = 0; s2 < splits_b; ++s2)
+            num += wts[s2 * 16 + g] *
+                   __ldcg(&a.part_o[(pbase + static_cast<int64_t>(s2) * G + g) * D + d]);
+        const float dn = dens[g];
+        const float ov = dn > 0.f ? num / dn : 0.f;
+        if (a.out_f32)
+            static_cast<float*>(a.out)[(qh0 + g) * D + d] = ov;
+        else
+            static_cast<__half*>(a.out)[(qh0 + g) * D + d] = __float2half_rn(ov);
+        if (d == 0 && a.lse) a.lse[qh0 + g] = dn > 0.f ? (Ms[g] + log2f(dn)) * kLn2 : -INFINITY;
+    }
+    if (tid == 0) a.counters[static_cast<int64_t>(b) * a.kv_heads + kvh] = 0;
+}
+
 // Any even head_dim: one CTA per (seq, query head), tiles of 128 positions, one thread per
 // position for QK^T and one thread per dimension for PV.  Used for head sizes the tiled
 // kernel does not instantiate (the reference's unit tests use D = 2 and 4).
@@ -652,6 +1043,20 @@ int launch_tiled(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
     return TMLLM_OK;
 }
 
+template <int D, int STAGES>
+int launch_mma(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
+    using Cfg = MmaCfg<D, STAGES>;
+    auto* fn = decode_mma_kernel<D, STAGES>;
+    const size_t bytes = static_cast<size_t>(Cfg::BYTES);
+    if ((static_cast<size_t>(grid.x) + 2) * 16 * 4 > static_cast<size_t>(4 * Cfg::WARP_RING))
+        return fail(TMLLM_INVALID_ARGUMENT, "too many splits (%u) for the merge scratch", grid.x);
+    TMLLM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(bytes)));
+    fn<<<grid, kDecodeThreads, bytes, s>>>(a);
+    TMLLM_LAUNCH_TRY();
+    return TMLLM_OK;
+}
+
 template <typename T, int D, int TT, int STAGES>
 int launch_gp(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
     if (a.group <= 4) return launch_tiled<T, D, 4, TT, STAGES>(a, grid, s);
@@ -660,13 +1065,18 @@ int launch_gp(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
 
 // Tiled configurations: (tile positions, ring depth) per (dtype, head_dim), each stage
 // 32 KB (K+V) so three stages fit two CTAs per SM.
-int launch_decode(int dtype, int D, const DecodeArgs& a, dim3 grid, cudaStream_t s, bool* done) {
+int launch_decode(int dtype, int D, int variant, const DecodeArgs& a, dim3 grid, cudaStream_t s,
+                  bool* done) {
     *done = true;
-    if (dtype == TMLLM_F16) {
+    if (dtype == TMLLM_F16 && a.group <= 16 && variant != 1) {
+        if (D == 64) return launch_mma<64, 3>(a, grid, s);
+        if (D == 128) return launch_mma<128, 3>(a, grid, s);
+    }
+    if (dtype == TMLLM_F16 && a.group <= 8) {
         if (D == 64) return launch_gp<__half, 64, 128, 3>(a, grid, s);
         if (D == 128) return launch_gp<__half, 128, 64, 3>(a, grid, s);
         if (D == 256) return launch_gp<__half, 256, 32, 3>(a, grid, s);
-    } else {
+    } else if (dtype == TMLLM_F32 && a.group <= 8) {
         if (D == 64) return launch_gp<float, 64, 64, 3>(a, grid, s);
         if (D == 128) return launch_gp<float, 128, 32, 3>(a, grid, s);
     }
@@ -718,7 +1128,15 @@ int decode_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, cons
         return fail(TMLLM_MODEL_FORMAT, "Q heads %d must be divisible by non-zero KV heads %d",
                     q_heads, Hkv);
     const int G = q_heads / Hkv;
-    if (G > 8) return fail(TMLLM_INVALID_SHAPE, "GQA group size %d exceeds 8", G);
+    if (opts && (opts->variant < 0 || opts->variant > 2))
+        return fail(TMLLM_INVALID_ARGUMENT, "unknown decode variant %d", opts->variant);
+    const bool mma_shape = kv->dtype == TMLLM_F16 && (D == 64 || D == 128) &&
+                           !(opts && opts->variant == 1);
+    if (opts && opts->variant == 2 && !mma_shape)
+        return fail(TMLLM_INVALID_ARGUMENT, "the tensor-core decode needs F16 and head_dim 64/128");
+    if (G > (mma_shape ? 16 : 8))
+        return fail(TMLLM_INVALID_SHAPE, "GQA group size %d exceeds %d for this head size", G,
+                    mma_shape ? 16 : 8);
     if ((k_new == nullptr) != (v_new == nullptr))
         return fail(TMLLM_INVALID_ARGUMENT, "k_new and v_new must both be given or both be NULL");
     if (!q || !out || !kv->k_cache || !kv->v_cache || !kv->block_table || !kv->seq_lens)
@@ -803,7 +1221,7 @@ int decode_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, cons
         dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(Hkv),
                   static_cast<unsigned>(B));
         bool done = false;
-        int st = launch_decode(kv->dtype, D, a, grid, stream, &done);
+        int st = launch_decode(kv->dtype, D, o.variant, a, grid, stream, &done);
         if (done) return st;
     }
     // generic path: one CTA per (query head, sequence), no splits

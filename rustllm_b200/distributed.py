@@ -27,10 +27,33 @@ def split_range(total: int, rank: int, world: int) -> tuple[int, int]:
     return total * rank // world, total * (rank + 1) // world
 
 
+def packed_width(q_heads: int, head_dim: int) -> int:
+    """Floats one rank publishes: its normalised output [Hq, D], then lse [Hq]."""
+    return q_heads * head_dim + q_heads
+
+
+def pack_partial(out: torch.Tensor, lse: torch.Tensor, buf: torch.Tensor | None = None):
+    """Packs (O [Hq, D] F32, lse [Hq] F32) into one [1, Hq*D + Hq] F32 row."""
+    hq, d = out.shape[-2], out.shape[-1]
+    if buf is None:
+        buf = torch.empty((1, packed_width(hq, d)), dtype=torch.float32, device=out.device)
+    buf[0, : hq * d] = out.reshape(-1)
+    buf[0, hq * d:] = lse.reshape(-1)
+    return buf
+
+
+def unpack_parts(parts: torch.Tensor, q_heads: int, head_dim: int):
+    """Views of gathered rows [n, Hq*D + Hq]: (O [n, Hq, D], lse [n, Hq])."""
+    n = parts.shape[0]
+    return (parts[:, : q_heads * head_dim].reshape(n, q_heads, head_dim),
+            parts[:, q_heads * head_dim:])
+
+
 class SequenceSplitAttention:
     def __init__(self, total_cached: int, q_heads: int, kv_heads: int, head_dim: int, *,
                  dtype=torch.float16, block_size: int = 16, max_new: int = 256,
-                 shuffle_seed: int = 0, device=None, group=None):
+                 shuffle_seed: int = 0, device=None, group=None, variant: int = 0,
+                 num_splits: int = 0):
         self.group = group
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -46,6 +69,7 @@ class SequenceSplitAttention:
         self.send = torch.zeros((1, width), dtype=torch.float32, device=self.device)
         self.recv = torch.zeros((self.world, width), dtype=torch.float32, device=self.device)
         self.global_len = total_cached
+        self.kw = {"variant": variant, "num_splits": num_splits}
 
     def fill(self, k: torch.Tensor, v: torch.Tensor) -> None:
         """Writes this rank's share: k, v [Hkv, hi-lo, D]."""
@@ -63,9 +87,11 @@ class SequenceSplitAttention:
         lse = self.send[0, self.hq * self.d:].view(1, self.hq)
         off = self.global_len - self.cache.len(0)
         if self.owner:
-            self.cache.decode(0, q, k_new, v_new, out=o, lse=lse, rope=rope, rope_pos_offset=off)
+            self.cache.decode(0, q, k_new, v_new, out=o, lse=lse, rope=rope, rope_pos_offset=off,
+                              **self.kw)
         else:
-            self.cache.decode(0, q, None, None, out=o, lse=lse, rope=rope, rope_pos_offset=off)
+            self.cache.decode(0, q, None, None, out=o, lse=lse, rope=rope, rope_pos_offset=off,
+                              **self.kw)
 
     def exchange_and_merge(self, out: torch.Tensor) -> torch.Tensor:
         if self.world > 1:
@@ -82,7 +108,8 @@ class SequenceSplitAttention:
         kernel writes ``out`` directly; there is nothing to merge."""
         if self.world == 1:
             off = self.global_len - self.cache.len(0)
-            self.cache.decode(0, q, k_new, v_new, out=out, rope=rope, rope_pos_offset=off)
+            self.cache.decode(0, q, k_new, v_new, out=out, rope=rope, rope_pos_offset=off,
+                              **self.kw)
             return out
         self.attend_local(q, k_new, v_new, rope)
         return self.exchange_and_merge(out)

@@ -153,7 +153,7 @@ class PagedKvCache:
                v_new: torch.Tensor | None, *, out: torch.Tensor | None = None,
                out_dtype: torch.dtype | None = None, lse: torch.Tensor | None = None,
                want_lse: bool = False, scale: float = 0.0, num_splits: int = 0, rope=None,
-               rope_pos_offset: int = 0):
+               rope_pos_offset: int = 0, variant: int = 0):
         """Fused append + GQA decode attention for every sequence (one query token each).
 
         q [num_seqs, Hq, D]; k_new, v_new [num_seqs, Hkv, D] or None (attend only).
@@ -179,7 +179,7 @@ class PagedKvCache:
         if lse is None and want_lse:
             lse = torch.empty((self.num_seqs, hq), dtype=torch.float32, device=self.device)
         opts = DecodeOpts(scale=scale, num_splits=num_splits, out_dtype=dtype_code(out.dtype),
-                          rope_pos_offset=rope_pos_offset)
+                          rope_pos_offset=rope_pos_offset, variant=variant)
         if rope is not None:
             cos, sin = rope
             opts.rope_cos, opts.rope_sin, opts.rope_len = cos.data_ptr(), sin.data_ptr(), cos.shape[0]

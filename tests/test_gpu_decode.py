@@ -157,10 +157,22 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("npd,hq,hkv,d,lens,bs,theta", CASES)
-def test_decode_matches_oracle(cuda, orc, npd, hq, hkv, d, lens, bs, theta):
+def variants(npd, d, hq, hkv):
+    """Kernel variants a case can run: automatic, plus both explicit kernels where the
+    tensor-core one applies (F16, D 64/128) and the CUDA-core one exists (G <= 8)."""
+    out = [0]
+    if npd == np.float16 and d in (64, 128):
+        out.append(2)
+        if hq // hkv <= 8:
+            out.append(1)
+    return out
+
+
+@pytest.mark.parametrize("npd,hq,hkv,d,lens,bs,theta,variant",
+                         [c + (v,) for c in CASES for v in variants(c[0], c[3], c[1], c[2])])
+def test_decode_matches_oracle(cuda, orc, npd, hq, hkv, d, lens, bs, theta, variant):
     case = Case(cuda, npd, hq, hkv, d, lens, block_size=bs, seed=sum(lens) + d, theta=theta)
-    got, lse = case.gpu()
+    got, lse = case.gpu(variant=variant)
     check(case, orc, got, lse)
     # the appended rows landed in their paged slots, bit-exact
     case.cache.advance(1)
@@ -172,14 +184,21 @@ def test_decode_matches_oracle(cuda, orc, npd, hq, hkv, d, lens, bs, theta):
 
 
 @pytest.mark.parametrize("splits", [1, 2, 7, 64])
-def test_split_count_does_not_change_results(cuda, orc, splits):
+@pytest.mark.parametrize("variant", [1, 2])
+def test_split_count_does_not_change_results(cuda, orc, splits, variant):
     case = Case(cuda, np.float16, 32, 8, 128, [3000, 17], seed=3)
-    got, lse = case.gpu(num_splits=splits)
+    got, lse = case.gpu(num_splits=splits, variant=variant)
     check(case, orc, got, lse)
     # repeated calls reuse the workspace tickets: identical results
     for _ in range(3):
-        again, _ = case.gpu(num_splits=splits)
+        again, _ = case.gpu(num_splits=splits, variant=variant)
         assert np.array_equal(again, got)
+
+
+def test_group_of_sixteen_on_tensor_cores(cuda, orc):
+    case = Case(cuda, np.float16, 32, 2, 64, [500, 77], seed=16)
+    got, lse = case.gpu()
+    check(case, orc, got, lse)
 
 
 def test_attend_without_append(cuda, orc):
