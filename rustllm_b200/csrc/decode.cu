@@ -438,18 +438,24 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_split_kernel(const D
 
     // merge weights w[s][g] = 2^(m_s - M_g), kept in the free ring
     float* wts = reinterpret_cast<float*>(smem);  // [splits_b][GP]
-    float* Ms = wts + static_cast<int64_t>(gridDim.x) * GP;
+    float* lsp = wts + static_cast<int64_t>(gridDim.x) * GP;  // [splits_b][GP]
+    float* Ms = lsp + static_cast<int64_t>(gridDim.x) * GP;
     float* den = Ms + GP;
+    for (int i = tid; i < splits_b * G; i += kDecodeThreads) {
+        const int s = i / G, g = i - s * G;
+        const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml) + pbase + i);
+        wts[s * GP + g] = ml.x;
+        lsp[s * GP + g] = ml.y;
+    }
+    __syncthreads();
     if (tid < G) {
         float M = -INFINITY;
-        for (int s = 0; s < splits_b; ++s)
-            M = fmaxf(M, __ldcg(&a.part_ml[(pbase + static_cast<int64_t>(s) * G + tid) * 2]));
+        for (int s = 0; s < splits_b; ++s) M = fmaxf(M, wts[s * GP + tid]);
         float dsum = 0.f;
         for (int s = 0; s < splits_b; ++s) {
-            const float* ml = a.part_ml + (pbase + static_cast<int64_t>(s) * G + tid) * 2;
-            const float w = (M == -INFINITY) ? 0.f : exp2f(__ldcg(ml) - M);
+            const float w = (M == -INFINITY) ? 0.f : exp2f(wts[s * GP + tid] - M);
             wts[s * GP + tid] = w;
-            dsum += w * __ldcg(ml + 1);
+            dsum += w * lsp[s * GP + tid];
         }
         Ms[tid] = M;
         den[tid] = dsum;
@@ -458,6 +464,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_split_kernel(const D
     for (int idx = tid; idx < G * D; idx += kDecodeThreads) {
         const int g = idx / D, d = idx - g * D;
         float num = 0.f;
+#pragma unroll 8
         for (int s = 0; s < splits_b; ++s)
             num += wts[s * GP + g] *
                    __ldcg(&a.part_o[(pbase + static_cast<int64_t>(s) * G + g) * D + d]);
@@ -506,6 +513,12 @@ __device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uin
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
+}
+// 2^x with the MUFU unit (PTX ex2.approx.ftz.f32: relative error about 2^-22; 2^-inf = 0).
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -560,7 +573,75 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_mma_kernel(const Dec
     const int half = D / 2;
     const int qpos = cached + a.rope_off;
 
-    // ---- q rows (rotated, rounded to F16) into q_s; rows >= G are zero
+    // ---- this warp's cp.async ring: sub-tiles warp, warp+4, ... of the chunk
+    unsigned char* ring = smem + warp * Cfg::WARP_RING;
+    const int nmine = nsub > warp ? (nsub - warp + 3) / 4 : 0;
+    const unsigned char* kbase = static_cast<const unsigned char*>(a.k_cache);
+    const unsigned char* vbase = static_cast<const unsigned char*>(a.v_cache);
+    const int lc = lane % C, lr0 = lane / C;
+    const bool whole_blocks = (a.block_size % 16) == 0;
+    int dst_off[Cfg::LOADS];
+#pragma unroll
+    for (int k = 0; k < Cfg::LOADS; ++k) {
+        const int r = lr0 + k * Cfg::RSTEP;
+        dst_off[k] = r * ROW + swz<C>(r, lc) * 16;
+    }
+    auto load_sub = [&](int j, int stage) {
+        unsigned char* ks = ring + stage * 2 * SUBB;
+        unsigned char* vs = ks + SUBB;
+        const int base = t0 + (warp + 4 * j) * 16;
+        int64_t row0 = -1;  // arena row of position `base` when the sub-tile is one block
+        if (whole_blocks) {
+            const int64_t blk = block_of(a, b, base);
+            if (blk >= 0)
+                row0 = (blk * a.kv_heads + kvh) * a.block_size + offset_in_block(a, base);
+        }
+        if (row0 >= 0 && base + 16 <= cached && base + 16 <= t1) {
+            // the common case: 16 cached positions inside one block
+            const int64_t off0 = row0 * ROW + lr0 * ROW + lc * 16;
+#pragma unroll
+            for (int k = 0; k < Cfg::LOADS; ++k) {
+                const int64_t off = off0 + static_cast<int64_t>(k * Cfg::RSTEP) * ROW;
+                cp_async16(ks + dst_off[k], kbase + off, 16);
+                cp_async16(vs + dst_off[k], vbase + off, 16);
+            }
+            return;
+        }
+#pragma unroll
+        for (int k = 0; k < Cfg::LOADS; ++k) {
+            const int r = lr0 + k * Cfg::RSTEP;
+            const int pos = base + r;
+            const unsigned char* ksrc = kbase;
+            const unsigned char* vsrc = vbase;
+            int bytes = 0;
+            if (pos < cached && pos < t1) {
+                int64_t arow = -1;
+                if (whole_blocks) {
+                    if (row0 >= 0) arow = row0 + r;
+                } else {
+                    const int64_t blk = block_of(a, b, pos);
+                    if (blk >= 0)
+                        arow = (blk * a.kv_heads + kvh) * a.block_size + offset_in_block(a, pos);
+                }
+                if (arow >= 0) {
+                    const int64_t off = arow * ROW + lc * 16;
+                    ksrc += off;
+                    vsrc += off;
+                    bytes = 16;
+                }
+            }
+            cp_async16(ks + dst_off[k], ksrc, bytes);
+            cp_async16(vs + dst_off[k], vsrc, bytes);
+        }
+    };
+#pragma unroll
+    for (int s = 0; s < STAGES - 1; ++s) {
+        if (s < nmine) load_sub(s, s);
+        cp_async_commit();
+    }
+
+    // ---- (while the first K/V tiles are in flight) q rows, rotated and rounded to F16,
+    // into q_s; rows >= G are zero
     for (int idx = tid; idx < 16 * half; idx += kDecodeThreads) {
         const int g = idx / half, i = idx - g * half;
         float x1 = 0.f, x2 = 0.f;
@@ -613,57 +694,6 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_mma_kernel(const Dec
         }
     }
 
-    // ---- this warp's cp.async ring: sub-tiles warp, warp+4, ... of the chunk
-    unsigned char* ring = smem + warp * Cfg::WARP_RING;
-    const int nmine = nsub > warp ? (nsub - warp + 3) / 4 : 0;
-    const unsigned char* kbase = static_cast<const unsigned char*>(a.k_cache);
-    const unsigned char* vbase = static_cast<const unsigned char*>(a.v_cache);
-    const int lc = lane % C, lr0 = lane / C;
-    const bool whole_blocks = (a.block_size % 16) == 0;
-    auto load_sub = [&](int j, int stage) {
-        unsigned char* ks = ring + stage * 2 * SUBB;
-        unsigned char* vs = ks + SUBB;
-        const int base = t0 + (warp + 4 * j) * 16;
-        int64_t row0 = -1;  // arena row of position `base` when the sub-tile is one block
-        if (whole_blocks) {
-            const int64_t blk = block_of(a, b, base);
-            if (blk >= 0)
-                row0 = (blk * a.kv_heads + kvh) * a.block_size + offset_in_block(a, base);
-        }
-#pragma unroll
-        for (int k = 0; k < Cfg::LOADS; ++k) {
-            const int r = lr0 + k * Cfg::RSTEP;
-            const int pos = base + r;
-            const unsigned char* ksrc = kbase;
-            const unsigned char* vsrc = vbase;
-            int bytes = 0;
-            if (pos < cached && pos < t1) {
-                int64_t arow = -1;
-                if (whole_blocks) {
-                    if (row0 >= 0) arow = row0 + r;
-                } else {
-                    const int64_t blk = block_of(a, b, pos);
-                    if (blk >= 0)
-                        arow = (blk * a.kv_heads + kvh) * a.block_size + offset_in_block(a, pos);
-                }
-                if (arow >= 0) {
-                    const int64_t off = arow * ROW + lc * 16;
-                    ksrc += off;
-                    vsrc += off;
-                    bytes = 16;
-                }
-            }
-            const int dst = r * ROW + swz<C>(r, lc) * 16;
-            cp_async16(ks + dst, ksrc, bytes);
-            cp_async16(vs + dst, vsrc, bytes);
-        }
-    };
-#pragma unroll
-    for (int s = 0; s < STAGES - 1; ++s) {
-        if (s < nmine) load_sub(s, s);
-        cp_async_commit();
-    }
-
     float o[NT][4];
 #pragma unroll
     for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
@@ -691,8 +721,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_mma_kernel(const Dec
             }
             __syncwarp();
         }
-        // S = Q K^T: two n-tiles of 8 positions
-        float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        // S = Q K^T: two n-tiles of 8 positions, even/odd k-steps in separate accumulators
+        float sc[2][4], sx[2][4];
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sc[n][e] = sx[n][e] = 0.f;
         {
             const int mi = lane >> 3, r = (mi >> 1) * 8 + (lane & 7);
             const uint32_t rbase = smem_u32(ks + r * ROW);
@@ -701,35 +735,39 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_mma_kernel(const Dec
                 const int c = kstep * 2 + (mi & 1);
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4(rbase + swz<C>(r, c) * 16, b0, b1, b2, b3);
-                mma16816(sc[0], qa[kstep][0], qa[kstep][1], qa[kstep][2], qa[kstep][3], b0, b1);
-                mma16816(sc[1], qa[kstep][0], qa[kstep][1], qa[kstep][2], qa[kstep][3], b2, b3);
+                float* c0 = (kstep & 1) ? sx[0] : sc[0];
+                float* c1 = (kstep & 1) ? sx[1] : sc[1];
+                mma16816(c0, qa[kstep][0], qa[kstep][1], qa[kstep][2], qa[kstep][3], b0, b1);
+                mma16816(c1, qa[kstep][0], qa[kstep][1], qa[kstep][2], qa[kstep][3], b2, b3);
             }
         }
+        const bool full = base + 16 <= t1;
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                float v = (sc[n][e] + sx[n][e]) * a.scale_log2;
+                if (!full && base + n * 8 + t4 * 2 + (e & 1) >= t1) v = -INFINITY;
+                sc[n][e] = v;
+            }
         // online softmax over the 16 positions, rows g4 and g4 + 8
         float alpha[2];
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr) {
-            float mx = -INFINITY;
-#pragma unroll
-            for (int n = 0; n < 2; ++n)
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int pos = base + n * 8 + t4 * 2 + e;
-                    float v = pos < t1 ? sc[n][rr * 2 + e] * a.scale_log2 : -INFINITY;
-                    sc[n][rr * 2 + e] = v;
-                    mx = fmaxf(mx, v);
-                }
+            float mx = fmaxf(fmaxf(sc[0][rr * 2], sc[0][rr * 2 + 1]),
+                             fmaxf(sc[1][rr * 2], sc[1][rr * 2 + 1]));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
             const float m_new = fmaxf(m_r[rr], mx);
-            alpha[rr] = (m_new == -INFINITY) ? 1.f : exp2f(m_r[rr] - m_new);
+            // rows that have seen no position yet keep m = -inf: use 0 as the reference
+            const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+            alpha[rr] = fast_exp2(m_r[rr] - m_use);
             float sum = 0.f;
 #pragma unroll
             for (int n = 0; n < 2; ++n)
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
-                    const float p =
-                        (m_new == -INFINITY) ? 0.f : exp2f(sc[n][rr * 2 + e] - m_new);
+                    const float p = fast_exp2(sc[n][rr * 2 + e] - m_use);
                     sc[n][rr * 2 + e] = p;
                     sum += p;
                 }
@@ -829,35 +867,67 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_mma_kernel(const Dec
     if (!*flag_s) return;
     __threadfence();
     float* wts = reinterpret_cast<float*>(smem);  // [splits_b][16] (red is consumed)
-    float* Ms = wts + static_cast<int64_t>(gridDim.x) * 16;
+    float* lsp = wts + static_cast<int64_t>(gridDim.x) * 16;  // [splits_b][16]
+    float* Ms = lsp + static_cast<int64_t>(gridDim.x) * 16;
     float* dens = Ms + 16;
+    // all (m, l) pairs of this (sequence, KV head) in one parallel round trip
+    for (int i = tid; i < splits_b * G; i += kDecodeThreads) {
+        const int s2 = i / G, g = i - s2 * G;
+        const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml) + pbase + i);
+        wts[s2 * 16 + g] = ml.x;
+        lsp[s2 * 16 + g] = ml.y;
+    }
+    __syncthreads();
     if (tid < G) {
         float M = -INFINITY;
-        for (int s2 = 0; s2 < splits_b; ++s2)
-            M = fmaxf(M, __ldcg(&a.part_ml[(pbase + static_cast<int64_t>(s2) * G + tid) * 2]));
+        for (int s2 = 0; s2 < splits_b; ++s2) M = fmaxf(M, wts[s2 * 16 + tid]);
         float dsum = 0.f;
         for (int s2 = 0; s2 < splits_b; ++s2) {
-            const float* ml = a.part_ml + (pbase + static_cast<int64_t>(s2) * G + tid) * 2;
-            const float w = (M == -INFINITY) ? 0.f : exp2f(__ldcg(ml) - M);
+            const float w = (M == -INFINITY) ? 0.f : exp2f(wts[s2 * 16 + tid] - M);
             wts[s2 * 16 + tid] = w;
-            dsum += w * __ldcg(ml + 1);
+            dsum += w * lsp[s2 * 16 + tid];
         }
         Ms[tid] = M;
         dens[tid] = dsum;
     }
     __syncthreads();
-    for (int idx = tid; idx < G * D; idx += kDecodeThreads) {
-        const int g = idx / D, d = idx - g * D;
-        float num = 0.f;
-        for (int s2 = 0; s2 < splits_b; ++s2)
-            num += wts[s2 * 16 + g] *
-                   __ldcg(&a.part_o[(pbase + static_cast<int64_t>(s2) * G + g) * D + d]);
+    // each thread merges 4 consecutive dims of one head.  When all partial outputs fit in
+    // the free rings they are staged there with one burst of cp.async (a single L2 round
+    // trip); otherwise they are read with one 16-byte L2 load per split.
+    const int64_t stride4 = static_cast<int64_t>(G) * D / 4;
+    const float4* src0 = reinterpret_cast<const float4*>(a.part_o + pbase * D);
+    const size_t stage_bytes = static_cast<size_t>(splits_b) * stride4 * 16;
+    const size_t stage_off = static_cast<size_t>(2 * gridDim.x * 16 + 32) * 4;
+    const bool staged = stage_off + stage_bytes <= static_cast<size_t>(4 * Cfg::WARP_RING);
+    float4* stage = reinterpret_cast<float4*>(smem + ((stage_off + 15) & ~static_cast<size_t>(15)));
+    if (staged) {
+        for (int64_t i = tid; i < splits_b * stride4; i += kDecodeThreads)
+            cp_async16(stage + i, src0 + i, 16);
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+    }
+    for (int idx = tid; idx < stride4; idx += kDecodeThreads) {
+        const int g = idx / (D / 4), d = (idx - g * (D / 4)) * 4;
+        float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+        for (int s2 = 0; s2 < splits_b; ++s2) {
+            const float w = wts[s2 * 16 + g];
+            const float4 v = staged ? stage[s2 * stride4 + idx] : __ldcg(src0 + s2 * stride4 + idx);
+            num.x += w * v.x;
+            num.y += w * v.y;
+            num.z += w * v.z;
+            num.w += w * v.w;
+        }
         const float dn = dens[g];
-        const float ov = dn > 0.f ? num / dn : 0.f;
-        if (a.out_f32)
-            static_cast<float*>(a.out)[(qh0 + g) * D + d] = ov;
-        else
-            static_cast<__half*>(a.out)[(qh0 + g) * D + d] = __float2half_rn(ov);
+        const float inv = dn > 0.f ? 1.f / dn : 0.f;
+        const float ov[4] = {num.x * inv, num.y * inv, num.z * inv, num.w * inv};
+        for (int e = 0; e < 4; ++e) {
+            if (a.out_f32)
+                static_cast<float*>(a.out)[(qh0 + g) * D + d + e] = ov[e];
+            else
+                static_cast<__half*>(a.out)[(qh0 + g) * D + d + e] = __float2half_rn(ov[e]);
+        }
         if (d == 0 && a.lse) a.lse[qh0 + g] = dn > 0.f ? (Ms[g] + log2f(dn)) * kLn2 : -INFINITY;
     }
     if (tid == 0) a.counters[static_cast<int64_t>(b) * a.kv_heads + kvh] = 0;
@@ -1033,7 +1103,7 @@ int launch_tiled(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
     using Cfg = DecodeCfg<T, D, GP, TT, STAGES>;
     auto* fn = decode_split_kernel<T, D, GP, TT, STAGES>;
     const size_t bytes = static_cast<size_t>(Cfg::BYTES);
-    const size_t need_merge = (static_cast<size_t>(grid.x) + 2) * GP * 4;
+    const size_t need_merge = (2 * static_cast<size_t>(grid.x) + 2) * GP * 4;
     if (need_merge > static_cast<size_t>(STAGES * 2 * Cfg::TILE))
         return fail(TMLLM_INVALID_ARGUMENT, "too many splits (%u) for the merge scratch", grid.x);
     TMLLM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1048,7 +1118,7 @@ int launch_mma(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
     using Cfg = MmaCfg<D, STAGES>;
     auto* fn = decode_mma_kernel<D, STAGES>;
     const size_t bytes = static_cast<size_t>(Cfg::BYTES);
-    if ((static_cast<size_t>(grid.x) + 2) * 16 * 4 > static_cast<size_t>(4 * Cfg::WARP_RING))
+    if ((2 * static_cast<size_t>(grid.x) + 2) * 16 * 4 > static_cast<size_t>(4 * Cfg::WARP_RING))
         return fail(TMLLM_INVALID_ARGUMENT, "too many splits (%u) for the merge scratch", grid.x);
     TMLLM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(bytes)));
@@ -1091,9 +1161,11 @@ int32_t auto_splits(int64_t B, int64_t Hkv, int64_t max_len) {
     const int64_t slots = static_cast<int64_t>(device_sm_count()) * 2;
     int64_t bh = B * Hkv;
     if (bh < 1) bh = 1;
-    int64_t s = (slots + bh - 1) / bh;
+    // as many splits as fit one wave of resident CTAs (a partial second wave would double
+    // the time), at least two for long sequences of a big batch so lengths balance
+    int64_t s = slots / bh;
     if (s < 2 && max_len > 1024) s = 2;
-    const int64_t by_len = (max_len + 255) / 256;
+    const int64_t by_len = (max_len + 255) / 256;  // and never chunks under 256 positions
     if (s > by_len) s = by_len;
     if (s < 1) s = 1;
     if (s > 1024) s = 1024;
