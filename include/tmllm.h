@@ -166,7 +166,7 @@ typedef struct tmllm_paged_kv {
 typedef struct tmllm_decode_opts {
     float scale;            /* logit scale; <= 0 means 1/sqrt(head_dim) (attention.rs:236) */
     int32_t num_splits;     /* sequence splits per (seq, kv head); 0 = automatic */
-    int32_t out_dtype;      /* tmllm_dtype of `out` (F32 is used for cross-GPU partials) */
+    int32_t out_f32;        /* 0: `out` has the cache dtype; 1: `out` is F32 (partials) */
     const float* rope_cos;  /* optional device RoPE tables [rope_len, head_dim/2]; when   */
     const float* rope_sin;  /* given, q and k_new are rotated at position               */
     int32_t rope_len;       /* seq_lens[s] + rope_pos_offset (attention.rs:202-207)     */
@@ -195,7 +195,7 @@ int32_t tmllm_decode_auto_splits(int32_t num_seqs, int32_t kv_heads, int64_t max
  *   q      [num_seqs, q_heads, head_dim]        (kv dtype)
  *   k_new  [num_seqs, num_kv_heads, head_dim]   appended at position seq_lens[s];
  *   v_new  [num_seqs, num_kv_heads, head_dim]   both NULL = attend the cache only
- *   out    [num_seqs, q_heads, head_dim]        (opts->out_dtype)
+ *   out    [num_seqs, q_heads, head_dim]        (cache dtype, or F32 if opts->out_f32)
  *   lse    [num_seqs, q_heads] F32, natural-log log-sum-exp of the scaled logits (NULL ok)
  * Each sequence attends keys [0, seq_lens[s] + (k_new != NULL)).  The block for the new
  * position must already be in the block table.  seq_lens is NOT advanced.

@@ -100,7 +100,7 @@ class PagedKV(C.Structure):
 class DecodeOpts(C.Structure):
     """``tmllm_decode_opts``."""
 
-    _fields_ = [("scale", C.c_float), ("num_splits", i32), ("out_dtype", i32),
+    _fields_ = [("scale", C.c_float), ("num_splits", i32), ("out_f32", i32),
                 ("rope_cos", vp), ("rope_sin", vp), ("rope_len", i32),
                 ("rope_pos_offset", i32), ("max_len_hint", i64), ("variant", i32),
                 ("reserved", i32)]

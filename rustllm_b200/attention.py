@@ -50,7 +50,9 @@ def gqa_decode(kv: PagedKV, q: torch.Tensor, k_new: torch.Tensor | None,
     [num_seqs, Hq, D] in ``out_dtype`` (default: q's dtype); lse [num_seqs, Hq] F32."""
     if out is None:
         out = torch.empty(q.shape, dtype=out_dtype or q.dtype, device=q.device)
-    opts = DecodeOpts(scale=scale, num_splits=num_splits, out_dtype=dtype_code(out.dtype),
+    if out.dtype not in (q.dtype, torch.float32) or out.shape != q.shape:
+        raise _lib.InvalidArgument("out must be [num_seqs, Hq, D] in the cache dtype or F32")
+    opts = DecodeOpts(scale=scale, num_splits=num_splits, out_f32=int(out.dtype == torch.float32),
                       rope_pos_offset=rope_pos_offset, max_len_hint=max_len_hint,
                       variant=variant)
     if rope is not None:

@@ -1218,8 +1218,8 @@ int decode_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, cons
         return fail(TMLLM_INVALID_SHAPE, "sequence capacity exceeds i32");
     tmllm_decode_opts o{};
     if (opts) o = *opts;
-    if (o.out_dtype != TMLLM_F32 && o.out_dtype != kv->dtype)
-        return fail(TMLLM_UNSUPPORTED_DTYPE, "out dtype must be F32 or the cache dtype");
+    if (o.out_f32 != 0 && o.out_f32 != 1)
+        return fail(TMLLM_INVALID_ARGUMENT, "out_f32 must be 0 or 1");
     if (o.rope_cos && (!o.rope_sin || o.rope_len <= 0))
         return fail(TMLLM_INVALID_ARGUMENT, "RoPE needs both tables and a positive length");
     const float scale = o.scale > 0.f ? o.scale : 1.0f / sqrtf(static_cast<float>(D));
@@ -1263,7 +1263,7 @@ int decode_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, cons
     a.bs_shift = bs_shift;
     a.max_blocks = kv->max_blocks_per_seq;
     a.chunk = static_cast<int32_t>(chunk);
-    a.out_f32 = o.out_dtype == TMLLM_F32;
+    a.out_f32 = o.out_f32 || kv->dtype == TMLLM_F32;
     a.scale_log2 = scale * kLog2e;
 
     const size_t es = dtype_size(kv->dtype);

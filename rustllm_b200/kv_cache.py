@@ -176,9 +176,13 @@ class PagedKvCache:
         if out is None:
             out = torch.empty((self.num_seqs, hq, self.head_dim), dtype=out_dtype or self.dtype,
                               device=self.device)
+        if out.dtype not in (self.dtype, torch.float32) or tuple(out.shape) != (
+                self.num_seqs, hq, self.head_dim) or not out.is_contiguous():
+            raise _lib.InvalidArgument("out must be a contiguous [num_seqs, Hq, D] tensor in the "
+                                       "cache dtype or F32")
         if lse is None and want_lse:
             lse = torch.empty((self.num_seqs, hq), dtype=torch.float32, device=self.device)
-        opts = DecodeOpts(scale=scale, num_splits=num_splits, out_dtype=dtype_code(out.dtype),
+        opts = DecodeOpts(scale=scale, num_splits=num_splits, out_f32=int(out.dtype == torch.float32),
                           rope_pos_offset=rope_pos_offset, variant=variant)
         if rope is not None:
             cos, sin = rope
