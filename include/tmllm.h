@@ -205,6 +205,29 @@ int tmllm_gqa_decode(const tmllm_paged_kv* kv, const void* q, const void* k_new,
                      const tmllm_decode_opts* opts, void* workspace, size_t workspace_bytes,
                      tmllm_stream stream);
 
+/* Size of the split scratch built into the library for tmllm_gqa_decode_noalloc. */
+#define TMLLM_NOALLOC_SCRATCH_BYTES (2 * 1024 * 1024)
+
+/* No counterpart in the reference (its Metal path allocates a buffer per op).
+ * tmllm_gqa_decode without a workspace argument, for callers that cannot allocate device
+ * memory at decode time: code inside a stream capture that must not add allocations,
+ * embedders whose memory comes from a pool they do not own, real-time loops that may not
+ * take allocator locks.  It calls no cudaMalloc/cudaFree and no allocating library
+ * routine; its split scratch is a TMLLM_NOALLOC_SCRATCH_BYTES (2 MiB) array compiled into
+ * the library, held on every GPU that loads the library until the process exits.
+ *  - The first call on a device (that device current) looks up the array's device address;
+ *    make it before any stream capture.
+ *  - All calls share the array and it keeps the last call's contents; the counters that
+ *    must start at zero are cleared on `stream` before each launch.  Calls that overlap on
+ *    the GPU race on it: serialise them.
+ *  - A call whose split partials exceed the array is rejected with TMLLM_INVALID_SHAPE
+ *    before anything is enqueued (config 4, 32 query heads x 128 dims x 37 splits, needs
+ *    about 0.6 MiB).
+ * Arguments and results are those of tmllm_gqa_decode. */
+int tmllm_gqa_decode_noalloc(const tmllm_paged_kv* kv, const void* q, const void* k_new,
+                             const void* v_new, void* out, float* lse, int32_t q_heads,
+                             const tmllm_decode_opts* opts, tmllm_stream stream);
+
 /* Log-sum-exp merge of partial attention results (the combine step of a sequence split
  * across GPUs).  Part p's normalised output rows are at parts_o + p*o_stride ([rows,
  * head_dim] F32) and its log-sum-exp values at parts_lse + p*lse_stride ([rows] F32);

@@ -135,6 +135,8 @@ _PROTOS = {
     "tmllm_decode_auto_splits": (i32, [i32, i32, i64]),
     "tmllm_gqa_decode": (C.c_int, [C.POINTER(PagedKV), vp, vp, vp, vp, vp, i32,
                                    C.POINTER(DecodeOpts), vp, sz, vp]),
+    "tmllm_gqa_decode_noalloc": (C.c_int, [C.POINTER(PagedKV), vp, vp, vp, vp, vp, i32,
+                                           C.POINTER(DecodeOpts), vp]),
     "tmllm_merge_lse": (C.c_int, [vp, vp, i32, i32, i32, i64, i64, vp, i32, vp, vp]),
     "tmllm_cache_create": (C.c_int, [C.POINTER(CacheConfig), C.POINTER(vp)]),
     "tmllm_cache_destroy": (C.c_int, [vp]),
