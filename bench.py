@@ -36,6 +36,10 @@ sys.path.insert(0, ROOT)
 METRIC = ("decode tok/s; fused KV-append+GQA attn HBM GB/s vs B200 peak at 1/2/4/8 GPU")
 HQ, HKV, D, CACHED, BS = 32, 8, 128, 131072, 16
 ESIZE = 2
+# DRAM bytes (read + write) of one full-size launch of decode_mma_kernel<128,3>, from the
+# ncu capture summarised in profiles/decode_mma_kernel_cfg4_32k.md (32768-position case,
+# reads scaled by the cached length, writes constant).
+NCU_TRAFFIC_PER_LAUNCH = 541.2e6
 
 
 def algorithmic_bytes(cached: int = CACHED, hq: int = HQ, hkv: int = HKV, d: int = D,
@@ -345,7 +349,10 @@ def run_ours(args) -> None:
             "gpu_launches": args.steps * (2 if world > 1 else 1),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
-                         "peak_source": peaks["source"], "traffic": args.traffic,
+                         "peak_source": peaks["source"],
+                         "traffic": (args.traffic if args.traffic is not None else
+                                     (NCU_TRAFFIC_PER_LAUNCH if world == 1 and cached == CACHED
+                                      and args.variant != 1 else None)),
                          "kernel": ("decode_split_kernel<__half,128,4,64,3>" if args.variant == 1
                                     else "decode_mma_kernel<128,3>"),
                          "kernel_ms": k_ms, "bytes_per_launch": launch_bytes},
