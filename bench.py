@@ -227,7 +227,7 @@ def run_ours(args) -> None:
     cached = args.cached
     sp = SequenceSplitAttention(cached, HQ, HKV, D, dtype=torch.float16, block_size=BS,
                                 shuffle_seed=77 + rank, device=dev, variant=args.variant,
-                                num_splits=args.splits)
+                                num_splits=args.splits, exchange=args.exchange)
     n_local = sp.hi - sp.lo
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     # fill in slabs to bound the temporary footprint
@@ -271,7 +271,7 @@ def run_ours(args) -> None:
     t_start.record(stream)
     for i in range(args.steps):
         kev[i][0].record(stream)
-        if world == 1:
+        if world == 1 or args.exchange == "p2p":
             sp.step(q, kn, vn, out)  # one launch: the fused kernel writes `out`
         else:
             sp.attend_local(q, kn, vn)
@@ -343,10 +343,12 @@ def run_ours(args) -> None:
             "config": {"workload": "cfg4 long-context decode attention op (Llama-3-8B "
                                    "attention shape), 131072 cached + 1 appended, batch 1",
                        "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "cached": CACHED,
-                       "block_size": BS, "parallelism": f"seqsplit{world}" if world > 1 else "1gpu",
+                       "block_size": BS,
+                       "parallelism": (f"seqsplit{world}-{args.exchange}" if world > 1
+                                       else "1gpu"),
                        "l2": "inputs larger than L2 (537 MB K/V per step vs 126 MB L2)"},
             "hbm_gbs": algorithmic_bytes(cached=cached) / (ms_step * 1e-3) / 1e9,
-            "gpu_launches": args.steps * (2 if world > 1 else 1),
+            "gpu_launches": args.steps * (2 if world > 1 and args.exchange == "nccl" else 1),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                          "peak_source": peaks["source"],
@@ -398,6 +400,8 @@ def main() -> None:
     ap.add_argument("--variant", type=int, default=0,
                     help="decode kernel: 0 auto (tensor-core for F16), 1 CUDA-core, 2 tensor-core")
     ap.add_argument("--splits", type=int, default=0, help="split count (0 = automatic)")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="N>1: exchange inside the decode kernel (p2p) or NCCL all-gather")
     ap.add_argument("--cached", type=int, default=CACHED,
                     help="cached positions (smaller values only for profiling captures)")
     ap.add_argument("--traffic", type=float, default=None,

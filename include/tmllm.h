@@ -238,6 +238,48 @@ int tmllm_merge_lse(const float* parts_o, const float* parts_lse, int32_t num_pa
                     void* out, int32_t out_dtype, float* out_lse, tmllm_stream stream);
 
 /* ---------------------------------------------------------------------------------- */
+/* Sequence split across GPUs, exchanged inside the decode kernel                      */
+/* ---------------------------------------------------------------------------------- */
+
+/* New (the reference is single-device).  One sequence split along its positions across
+ * `world` GPUs (BASELINE config 4's multi-GPU form): each rank holds a contiguous share of
+ * the positions in its own paged cache.  Instead of a separate collective, the decode
+ * kernel's final CTA of each (sequence, KV head) stores its normalised rows and their
+ * log-sum-exp into every other rank's receive buffer over NVLink as {value, step} 8-byte
+ * cells, reads the other ranks' rows from its own buffer as their cells reach this step
+ * (waiting at most 2 s by default), and merges them into `out`: every rank ends with the
+ * full result.  Ranks must issue the same sequence of
+ * tmllm_gqa_decode_exchange calls.  An expired wait writes zeros and sets the status that
+ * tmllm_exchange_status returns (TMLLM_TIMEOUT). */
+#define TMLLM_IPC_HANDLE_BYTES 64
+typedef struct tmllm_exchange tmllm_exchange;
+
+/* Allocates this rank's buffer on the current device for `rows` = num_seqs * q_heads
+ * output rows in `groups` = num_seqs * num_kv_heads groups, and writes its CUDA IPC handle
+ * (TMLLM_IPC_HANDLE_BYTES bytes) to ipc_handle_out (may be NULL). */
+int tmllm_exchange_create(int32_t world, int32_t rank, int32_t rows, int32_t groups,
+                          int32_t head_dim, tmllm_exchange** out, void* ipc_handle_out);
+/* Maps every other rank's buffer from the gathered handles ([world][64] bytes, rank order;
+ * this rank's own entry is ignored).  One process per GPU. */
+int tmllm_exchange_connect(tmllm_exchange* ex, const void* handles);
+/* The same for exchanges created in this process (one process driving several GPUs, or
+ * ranks emulated on one GPU): ranks[p] is rank p's exchange. */
+int tmllm_exchange_connect_local(tmllm_exchange* ex, tmllm_exchange* const* ranks);
+/* Bound of the in-kernel wait for the other ranks, in nanoseconds of %globaltimer. */
+int tmllm_exchange_set_timeout(tmllm_exchange* ex, uint64_t timeout_ns);
+/* Reads (synchronously) and clears this rank's status: 0, or TMLLM_TIMEOUT if a wait expired. */
+int tmllm_exchange_status(tmllm_exchange* ex, int32_t* status);
+int tmllm_exchange_destroy(tmllm_exchange* ex);
+/* tmllm_gqa_decode over this rank's share, finished by the exchange and merge: `out` and
+ * `lse` receive the result over all ranks' positions.  F16 caches with head_dim 64 or 128.
+ * k_new/v_new: the new token on the rank that holds the sequence's tail, NULL elsewhere;
+ * RoPE positions come from opts->rope_pos_offset (global position minus local length). */
+int tmllm_gqa_decode_exchange(const tmllm_paged_kv* kv, const void* q, const void* k_new,
+                              const void* v_new, void* out, float* lse, int32_t q_heads,
+                              const tmllm_decode_opts* opts, void* workspace,
+                              size_t workspace_bytes, tmllm_exchange* ex, tmllm_stream stream);
+
+/* ---------------------------------------------------------------------------------- */
 /* Paged KV cache runtime                                                              */
 /* ---------------------------------------------------------------------------------- */
 

@@ -138,6 +138,14 @@ _PROTOS = {
     "tmllm_gqa_decode_noalloc": (C.c_int, [C.POINTER(PagedKV), vp, vp, vp, vp, vp, i32,
                                            C.POINTER(DecodeOpts), vp]),
     "tmllm_merge_lse": (C.c_int, [vp, vp, i32, i32, i32, i64, i64, vp, i32, vp, vp]),
+    "tmllm_exchange_create": (C.c_int, [i32, i32, i32, i32, i32, C.POINTER(vp), vp]),
+    "tmllm_exchange_connect": (C.c_int, [vp, vp]),
+    "tmllm_exchange_connect_local": (C.c_int, [vp, C.POINTER(vp)]),
+    "tmllm_exchange_set_timeout": (C.c_int, [vp, C.c_uint64]),
+    "tmllm_exchange_status": (C.c_int, [vp, C.POINTER(i32)]),
+    "tmllm_exchange_destroy": (C.c_int, [vp]),
+    "tmllm_gqa_decode_exchange": (C.c_int, [C.POINTER(PagedKV), vp, vp, vp, vp, vp, i32,
+                                            C.POINTER(DecodeOpts), vp, sz, vp, vp]),
     "tmllm_cache_create": (C.c_int, [C.POINTER(CacheConfig), C.POINTER(vp)]),
     "tmllm_cache_destroy": (C.c_int, [vp]),
     "tmllm_cache_len": (C.c_int, [vp, i32, C.POINTER(i64)]),

@@ -39,6 +39,22 @@ int device_sm_count();
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Cross-GPU exchange of a sequence split (device-resident; see exchange.cu).  Every rank
+// owns one buffer of 8-byte cells {F32 value bits, step number}:
+//   recv_o   [2 parities][world][rows][head_dim]   normalised partial outputs
+//   recv_lse [2 parities][world][rows]             their natural-log log-sum-exp
+// plus a status word (TMLLM_TIMEOUT after an expired wait), and holds device pointers to
+// every rank's buffer.  A cell is written with one 8-byte store, so a reader that sees the
+// current step number in a cell also sees its value: no fences or flags are needed.
+constexpr int kMaxRanks = 8;
+struct ExchangeArgs {
+    uint2* recv_o[kMaxRanks];
+    uint2* recv_lse[kMaxRanks];
+    int* status;
+    unsigned long long timeout_ns;
+    int32_t rank, world, rows, groups, head_dim, pad;
+};
+
 }  // namespace tmllm
 
 #define TMLLM_CUDA_TRY(expr)                                          \

@@ -49,6 +49,8 @@ struct DecodeArgs {
     int32_t q_heads, kv_heads, group, block_size, bs_shift, max_blocks, chunk;
     int32_t rope_len, rope_off, out_f32;
     float scale_log2;
+    const ExchangeArgs* ex;  // cross-GPU split exchange, or null
+    uint32_t epoch;          // exchange step number (1, 2, ...)
 };
 
 // Physical slot of 16-byte chunk `c` of tile row `r` (XOR swizzle inside groups of 8).
@@ -524,6 +526,105 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void st_cell(uint2* p, float v, unsigned step) {
+    asm volatile("st.relaxed.sys.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)),
+                 "r"(step)
+                 : "memory");
+}
+__device__ __forceinline__ uint2 ld_cell(const uint2* p) {
+    uint2 v;
+    asm volatile("ld.relaxed.sys.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p)
+                 : "memory");
+    return v;
+}
+
+// Reads cell `p` once it carries `step`; gives up (and returns false) once `deadline`
+// of %globaltimer has passed.
+__device__ __forceinline__ bool wait_cell(const uint2* p, unsigned step,
+                                          unsigned long long deadline, float* out) {
+    for (int spin = 0;; ++spin) {
+        const uint2 c = ld_cell(p);
+        if (c.y == step) {
+            *out = __uint_as_float(c.x);
+            return true;
+        }
+        if ((spin & 15) == 15) {
+            if (global_ns() > deadline) return false;
+            __nanosleep(32);
+        }
+    }
+}
+
+// Final step of a sequence split across GPUs, run by the CTA that holds the final
+// (O, lse) of one (sequence, KV head) group on this rank (G rows from `row0`, staged in
+// shared memory `fin`/`flse`): store the rows into every other rank's receive buffer over
+// NVLink as {value, step} cells, then read the other ranks' rows of this group from this
+// rank's buffer as their cells turn to this step (waiting at most ex->timeout_ns), and
+// merge everything by log-sum-exp into `out`/`lse`.  Slots alternate by step parity, so a
+// rank one step ahead never overwrites cells another rank is still reading.
+template <typename T>
+__device__ void exchange_tail(const DecodeArgs& a, const float* fin, const float* flse, int G,
+                              int D, int64_t row0, int* flag_s) {
+    const ExchangeArgs* ex = a.ex;
+    const int tid = threadIdx.x, world = ex->world, rank = ex->rank;
+    const int64_t rows = ex->rows;
+    const unsigned step = a.epoch;
+    const int64_t par = static_cast<int64_t>(step & 1u) * world;
+    const int64_t mine = (par + rank) * rows + row0;
+    for (int p = 0; p < world; ++p) {
+        if (p == rank) continue;
+        uint2* dst = ex->recv_o[p] + mine * D;
+        for (int i = tid; i < G * D; i += kDecodeThreads) st_cell(dst + i, fin[i], step);
+        if (tid < G) st_cell(ex->recv_lse[p] + mine + tid, flse[tid], step);
+    }
+    if (tid == 0) *flag_s = 0;
+    __syncthreads();
+    const unsigned long long deadline = global_ns() + ex->timeout_ns;
+    bool ok = true;
+    for (int idx = tid; idx < G * D; idx += kDecodeThreads) {
+        const int g = idx / D;
+        const int64_t row = row0 + g;
+        float M = flse[g];
+        float lp[kMaxRanks];
+        for (int p = 0; p < world; ++p) {
+            if (p == rank) {
+                lp[p] = flse[g];
+                continue;
+            }
+            float v = -INFINITY;
+            if (ok) ok = wait_cell(ex->recv_lse[rank] + (par + p) * rows + row, step, deadline, &v);
+            lp[p] = v;
+            M = fmaxf(M, v);
+        }
+        float num = 0.f, den = 0.f;
+        for (int p = 0; p < world; ++p) {
+            const float w = (M == -INFINITY) ? 0.f : __expf(lp[p] - M);
+            float o = fin[idx];
+            if (p != rank && ok)
+                ok = wait_cell(ex->recv_o[rank] + ((par + p) * rows + row0) * D + idx, step,
+                               deadline, &o);
+            num += w * o;
+            den += w;
+        }
+        const float ov = (!ok || !(den > 0.f)) ? 0.f : num / den;
+        if (a.out_f32)
+            static_cast<float*>(a.out)[row * D + (idx - g * D)] = ov;
+        else
+            static_cast<T*>(a.out)[row * D + (idx - g * D)] = from_f32<T>(ov);
+        if (idx - g * D == 0 && a.lse)
+            a.lse[row] = (!ok || !(den > 0.f)) ? -INFINITY : M + logf(den);
+    }
+    if (!ok) {
+        atomicExch(ex->status, TMLLM_TIMEOUT);
+        *flag_s = 1;
+    }
+}
+
 template <int D, int STAGES>
 struct MmaCfg {
     static constexpr int C = D / 8;         // 16-byte chunks per row
@@ -536,10 +637,12 @@ struct MmaCfg {
     static constexpr int OFF_ST = OFF_Q + 16 * QROW * 2;  // m, l per warp x row + flag
     static constexpr int OFF_NEW = OFF_ST + (2 * 4 * 16 + 16) * 4;
     static constexpr int BYTES = OFF_NEW + 2 * ROW;
+    // exchange staging (final rows of a group) at the end of the rings: [16][D] + [16] F32
+    static constexpr int OFF_FIN = 4 * WARP_RING - (16 * D + 16) * 4;
     static constexpr int LOADS = SUB * C / 32;  // 16-byte copies per lane per K sub-tile
     static constexpr int RSTEP = 32 / C;
     static_assert(C == 8 || C == 16, "D must be 64 or 128");
-    static_assert(4 * WARP_RING >= 4 * 16 * D * 4, "warp-merge scratch fits in the rings");
+    static_assert(OFF_FIN >= 4 * 16 * D * 4, "warp-merge scratch and staging fit in the rings");
 };
 
 template <int D, int STAGES>
@@ -555,6 +658,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_mma_kernel(const Dec
     int* flag_s = reinterpret_cast<int*>(wl + 64);
     __half* knew_s = reinterpret_cast<__half*>(smem + Cfg::OFF_NEW);
     __half* vnew_s = knew_s + D;
+    float* fin = reinterpret_cast<float*>(smem + Cfg::OFF_FIN);  // [16][D] exchange staging
+    float* flse = fin + 16 * D;                                  // [16]
 
     const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -843,11 +948,17 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_mma_kernel(const Dec
         }
         if (splits_b == 1) {
             const float ov = den > 0.f ? num / den : 0.f;
-            if (a.out_f32)
-                static_cast<float*>(a.out)[(qh0 + g) * D + d] = ov;
-            else
-                static_cast<__half*>(a.out)[(qh0 + g) * D + d] = __float2half_rn(ov);
-            if (d == 0 && a.lse) a.lse[qh0 + g] = den > 0.f ? (M + log2f(den)) * kLn2 : -INFINITY;
+            const float lv = den > 0.f ? (M + log2f(den)) * kLn2 : -INFINITY;
+            if (a.ex) {
+                fin[g * D + d] = ov;
+                if (d == 0) flse[g] = lv;
+            } else {
+                if (a.out_f32)
+                    static_cast<float*>(a.out)[(qh0 + g) * D + d] = ov;
+                else
+                    static_cast<__half*>(a.out)[(qh0 + g) * D + d] = __float2half_rn(ov);
+                if (d == 0 && a.lse) a.lse[qh0 + g] = lv;
+            }
         } else {
             a.part_o[(pbase + static_cast<int64_t>(split) * G + g) * D + d] = num;
             if (d == 0) {
@@ -856,7 +967,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_mma_kernel(const Dec
             }
         }
     }
-    if (splits_b == 1) return;
+    if (splits_b == 1) {
+        if (a.ex) {
+            __syncthreads();
+            exchange_tail<__half>(a, fin, flse, G, D, qh0, flag_s);
+        }
+        return;
+    }
     __threadfence();
     __syncthreads();
     if (tid == 0) {
@@ -898,7 +1015,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_mma_kernel(const Dec
     const float4* src0 = reinterpret_cast<const float4*>(a.part_o + pbase * D);
     const size_t stage_bytes = static_cast<size_t>(splits_b) * stride4 * 16;
     const size_t stage_off = static_cast<size_t>(2 * gridDim.x * 16 + 32) * 4;
-    const bool staged = stage_off + stage_bytes <= static_cast<size_t>(4 * Cfg::WARP_RING);
+    const bool staged = stage_off + stage_bytes <= static_cast<size_t>(Cfg::OFF_FIN);
     float4* stage = reinterpret_cast<float4*>(smem + ((stage_off + 15) & ~static_cast<size_t>(15)));
     if (staged) {
         for (int64_t i = tid; i < splits_b * stride4; i += kDecodeThreads)
@@ -922,15 +1039,25 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_mma_kernel(const Dec
         const float dn = dens[g];
         const float inv = dn > 0.f ? 1.f / dn : 0.f;
         const float ov[4] = {num.x * inv, num.y * inv, num.z * inv, num.w * inv};
+        const float lv = dn > 0.f ? (Ms[g] + log2f(dn)) * kLn2 : -INFINITY;
+        if (a.ex) {
+            for (int e = 0; e < 4; ++e) fin[g * D + d + e] = ov[e];
+            if (d == 0) flse[g] = lv;
+            continue;
+        }
         for (int e = 0; e < 4; ++e) {
             if (a.out_f32)
                 static_cast<float*>(a.out)[(qh0 + g) * D + d + e] = ov[e];
             else
                 static_cast<__half*>(a.out)[(qh0 + g) * D + d + e] = __float2half_rn(ov[e]);
         }
-        if (d == 0 && a.lse) a.lse[qh0 + g] = dn > 0.f ? (Ms[g] + log2f(dn)) * kLn2 : -INFINITY;
+        if (d == 0 && a.lse) a.lse[qh0 + g] = lv;
     }
     if (tid == 0) a.counters[static_cast<int64_t>(b) * a.kv_heads + kvh] = 0;
+    if (a.ex) {
+        __syncthreads();
+        exchange_tail<__half>(a, fin, flse, G, D, qh0, flag_s);
+    }
 }
 
 // Any even head_dim: one CTA per (seq, query head), tiles of 128 positions, one thread per
@@ -1118,7 +1245,7 @@ int launch_mma(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
     using Cfg = MmaCfg<D, STAGES>;
     auto* fn = decode_mma_kernel<D, STAGES>;
     const size_t bytes = static_cast<size_t>(Cfg::BYTES);
-    if ((2 * static_cast<size_t>(grid.x) + 2) * 16 * 4 > static_cast<size_t>(4 * Cfg::WARP_RING))
+    if ((2 * static_cast<size_t>(grid.x) + 2) * 16 * 4 > static_cast<size_t>(Cfg::OFF_FIN))
         return fail(TMLLM_INVALID_ARGUMENT, "too many splits (%u) for the merge scratch", grid.x);
     TMLLM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(bytes)));
@@ -1184,10 +1311,27 @@ int32_t auto_splits_bound(int64_t B, int64_t Hkv) {
 
 }  // namespace
 
+int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
+                   const void* v_new, void* out, float* lse, int32_t q_heads,
+                   const tmllm_decode_opts* opts, void* workspace, size_t workspace_bytes,
+                   int64_t max_len_hint, const ExchangeArgs* ex, uint32_t epoch,
+                   cudaStream_t stream);
+
 int decode_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, const void* v_new,
                 void* out, float* lse, int32_t q_heads, const tmllm_decode_opts* opts,
                 void* workspace, size_t workspace_bytes, int64_t max_len_hint,
                 cudaStream_t stream) {
+    return decode_impl_ex(kv, q, k_new, v_new, out, lse, q_heads, opts, workspace,
+                          workspace_bytes, max_len_hint, nullptr, 0, stream);
+}
+
+// `ex` (device-resident) makes the launch finish a sequence split across GPUs: the final
+// rows are exchanged with every rank and merged (tensor-core kernel only).
+int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
+                   const void* v_new, void* out, float* lse, int32_t q_heads,
+                   const tmllm_decode_opts* opts, void* workspace, size_t workspace_bytes,
+                   int64_t max_len_hint, const ExchangeArgs* ex, uint32_t epoch,
+                   cudaStream_t stream) {
     if (!kv) return fail(TMLLM_INVALID_ARGUMENT, "null paged KV descriptor");
     if (!valid_dtype(kv->dtype)) return fail(TMLLM_UNSUPPORTED_DTYPE, "unknown cache dtype");
     const int D = kv->head_dim, Hkv = kv->num_kv_heads, B = kv->num_seqs;
@@ -1265,6 +1409,11 @@ int decode_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, cons
     a.chunk = static_cast<int32_t>(chunk);
     a.out_f32 = o.out_f32 || kv->dtype == TMLLM_F32;
     a.scale_log2 = scale * kLog2e;
+    a.ex = ex;
+    a.epoch = epoch;
+    if (ex && !(mma_shape && o.variant != 1))
+        return fail(TMLLM_INVALID_ARGUMENT,
+                    "the cross-GPU exchange needs the tensor-core decode (F16, head_dim 64/128)");
 
     const size_t es = dtype_size(kv->dtype);
     auto misaligned = [es](const void* p) {
@@ -1296,6 +1445,9 @@ int decode_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, cons
         int st = launch_decode(kv->dtype, D, o.variant, a, grid, stream, &done);
         if (done) return st;
     }
+    if (ex)
+        return fail(TMLLM_INVALID_ARGUMENT,
+                    "the cross-GPU exchange needs 16-byte aligned K/V arenas");
     // generic path: one CTA per (query head, sequence), no splits
     const size_t smem = (3 * static_cast<size_t>(D) + 128 + 4) * sizeof(float);
     dim3 grid(static_cast<unsigned>(q_heads), static_cast<unsigned>(B));

@@ -7,14 +7,76 @@
   rank merges by log-sum-exp (``tmllm_merge_lse``).
 * ``shard_sequences`` — batch sharding (config 3): sequence s goes to rank s mod N; the
   ranks never exchange data.
+
+The default exchange (``exchange="p2p"``) happens inside the decode kernel: each rank's
+final CTAs write their rows into every rank's buffer over NVLink (CUDA IPC mappings from
+``PeerExchange``) and merge what arrives, so a step is one launch per rank.  ``"nccl"``
+keeps the all-gather + merge-kernel form for comparison.
 """
 from __future__ import annotations
+
+import ctypes as C
 
 import torch
 import torch.distributed as dist
 
-from .attention import merge_packed
+from . import _lib
+from ._lib import DecodeOpts, call
+from .attention import DecodeWorkspace, merge_packed
 from .kv_cache import PagedKvCache
+from .tensor_ops import stream_ptr
+
+HANDLE_BYTES = 64
+
+
+class PeerExchange:
+    """This rank's ``tmllm_exchange``: a receive buffer shared with every rank by CUDA IPC.
+    ``rows`` = num_seqs * q_heads, ``groups`` = num_seqs * kv_heads."""
+
+    def __init__(self, rows: int, groups: int, head_dim: int, *, device=None, group=None,
+                 timeout_s: float = 2.0):
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.device = torch.device(device or "cuda")
+        self._h = None
+        handle = (C.c_uint8 * HANDLE_BYTES)()
+        h = C.c_void_p()
+        with torch.cuda.device(self.device):
+            call("tmllm_exchange_create", self.world, self.rank, rows, groups, head_dim,
+                 C.byref(h), handle)
+        self._h = h
+        mine = bytes(handle)
+        handles = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(handles, mine, group=group)
+        else:
+            handles = [mine]
+        buf = (C.c_uint8 * (HANDLE_BYTES * self.world)).from_buffer_copy(b"".join(handles))
+        with torch.cuda.device(self.device):
+            call("tmllm_exchange_connect", self._h, buf)
+            call("tmllm_exchange_set_timeout", self._h, int(timeout_s * 1e9))
+
+    @property
+    def handle(self):
+        return self._h
+
+    def status(self) -> int:
+        st = C.c_int32()
+        with torch.cuda.device(self.device):
+            call("tmllm_exchange_status", self._h, C.byref(st))
+        return st.value
+
+    def close(self) -> None:
+        if self._h is not None:
+            with torch.cuda.device(self.device):
+                _lib.load().tmllm_exchange_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def shard_sequences(num_seqs: int, rank: int, world: int) -> list[int]:
@@ -53,7 +115,7 @@ class SequenceSplitAttention:
     def __init__(self, total_cached: int, q_heads: int, kv_heads: int, head_dim: int, *,
                  dtype=torch.float16, block_size: int = 16, max_new: int = 256,
                  shuffle_seed: int = 0, device=None, group=None, variant: int = 0,
-                 num_splits: int = 0):
+                 num_splits: int = 0, exchange: str = "p2p"):
         self.group = group
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -70,6 +132,13 @@ class SequenceSplitAttention:
         self.recv = torch.zeros((self.world, width), dtype=torch.float32, device=self.device)
         self.global_len = total_cached
         self.kw = {"variant": variant, "num_splits": num_splits}
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError(f"unknown exchange {exchange!r}")
+        self.exchange = exchange if self.world > 1 else "none"
+        self.peer = None
+        if self.exchange == "p2p":
+            self.peer = PeerExchange(q_heads, kv_heads, head_dim, device=self.device, group=group)
+            self.ws = DecodeWorkspace(1, q_heads, kv_heads, head_dim, device=self.device)
 
     def fill(self, k: torch.Tensor, v: torch.Tensor) -> None:
         """Writes this rank's share: k, v [Hkv, hi-lo, D]."""
@@ -101,11 +170,33 @@ class SequenceSplitAttention:
             parts = self.send
         return merge_packed(parts, self.hq, self.d, out=out.view(self.hq, self.d))
 
+    def step_p2p(self, q: torch.Tensor, k_new: torch.Tensor | None,
+                 v_new: torch.Tensor | None, out: torch.Tensor, rope=None) -> torch.Tensor:
+        """One decode token with the exchange inside the kernel: one launch per rank."""
+        if self.owner:
+            self.cache.reserve(0, 1)
+        kv = self.cache.view(0)
+        opts = DecodeOpts(num_splits=self.kw["num_splits"], variant=self.kw["variant"],
+                          out_f32=int(out.dtype == torch.float32),
+                          rope_pos_offset=self.global_len - self.cache.len(0),
+                          max_len_hint=self.cache.len(0) + 1)
+        if rope is not None:
+            cos, sin = rope
+            opts.rope_cos, opts.rope_sin, opts.rope_len = cos.data_ptr(), sin.data_ptr(), cos.shape[0]
+        own = self.owner
+        call("tmllm_gqa_decode_exchange", C.byref(kv), q.data_ptr(),
+             k_new.data_ptr() if own else None, v_new.data_ptr() if own else None,
+             out.data_ptr(), None, self.hq, C.byref(opts), self.ws.ptr, self.ws.nbytes,
+             self.peer.handle, stream_ptr(self.device))
+        return out
+
     def step(self, q: torch.Tensor, k_new: torch.Tensor | None, v_new: torch.Tensor | None,
              out: torch.Tensor, rope=None) -> torch.Tensor:
         """One decode token: q [1, Hq, D]; k_new, v_new [1, Hkv, D] (used by the owner);
         out [1, Hq, D].  Lengths are not advanced (see ``advance``).  On one GPU the fused
         kernel writes ``out`` directly; there is nothing to merge."""
+        if self.exchange == "p2p":
+            return self.step_p2p(q, k_new, v_new, out, rope)
         if self.world == 1:
             off = self.global_len - self.cache.len(0)
             self.cache.decode(0, q, k_new, v_new, out=out, rope=rope, rope_pos_offset=off,
