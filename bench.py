@@ -388,6 +388,119 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------------------------------------
+# Decoder workloads (3 and 5): decode tok/s of the whole model
+# ------------------------------------------------------------------------------------
+
+DECODER_WORKLOADS = {
+    # name: (preset, sequences, prompt/context, decode tokens, description)
+    "cfg2": ("smollm2-135m", 1, 32, 256,
+             "cfg2 SmolLM2-135M decoder, batch 1, 32-token prompt then 256 greedy tokens"),
+    "cfg3": ("smollm2-360m", 64, None, 128,
+             "cfg3 SmolLM2-360M batched paged decode, 64 sequences with contexts U[256,2048], "
+             "128 tokens each"),
+    "cfg5": ("tinystories-110m", 16, 512, 64,
+             "cfg5 TinyStories-110M, 16 prompts x 512 tokens then 64 decode tokens each"),
+}
+
+
+def run_decoder(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from rustllm_b200.decoder import PRESETS, Decoder, DecoderWeights, GraphedDecoder
+    from rustllm_b200.distributed import shard_sequences
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    preset, total_seqs, prompt, steps, desc = DECODER_WORKLOADS[args.workload]
+    cfg = PRESETS[preset]
+    gen = torch.Generator().manual_seed(1234)
+    if args.workload == "cfg3":
+        ctx = torch.randint(256, 2049, (total_seqs,), generator=gen).tolist()
+        mine = shard_sequences(total_seqs, rank, world)  # batch sharding, no collective
+        scaling = "strong"
+    else:
+        ctx = [prompt] * total_seqs
+        mine = list(range(total_seqs))  # replicas: every GPU runs its own copy
+        scaling = "weak"
+    B = len(mine)
+    need = max(ctx[s] for s in mine) + args.warmup + steps + 2
+    w = DecoderWeights(cfg, device=dev, seed=7)
+    dec = Decoder(cfg, w, B, device=dev, shuffle_seed=11 + rank, max_seq_len=need)
+    if args.workload == "cfg3":
+        # synthetic contexts: N(0,1) K/V written straight into every layer's paged cache
+        g = torch.Generator(device=dev).manual_seed(100 + rank)
+        for i, s in enumerate(mine):
+            for layer in range(cfg.num_layers):
+                k = torch.randn((cfg.num_kv_heads, ctx[s], cfg.head_dim), generator=g,
+                                device=dev).half()
+                dec.cache.append(layer, i, k, k)
+            dec.cache.advance(ctx[s], i)
+        first = torch.randint(0, cfg.vocab_size, (B,), generator=gen).to(dev, torch.int32)
+    else:
+        prompts = torch.randint(0, cfg.vocab_size, (B, prompt), generator=gen).to(dev)
+        first = dec.prefill(prompts)
+    dec.ids.copy_(first)
+    runner = GraphedDecoder(dec, args.warmup + steps)
+    for _ in range(args.warmup):
+        runner.step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    kv_before = sum(dec.cache.lens())
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall0 = time.time()
+    e0.record()
+    for _ in range(steps):
+        runner.step()
+    e1.record()
+    torch.cuda.synchronize()
+    wall1 = time.time()
+    ms = e0.elapsed_time(e1)
+    clocks = sampler.stop(wall0, wall1) if sampler else None
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0])
+    tokens = (total_seqs if args.workload == "cfg3" else B * world) * steps
+    tok_s = tokens / (ms * 1e-3)
+    # step bytes on this rank: every weight once + the K/V each sequence reads
+    e = 2
+    mean_len = kv_before / max(B, 1) + steps / 2
+    kv_bytes = B * cfg.num_layers * 2 * cfg.num_kv_heads * cfg.head_dim * e * mean_len
+    step_bytes = cfg.weight_params() * e + kv_bytes
+    achieved = step_bytes / (ms * 1e-3 / steps) / 1e9
+    if rank == 0:
+        peaks = load_peaks()
+        line = {
+            "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": ms / steps, "higher_is_better": True,
+            "scaling": scaling, "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (random-init weights N(0,0.02), random token ids, seeded)",
+            "config": {"workload": desc, "preset": preset, "sequences": total_seqs,
+                       "parallelism": (f"batch-shard{world}" if args.workload == "cfg3"
+                                       else f"replicas{world}") if world > 1 else "1gpu",
+                       "graph": "one CUDA graph per decode step"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                         "peak_source": peaks["source"], "traffic": None,
+                         "scope": "whole decode step on rank 0: weights + K/V read per step"},
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -397,6 +510,8 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--ref-budget", type=float, default=60.0)
+    ap.add_argument("--workload", choices=["cfg4", "cfg2", "cfg3", "cfg5"], default="cfg4",
+                    help="cfg4 (default): the fused attention op; cfg2/3/5: whole-model decode")
     ap.add_argument("--variant", type=int, default=0,
                     help="decode kernel: 0 auto (tensor-core for F16), 1 CUDA-core, 2 tensor-core")
     ap.add_argument("--splits", type=int, default=0, help="split count (0 = automatic)")
@@ -411,6 +526,8 @@ def main() -> None:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload != "cfg4":
+        run_decoder(args)
     else:
         run_ours(args)
 

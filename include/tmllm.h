@@ -138,6 +138,37 @@ int tmllm_rope(tmllm_dtype dtype, const void* in, void* out, const float* cos_ta
                size_t head_dim, size_t start_pos, tmllm_stream stream);
 
 /* ---------------------------------------------------------------------------------- */
+/* Decoder layers around the attention path                                            */
+/* ---------------------------------------------------------------------------------- */
+
+/* Replaces Embedding::forward_encode (src/ops/embedding.rs, kernels/embedding.metal:39-53):
+ * out [n, hidden] = table [vocab, hidden][ids].  A device id outside [0, vocab) yields a
+ * zero row and sets *bad_id_flag (device int, may be NULL); the reference rejects such
+ * ids on the host (TinyError::InvalidTokenId). */
+int tmllm_embedding(tmllm_dtype dtype, const void* table, const int32_t* ids, void* out,
+                    size_t n, size_t hidden, size_t vocab, int32_t* bad_id_flag,
+                    tmllm_stream stream);
+
+/* Replaces the residual add (Tensor::add_encode, kernels/vector_add.metal:15-21) and
+ * RmsNorm::forward_encode (src/nn/rmsnorm.rs, kernels/rmsnorm.metal:71-126) that follow
+ * each other in TransformerBlock (src/nn/transformer_block.rs:137-158):
+ * s = x + residual (storage-rounded; residual may be NULL: s = x), written to sum_out
+ * (may be NULL), and out = s * rsqrt(mean(s^2) + eps) * weight, per row of `hidden`. */
+int tmllm_add_rmsnorm(tmllm_dtype dtype, const void* x, const void* residual, const void* weight,
+                      void* out, void* sum_out, size_t rows, size_t hidden, float eps,
+                      tmllm_stream stream);
+
+/* Replaces SwiGlu (kernels/silu.metal:38-46) on a fused projection: gate_up [rows,
+ * 2*inter] holds gate then up; out [rows, inter] = silu(gate) * up. */
+int tmllm_swiglu(tmllm_dtype dtype, const void* gate_up, void* out, size_t rows, size_t inter,
+                 tmllm_stream stream);
+
+/* Replaces greedy sampling (src/generation/sampler.rs:79-88, on the CPU in the reference):
+ * ids[r] = index of the largest of logits [rows, vocab] row r; the last of equal maxima. */
+int tmllm_argmax(tmllm_dtype dtype, const void* logits, int32_t* ids, size_t rows, size_t vocab,
+                 tmllm_stream stream);
+
+/* ---------------------------------------------------------------------------------- */
 /* Fused paged decode attention (the hot path)                                         */
 /* ---------------------------------------------------------------------------------- */
 
@@ -176,6 +207,9 @@ typedef struct tmllm_decode_opts {
     int32_t variant;        /* 0 = automatic; 1 = CUDA-core FMA kernel; 2 = tensor-core */
                             /* (mma.sync) kernel, F16 with head_dim 64 or 128 only     */
     int32_t reserved;
+    int64_t q_seq_stride;   /* elements between sequences in q (0 = q_heads*head_dim),  */
+    int64_t kv_seq_stride;  /* and in k_new/v_new (0 = num_kv_heads*head_dim): lets the */
+                            /* outputs of one fused QKV projection be read in place.    */
 } tmllm_decode_opts;
 
 /* Bytes of scratch tmllm_gqa_decode needs for `num_splits` splits (0 = enough for any

@@ -103,7 +103,7 @@ class DecodeOpts(C.Structure):
     _fields_ = [("scale", C.c_float), ("num_splits", i32), ("out_f32", i32),
                 ("rope_cos", vp), ("rope_sin", vp), ("rope_len", i32),
                 ("rope_pos_offset", i32), ("max_len_hint", i64), ("variant", i32),
-                ("reserved", i32)]
+                ("reserved", i32), ("q_seq_stride", i64), ("kv_seq_stride", i64)]
 
 
 class CacheConfig(C.Structure):
@@ -130,6 +130,10 @@ _PROTOS = {
     "tmllm_batched_matmul": (C.c_int, [C.c_int, vp, vp, vp, sz, sz, sz, sz, vp]),
     "tmllm_rope_tables": (C.c_int, [vp, vp, sz, sz, C.c_float]),
     "tmllm_rope": (C.c_int, [C.c_int, vp, vp, vp, vp, sz, sz, sz, sz, sz, vp]),
+    "tmllm_embedding": (C.c_int, [C.c_int, vp, vp, vp, sz, sz, sz, vp, vp]),
+    "tmllm_add_rmsnorm": (C.c_int, [C.c_int, vp, vp, vp, vp, vp, sz, sz, C.c_float, vp]),
+    "tmllm_swiglu": (C.c_int, [C.c_int, vp, vp, sz, sz, vp]),
+    "tmllm_argmax": (C.c_int, [C.c_int, vp, vp, sz, sz, vp]),
     "tmllm_decode_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
     "tmllm_decode_workspace_init": (C.c_int, [vp, sz, vp]),
     "tmllm_decode_auto_splits": (i32, [i32, i32, i64]),

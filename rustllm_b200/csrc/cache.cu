@@ -284,6 +284,8 @@ int tmllm_cache_create(const tmllm_cache_config* config, tmllm_cache** out) {
         }
     }
     cudaError_t e = cudaMalloc(&c->arena, static_cast<size_t>(total));
+    // zeroed once, so slots never written (a block's tail) hold finite values
+    if (e == cudaSuccess) e = cudaMemset(c->arena, 0, static_cast<size_t>(total));
     if (e == cudaSuccess)
         e = cudaMalloc(&c->d_table, sizeof(int32_t) * c->h_table.size());
     if (e == cudaSuccess) e = cudaMalloc(&c->d_lens, sizeof(int32_t) * cf.num_seqs);
@@ -499,7 +501,8 @@ int tmllm_cache_decode(tmllm_cache* cache, int32_t layer, const void* q, const v
     }
     const int32_t splits =
         o.num_splits > 0 ? o.num_splits
-                         : decode_auto_splits(cache->cfg.num_seqs, cache->cfg.num_kv_heads, max_len);
+                         : decode_auto_splits(cache->cfg.num_seqs, cache->cfg.num_kv_heads,
+                                              std::max<int64_t>(max_len, o.max_len_hint));
     o.num_splits = splits;
     const size_t need = decode_workspace_bytes(cache->cfg.num_seqs, q_heads,
                                                cache->cfg.num_kv_heads, cache->cfg.head_dim,
@@ -518,8 +521,11 @@ int tmllm_cache_decode(tmllm_cache* cache, int32_t layer, const void* q, const v
     if (append)
         for (int i = 0; i < cache->cfg.num_seqs; ++i)
             if (int st = assign_blocks(cache, i, cache->h_lens[i] + 1, s)) return st;
+    // a caller that knows lengths will grow (a captured graph replayed for several steps)
+    // may ask for splits sized for the longest length it will see
+    const int64_t hint = std::max<int64_t>(max_len, o.max_len_hint);
     return decode_impl(&view, q, k_new, v_new, out, lse, q_heads, &o, cache->ws, cache->ws_bytes,
-                       max_len, s);
+                       hint, s);
 }
 
 }  // extern "C"

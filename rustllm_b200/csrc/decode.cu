@@ -51,6 +51,8 @@ struct DecodeArgs {
     float scale_log2;
     const ExchangeArgs* ex;  // cross-GPU split exchange, or null
     uint32_t epoch;          // exchange step number (1, 2, ...)
+    int64_t q_stride;        // elements between sequences in q
+    int64_t kv_stride;       // elements between sequences in k_new / v_new
 };
 
 // Physical slot of 16-byte chunk `c` of tile row `r` (XOR swizzle inside groups of 8).
@@ -163,8 +165,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_split_kernel(const D
         int g = idx / half, i = idx - g * half;
         float x1 = 0.f, x2 = 0.f;
         if (g < G) {
-            const T* qr = static_cast<const T*>(a.q) +
-                          (static_cast<int64_t>(b) * a.q_heads + kvh * G + g) * D;
+            const T* qr = static_cast<const T*>(a.q) + static_cast<int64_t>(b) * a.q_stride +
+                          static_cast<int64_t>(kvh * G + g) * D;
             x1 = to_f32<T>(qr[i]);
             x2 = to_f32<T>(qr[i + half]);
             rope_pair(a, qpos, i, half, x1, x2);
@@ -182,7 +184,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_split_kernel(const D
     }
     // ---- the new token: rotate k, keep both rows in shared memory, write them to the cache
     if (owns_new) {
-        const int64_t nrow = (static_cast<int64_t>(b) * a.kv_heads + kvh) * D;
+        const int64_t nrow = static_cast<int64_t>(b) * a.kv_stride + static_cast<int64_t>(kvh) * D;
         const T* kn = static_cast<const T*>(a.k_new) + nrow;
         const T* vn = static_cast<const T*>(a.v_new) + nrow;
         for (int i = tid; i < half; i += kDecodeThreads) {
@@ -752,7 +754,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_mma_kernel(const Dec
         float x1 = 0.f, x2 = 0.f;
         if (g < G) {
             const __half* qr = static_cast<const __half*>(a.q) +
-                               (static_cast<int64_t>(b) * a.q_heads + kvh * G + g) * D;
+                               static_cast<int64_t>(b) * a.q_stride +
+                               static_cast<int64_t>(kvh * G + g) * D;
             x1 = __half2float(qr[i]);
             x2 = __half2float(qr[i + half]);
             rope_pair(a, qpos, i, half, x1, x2);
@@ -761,7 +764,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_mma_kernel(const Dec
         q_s[g * QROW + i + half] = __float2half_rn(x2);
     }
     if (owns_new) {
-        const int64_t nrow = (static_cast<int64_t>(b) * a.kv_heads + kvh) * D;
+        const int64_t nrow = static_cast<int64_t>(b) * a.kv_stride + static_cast<int64_t>(kvh) * D;
         const __half* kn = static_cast<const __half*>(a.k_new) + nrow;
         const __half* vn = static_cast<const __half*>(a.v_new) + nrow;
         for (int i = tid; i < half; i += kDecodeThreads) {
@@ -1079,7 +1082,8 @@ __global__ void __launch_bounds__(128) decode_generic_kernel(const DecodeArgs a,
     const int L = cached + (has_new ? 1 : 0);
     const int half = D / 2;
     const int qpos = cached + a.rope_off;
-    const T* qr = static_cast<const T*>(a.q) + (static_cast<int64_t>(b) * a.q_heads + qh) * D;
+    const T* qr = static_cast<const T*>(a.q) + static_cast<int64_t>(b) * a.q_stride +
+                  static_cast<int64_t>(qh) * D;
     for (int i = tid; i < half; i += 128) {
         float x1 = to_f32<T>(qr[i]), x2 = to_f32<T>(qr[i + half]);
         rope_pair(a, qpos, i, half, x1, x2);
@@ -1087,7 +1091,7 @@ __global__ void __launch_bounds__(128) decode_generic_kernel(const DecodeArgs a,
         q_s[i + half] = round_store<T>(x2);
     }
     if (has_new) {
-        const int64_t nrow = (static_cast<int64_t>(b) * a.kv_heads + kvh) * D;
+        const int64_t nrow = static_cast<int64_t>(b) * a.kv_stride + static_cast<int64_t>(kvh) * D;
         const T* kn = static_cast<const T*>(a.k_new) + nrow;
         const T* vn = static_cast<const T*>(a.v_new) + nrow;
         for (int i = tid; i < half; i += 128) {
@@ -1411,6 +1415,12 @@ int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
     a.scale_log2 = scale * kLog2e;
     a.ex = ex;
     a.epoch = epoch;
+    if (o.q_seq_stride < 0 || o.kv_seq_stride < 0 ||
+        (o.q_seq_stride > 0 && o.q_seq_stride < static_cast<int64_t>(q_heads) * D) ||
+        (o.kv_seq_stride > 0 && o.kv_seq_stride < static_cast<int64_t>(Hkv) * D))
+        return fail(TMLLM_INVALID_SHAPE, "sequence strides of q / k_new must cover a sequence");
+    a.q_stride = o.q_seq_stride > 0 ? o.q_seq_stride : static_cast<int64_t>(q_heads) * D;
+    a.kv_stride = o.kv_seq_stride > 0 ? o.kv_seq_stride : static_cast<int64_t>(Hkv) * D;
     if (ex && !(mma_shape && o.variant != 1))
         return fail(TMLLM_INVALID_ARGUMENT,
                     "the cross-GPU exchange needs the tensor-core decode (F16, head_dim 64/128)");

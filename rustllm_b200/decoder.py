@@ -1,0 +1,283 @@
+"""Llama-family decoder around the fused decode path: the callers either side of it.
+
+Mirrors the reference's cached forward (src/model/transformer/cache.rs:25-82,
+src/nn/transformer_block.rs:128-159, src/nn/attention.rs:269-333, src/nn/mlp.rs) for a
+batch of sequences, one decode token per sequence per step:
+
+    embedding -> for each layer: [residual add +] RMSNorm -> fused QKV GEMM ->
+    fused RoPE + KV append + GQA attention -> O GEMM -> residual add + RMSNorm ->
+    fused gate/up GEMM -> SwiGLU -> down GEMM -> ... -> final norm -> lm_head -> argmax
+
+The attention, the norms, SwiGLU, the embedding and the greedy argmax are this package's
+CUDA kernels; the dense projections are plain cuBLAS GEMMs (torch.matmul).  Weights keep
+the reference's [in, out] layout (src/nn/linear.rs:26-27); Q, K, V and gate/up are
+concatenated along `out` so each pair/triple is one GEMM, and the attention reads q, k, v
+in place from the fused output through per-sequence strides.  A whole step is captured
+into one CUDA graph (``GraphedDecoder``).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import DecodeOpts, call
+from .kv_cache import PagedKvCache
+from .tensor_ops import dtype_code, rope_tables, stream_ptr
+
+
+@dataclass(frozen=True)
+class ModelConfig:
+    """src/model/config.rs:8-22."""
+
+    vocab_size: int
+    hidden_size: int
+    intermediate_size: int
+    num_layers: int
+    num_heads: int
+    num_kv_heads: int
+    max_seq_len: int
+    rms_norm_eps: float
+    rope_theta: float
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden_size // self.num_heads
+
+    def validate(self) -> None:
+        """src/model/config.rs:24-105."""
+        if min(self.vocab_size, self.hidden_size, self.intermediate_size, self.num_layers,
+               self.num_heads, self.num_kv_heads, self.max_seq_len) <= 0:
+            raise _lib.InvalidShape("model dimensions must be positive")
+        if self.hidden_size % self.num_heads or self.num_heads % self.num_kv_heads:
+            raise _lib.InvalidShape("hidden size must divide into heads and heads into KV heads")
+        if self.head_dim % 2:
+            raise _lib.InvalidShape("RoPE needs an even head dimension")
+        if not (self.rms_norm_eps > 0) or not (self.rope_theta > 0):
+            raise _lib.InvalidShape("rms_norm_eps and rope_theta must be positive")
+
+    def weight_params(self) -> int:
+        h, i, d = self.hidden_size, self.intermediate_size, self.head_dim
+        per_layer = (h * (self.num_heads + 2 * self.num_kv_heads) * d + self.num_heads * d * h
+                     + 3 * h * i + 2 * h)
+        return self.num_layers * per_layer + 2 * self.vocab_size * h + h
+
+
+# BASELINE.json configs 2, 3 and 5.
+PRESETS = {
+    "smollm2-135m": ModelConfig(49152, 576, 1536, 30, 9, 3, 2048, 1e-5, 100000.0),
+    "smollm2-360m": ModelConfig(49152, 960, 2560, 32, 15, 5, 2304, 1e-5, 100000.0),
+    "tinystories-110m": ModelConfig(32000, 768, 2048, 12, 12, 12, 1024, 1e-5, 10000.0),
+}
+
+
+class DecoderWeights:
+    """Random-init weights, N(0, std) for every projection and the embedding (the
+    BASELINE configs' synthetic models), unit RMSNorm scales, in the model dtype."""
+
+    def __init__(self, cfg: ModelConfig, *, dtype=torch.float16, device=None, seed: int = 0,
+                 std: float = 0.02):
+        cfg.validate()
+        dev = torch.device(device or "cuda")
+        g = torch.Generator(device=dev).manual_seed(seed)
+        h, i, d = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
+        qkv = (cfg.num_heads + 2 * cfg.num_kv_heads) * d
+
+        def rnd(*shape):
+            return (torch.randn(shape, generator=g, device=dev) * std).to(dtype)
+
+        self.embedding = rnd(cfg.vocab_size, h)
+        self.layers = []
+        for _ in range(cfg.num_layers):
+            self.layers.append({
+                "attn_norm": torch.ones(h, dtype=dtype, device=dev),
+                "wqkv": rnd(h, qkv),
+                "wo": rnd(cfg.num_heads * d, h),
+                "mlp_norm": torch.ones(h, dtype=dtype, device=dev),
+                "wgu": rnd(h, 2 * i),
+                "wd": rnd(i, h),
+            })
+        self.final_norm = torch.ones(h, dtype=dtype, device=dev)
+        self.lm_head = rnd(h, cfg.vocab_size)
+        self.dtype = dtype
+
+
+class Decoder:
+    """Batched greedy decoding for ``num_seqs`` sequences on one GPU."""
+
+    def __init__(self, cfg: ModelConfig, weights: DecoderWeights, num_seqs: int, *,
+                 block_size: int = 16, shuffle_seed: int = 0, device=None,
+                 max_seq_len: int | None = None):
+        self.cfg, self.w, self.B = cfg, weights, num_seqs
+        self.device = torch.device(device or "cuda")
+        self.dtype = weights.dtype
+        self.max_seq_len = max_seq_len or cfg.max_seq_len
+        self.cache = PagedKvCache(cfg.num_layers, num_seqs, self.max_seq_len, cfg.num_kv_heads,
+                                  cfg.head_dim, dtype=self.dtype, block_size=block_size,
+                                  shuffle_seed=shuffle_seed, device=self.device)
+        self.rope = rope_tables(cfg.head_dim, self.max_seq_len + 1, cfg.rope_theta,
+                                device=self.device)
+        B, h, d = num_seqs, cfg.hidden_size, cfg.head_dim
+        hq, hkv = cfg.num_heads, cfg.num_kv_heads
+        e = dict(dtype=self.dtype, device=self.device)
+        self.ids = torch.zeros(B, dtype=torch.int32, device=self.device)
+        self.next_ids = torch.zeros(B, dtype=torch.int32, device=self.device)
+        self.x = torch.empty((B, h), **e)
+        self.hn = torch.empty((B, h), **e)
+        self.qkv = torch.empty((B, (hq + 2 * hkv) * d), **e)
+        self.attn = torch.empty((B, hq, d), **e)
+        self.o = torch.empty((B, h), **e)
+        self.gu = torch.empty((B, 2 * cfg.intermediate_size), **e)
+        self.act = torch.empty((B, cfg.intermediate_size), **e)
+        self.down = torch.empty((B, h), **e)
+        self.logits = torch.empty((B, cfg.vocab_size), **e)
+        self.bad = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.dt = dtype_code(self.dtype)
+        self.max_len_hint = 0
+
+    # -- pieces ------------------------------------------------------------------------
+    def _norm(self, x, residual, weight, out, sum_out):
+        call("tmllm_add_rmsnorm", self.dt, x.data_ptr(),
+             residual.data_ptr() if residual is not None else None, weight.data_ptr(),
+             out.data_ptr(), sum_out.data_ptr() if sum_out is not None else None, x.shape[0],
+             x.shape[1], self.cfg.rms_norm_eps, stream_ptr(self.device))
+
+    def _attention(self, layer: int) -> None:
+        cfg, B = self.cfg, self.B
+        hq, hkv, d = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+        w = self.qkv.shape[1]
+        base = self.qkv.data_ptr()
+        es = self.qkv.element_size()
+        opts = DecodeOpts(q_seq_stride=w, kv_seq_stride=w, max_len_hint=self.max_len_hint)
+        cos, sin = self.rope
+        opts.rope_cos, opts.rope_sin, opts.rope_len = cos.data_ptr(), sin.data_ptr(), cos.shape[0]
+        call("tmllm_cache_decode", self.cache.handle, layer, base, base + hq * d * es,
+             base + (hq + hkv) * d * es, self.attn.data_ptr(), None, hq, C.byref(opts),
+             stream_ptr(self.device))
+
+    def forward_step(self) -> None:
+        """One decode step for every sequence: reads ``self.ids``, appends K/V at each
+        sequence's length, writes ``self.next_ids``.  Lengths are not advanced."""
+        cfg, w = self.cfg, self.w
+        call("tmllm_embedding", self.dt, w.embedding.data_ptr(), self.ids.data_ptr(),
+             self.x.data_ptr(), self.B, cfg.hidden_size, cfg.vocab_size, self.bad.data_ptr(),
+             stream_ptr(self.device))
+        residual = None
+        for li, L in enumerate(w.layers):
+            # x <- x + residual; hn <- rmsnorm(x)  (transformer_block.rs:137-139,148)
+            self._norm(self.x, residual, L["attn_norm"], self.hn, self.x)
+            torch.matmul(self.hn, L["wqkv"], out=self.qkv)
+            self._attention(li)
+            torch.matmul(self.attn.view(self.B, -1), L["wo"], out=self.o)
+            self._norm(self.x, self.o, L["mlp_norm"], self.hn, self.x)
+            torch.matmul(self.hn, L["wgu"], out=self.gu)
+            call("tmllm_swiglu", self.dt, self.gu.data_ptr(), self.act.data_ptr(), self.B,
+                 cfg.intermediate_size, stream_ptr(self.device))
+            torch.matmul(self.act, L["wd"], out=self.down)
+            residual = self.down
+        self._norm(self.x, residual, w.final_norm, self.hn, None)
+        torch.matmul(self.hn, w.lm_head, out=self.logits)
+        call("tmllm_argmax", self.dt, self.logits.data_ptr(), self.next_ids.data_ptr(), self.B,
+             cfg.vocab_size, stream_ptr(self.device))
+
+    # -- driving -----------------------------------------------------------------------
+    def check_ids(self, ids: torch.Tensor) -> None:
+        bad = (ids < 0) | (ids >= self.cfg.vocab_size)
+        if bool(bad.any()):  # TinyError::InvalidTokenId
+            raise _lib.InvalidArgument(f"token id outside the vocabulary of {self.cfg.vocab_size}")
+
+    def prefill(self, prompts: torch.Tensor) -> torch.Tensor:
+        """Feeds prompts [B, S] token by token (each position through the fused decode
+        path, which is exact causal attention), returns the greedy token after the prompt."""
+        self.check_ids(prompts)
+        B, S = prompts.shape
+        self.max_len_hint = max(self.cache.lens()) + S
+        for t in range(S):
+            self.ids.copy_(prompts[:, t].to(torch.int32))
+            self.forward_step()
+            self.cache.advance(1)
+        return self.next_ids.clone()
+
+    def decode(self, steps: int, first: torch.Tensor | None = None) -> torch.Tensor:
+        """Greedy-decodes ``steps`` tokens per sequence without graphs; returns [steps, B]."""
+        out = torch.empty((steps, self.B), dtype=torch.int32, device=self.device)
+        self.ids.copy_(first if first is not None else self.next_ids)
+        self.max_len_hint = max(self.cache.lens()) + steps
+        for i in range(steps):
+            self.forward_step()
+            self.cache.advance(1)
+            out[i].copy_(self.next_ids)
+            self.ids.copy_(self.next_ids)
+        return out
+
+
+class GraphedDecoder:
+    """Captures one decode step of a ``Decoder`` (embedding .. argmax, plus feeding the
+    chosen token back as the next input) into a CUDA graph.  Blocks for ``steps`` more
+    tokens per sequence are reserved before capture, since a replay cannot run the cache's
+    host-side block allocation."""
+
+    def __init__(self, dec: Decoder, steps: int):
+        self.dec = dec
+        for s in range(dec.B):
+            dec.cache.reserve(s, steps + 1)
+        dec.max_len_hint = max(dec.cache.lens()) + steps + 1
+        stream = torch.cuda.Stream(dec.device)
+        stream.wait_stream(torch.cuda.current_stream(dec.device))
+        with torch.cuda.stream(stream):
+            dec.forward_step()  # first call sizes the cache's workspace outside the capture
+        torch.cuda.current_stream(dec.device).wait_stream(stream)
+        torch.cuda.synchronize(dec.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=stream):
+            dec.forward_step()
+            dec.ids.copy_(dec.next_ids)
+        self.steps_left = steps
+
+    def step(self) -> None:
+        if self.steps_left <= 0:
+            raise _lib.PositionOutOfRange("graph was captured for fewer steps")
+        self.graph.replay()
+        self.dec.cache.advance(1)
+        self.steps_left -= 1
+
+
+def reference_forward(cfg: ModelConfig, w: DecoderWeights, tokens: torch.Tensor) -> torch.Tensor:
+    """Float32 restatement of the whole model on one sequence (tokens [S]) with full causal
+    attention, used as the test reference: logits [S, vocab]."""
+    f = torch.float32
+    x = w.embedding[tokens.long()].to(f)
+    S = x.shape[0]
+    hq, hkv, d = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+    pos = torch.arange(S, device=x.device, dtype=f)
+    inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, d, 2, device=x.device, dtype=f) / d))
+    ang = pos[:, None] * inv[None, :]
+    cos, sin = torch.cos(ang), torch.sin(ang)
+
+    def rope(t):  # t [S, H, d], half-split pairs (kernels/rope.metal:57-63)
+        a, b = t[..., : d // 2], t[..., d // 2:]
+        return torch.cat([a * cos[:, None] - b * sin[:, None], b * cos[:, None] + a * sin[:, None]], -1)
+
+    def norm(t, wt):
+        return t * torch.rsqrt((t * t).mean(-1, keepdim=True) + cfg.rms_norm_eps) * wt.to(f)
+
+    mask = torch.full((S, S), float("-inf"), device=x.device).triu(1)
+    for L in w.layers:
+        hn = norm(x, L["attn_norm"])
+        qkv = hn @ L["wqkv"].to(f)
+        q = rope(qkv[:, : hq * d].view(S, hq, d))
+        k = rope(qkv[:, hq * d:(hq + hkv) * d].view(S, hkv, d))
+        v = qkv[:, (hq + hkv) * d:].view(S, hkv, d)
+        k = k.repeat_interleave(hq // hkv, dim=1)
+        v = v.repeat_interleave(hq // hkv, dim=1)
+        att = torch.einsum("shd,thd->hst", q, k) / math.sqrt(d) + mask
+        o = torch.einsum("hst,thd->shd", att.softmax(-1), v).reshape(S, hq * d)
+        x = x + o @ L["wo"].to(f)
+        hn = norm(x, L["mlp_norm"])
+        gu = hn @ L["wgu"].to(f)
+        g_, u_ = gu[:, : cfg.intermediate_size], gu[:, cfg.intermediate_size:]
+        x = x + (g_ * torch.sigmoid(g_) * u_) @ L["wd"].to(f)
+    return norm(x, w.final_norm) @ w.lm_head.to(f)

@@ -1,0 +1,137 @@
+"""The decoder around the decode path (embedding, add+RMSNorm, SwiGLU, argmax, GEMMs, the
+fused attention) against a float32 PyTorch restatement of the same model, plus graph
+replay against eager decoding.  Tolerances: kernels 1e-2 relative (F16 storage), model
+logits 3e-2 relative to the largest logit after a few F16 layers."""
+from __future__ import annotations
+
+import ctypes as C
+
+import pytest
+import torch
+
+import rustllm_b200 as rb
+from rustllm_b200 import _lib
+from rustllm_b200.decoder import (Decoder, DecoderWeights, GraphedDecoder, ModelConfig,
+                                  reference_forward)
+
+pytestmark = pytest.mark.gpu
+
+TINY = ModelConfig(vocab_size=1000, hidden_size=256, intermediate_size=512, num_layers=2,
+                   num_heads=4, num_kv_heads=2, max_seq_len=96, rms_norm_eps=1e-5,
+                   rope_theta=10000.0)
+
+
+def rel(a, b):
+    a, b = a.double(), b.double()
+    return float((a - b).abs().max() / b.abs().max())
+
+
+def stream(dev):
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def test_embedding_gathers_rows(cuda):
+    table = torch.randn((50, 24), device=cuda).half()
+    ids = torch.tensor([3, 0, 49, 7, 3], dtype=torch.int32, device=cuda)
+    out = torch.empty((5, 24), dtype=torch.float16, device=cuda)
+    bad = torch.zeros(1, dtype=torch.int32, device=cuda)
+    _lib.call("tmllm_embedding", 1, table.data_ptr(), ids.data_ptr(), out.data_ptr(), 5, 24, 50,
+              bad.data_ptr(), stream(cuda))
+    assert torch.equal(out, table[ids.long()]) and int(bad) == 0
+    ids[2] = 50  # outside the table: zero row, flag set
+    _lib.call("tmllm_embedding", 1, table.data_ptr(), ids.data_ptr(), out.data_ptr(), 5, 24, 50,
+              bad.data_ptr(), stream(cuda))
+    assert int(bad) == 1 and torch.count_nonzero(out[2]) == 0
+
+
+@pytest.mark.parametrize("hidden", [576, 960, 100])
+def test_add_rmsnorm_matches_float32(cuda, hidden):
+    x = torch.randn((3, hidden), device=cuda).half()
+    r = torch.randn((3, hidden), device=cuda).half()
+    w = (torch.rand(hidden, device=cuda) + 0.5).half()
+    out = torch.empty_like(x)
+    s = (x.float() + r.float()).half()
+    want = s.float() * torch.rsqrt((s.float() ** 2).mean(-1, keepdim=True) + 1e-5) * w.float()
+    xs = x.clone()
+    _lib.call("tmllm_add_rmsnorm", 1, xs.data_ptr(), r.data_ptr(), w.data_ptr(), out.data_ptr(),
+              xs.data_ptr(), 3, hidden, 1e-5, stream(cuda))  # in-place residual update
+    assert torch.equal(xs, s)
+    assert rel(out, want) < 1e-2
+    with pytest.raises(rb.InvalidShape):
+        _lib.call("tmllm_add_rmsnorm", 1, x.data_ptr(), None, w.data_ptr(), out.data_ptr(), None,
+                  3, hidden, 0.0, stream(cuda))
+
+
+def test_swiglu_matches_float32(cuda):
+    gu = torch.randn((4, 2 * 300), device=cuda).half()
+    out = torch.empty((4, 300), dtype=torch.float16, device=cuda)
+    _lib.call("tmllm_swiglu", 1, gu.data_ptr(), out.data_ptr(), 4, 300, stream(cuda))
+    g, u = gu[:, :300].float(), gu[:, 300:].float()
+    assert rel(out, g * torch.sigmoid(g) * u) < 1e-2
+
+
+def test_argmax_takes_last_of_equal_maxima(cuda):
+    """src/generation/sampler.rs:79-88 keeps the last maximum (Iterator::max_by)."""
+    logits = torch.randn((3, 49152), device=cuda).half()
+    logits[1, 100] = 30.0
+    logits[1, 40000] = 30.0
+    logits[2, 7] = 20.0
+    ids = torch.empty(3, dtype=torch.int32, device=cuda)
+    _lib.call("tmllm_argmax", 1, logits.data_ptr(), ids.data_ptr(), 3, 49152, stream(cuda))
+    assert int(ids[0]) == int(logits[0].float().argmax())
+    assert int(ids[1]) == 40000 and int(ids[2]) == 7
+
+
+def test_decoder_logits_match_float32_model(cuda):
+    w = DecoderWeights(TINY, device=cuda, seed=1, std=0.08)
+    dec = Decoder(TINY, w, 1, device=cuda)
+    prompt = torch.randint(0, TINY.vocab_size, (12,), generator=torch.Generator().manual_seed(2))
+    want = reference_forward(TINY, w, prompt.to(cuda))
+    for t in range(12):
+        dec.ids.copy_(prompt[t:t + 1].to(torch.int32))
+        dec.forward_step()
+        dec.cache.advance(1)
+        assert rel(dec.logits[0], want[t]) < 3e-2, t
+    assert dec.cache.len(0) == 12
+
+
+def test_batched_decode_matches_single_sequences(cuda):
+    w = DecoderWeights(TINY, device=cuda, seed=3, std=0.08)
+    g = torch.Generator().manual_seed(4)
+    prompts = torch.randint(0, TINY.vocab_size, (3, 9), generator=g)
+    batch = Decoder(TINY, w, 3, device=cuda, shuffle_seed=9)
+    nb = batch.prefill(prompts.to(cuda))
+    toks = batch.decode(6, nb)
+    for s in range(3):
+        single = Decoder(TINY, w, 1, device=cuda)
+        n1 = single.prefill(prompts[s:s + 1].to(cuda))
+        assert int(n1[0]) == int(nb[s])
+        t1 = single.decode(6, n1)
+        assert torch.equal(t1[:, 0], toks[:, s])
+
+
+def test_graph_replay_equals_eager_decoding(cuda):
+    cfg = TINY
+    w = DecoderWeights(cfg, device=cuda, seed=5, std=0.08)
+    prompts = torch.randint(0, cfg.vocab_size, (2, 5), generator=torch.Generator().manual_seed(6))
+    eager = Decoder(cfg, w, 2, device=cuda)
+    first = eager.prefill(prompts.to(cuda))
+    want = eager.decode(10, first)
+    graphed = Decoder(cfg, w, 2, device=cuda)
+    first2 = graphed.prefill(prompts.to(cuda))
+    assert torch.equal(first, first2)
+    graphed.ids.copy_(first2)
+    runner = GraphedDecoder(graphed, 10)
+    got = []
+    for _ in range(10):
+        runner.step()
+        got.append(graphed.ids.clone())  # the graph fed the chosen token back
+    assert torch.equal(torch.stack(got), want)
+    assert graphed.cache.lens() == [15, 15]
+
+
+def test_invalid_prompt_token_rejected(cuda):
+    w = DecoderWeights(TINY, device=cuda, seed=0)
+    dec = Decoder(TINY, w, 1, device=cuda)
+    with pytest.raises(rb.InvalidArgument):
+        dec.prefill(torch.tensor([[1, TINY.vocab_size]], device=cuda))
