@@ -262,6 +262,35 @@ int tmllm_gqa_decode_noalloc(const tmllm_paged_kv* kv, const void* q, const void
                              const void* v_new, void* out, float* lse, int32_t q_heads,
                              const tmllm_decode_opts* opts, tmllm_stream stream);
 
+/* Fused KV-append + causal attention for a chunk of new tokens per sequence (prefill).
+ * Replaces, for q_len > 1, the chain SelfAttention::forward_with_cache_encode runs
+ * (src/nn/attention.rs:303-315): LayerKvCache::append_encode (kv_cache.rs:112-142) of the
+ * RoPE'd keys and the values, then attention_core_encode (attention.rs:216-247) with
+ * start = the cached length, i.e. query row i of a sequence attends keys
+ * [0, seq_lens[s] + i] (attention_scale_mask.metal:21-41).
+ *   q      [total_rows, q_heads, head_dim]       (cache dtype; row stride opts->q_seq_stride)
+ *   k_new  [total_rows, num_kv_heads, head_dim]  appended at seq_lens[s] + i
+ *   v_new  [total_rows, num_kv_heads, head_dim]  (row stride opts->kv_seq_stride)
+ *   out    [total_rows, q_heads, head_dim]       (cache dtype, or F32 if opts->out_f32)
+ * Rows are grouped by sequence.  q_start (device, int32 [num_seqs + 1]) gives each
+ * sequence's first row; with q_start == NULL every sequence has rows_per_seq rows and
+ * max_rows / total_rows are ignored.  Otherwise max_rows is the largest row count and
+ * total_rows = q_start[num_seqs].  RoPE (opts->rope_*) rotates q and k at position
+ * seq_lens[s] + i + opts->rope_pos_offset.  Blocks for the new positions must already be in
+ * the block table; seq_lens is NOT advanced.  opts->num_splits, max_len_hint and lse are not
+ * used.  F16 with head_dim 64/128 and power-of-two pages of >= 16 positions runs on the
+ * tensor cores (opts->variant 0 or 2); everything else on the CUDA cores (variant 1 forces
+ * that path). */
+int tmllm_gqa_prefill(const tmllm_paged_kv* kv, const void* q, const void* k_new,
+                      const void* v_new, const int32_t* q_start, int32_t rows_per_seq,
+                      int32_t max_rows, int32_t total_rows, void* out, int32_t q_heads,
+                      const tmllm_decode_opts* opts, tmllm_stream stream);
+/* New (the reference's kernels cannot stall).  Reads and clears the status word of the
+ * prefill kernel's bounded waits on the current device: TMLLM_OK, or TMLLM_TIMEOUT when a
+ * wait inside the kernel expired (that launch's output rows are unspecified).
+ * Synchronises with the device. */
+int tmllm_prefill_status(int32_t* status);
+
 /* Log-sum-exp merge of partial attention results (the combine step of a sequence split
  * across GPUs).  Part p's normalised output rows are at parts_o + p*o_stride ([rows,
  * head_dim] F32) and its log-sum-exp values at parts_lse + p*lse_stride ([rows] F32);
@@ -377,6 +406,13 @@ int tmllm_cache_gather(const tmllm_cache* cache, int32_t layer, int32_t seq, voi
 int tmllm_cache_decode(tmllm_cache* cache, int32_t layer, const void* q, const void* k_new,
                        const void* v_new, void* out, float* lse, int32_t q_heads,
                        const tmllm_decode_opts* opts, tmllm_stream stream);
+/* Fused append + causal prefill attention over every sequence of the cache for `layer`
+ * (see tmllm_gqa_prefill): sequence s owns rows [s * n, (s + 1) * n) of q / k_new / v_new /
+ * out.  Blocks for the n new positions of every sequence are reserved first.  Lengths are
+ * not advanced (tmllm_cache_advance by n after the last layer). */
+int tmllm_cache_prefill(tmllm_cache* cache, int32_t layer, const void* q, const void* k_new,
+                        const void* v_new, int64_t n, void* out, int32_t q_heads,
+                        const tmllm_decode_opts* opts, tmllm_stream stream);
 
 #ifdef __cplusplus
 }

@@ -6,7 +6,8 @@ host-side mirror of the reference's Rust call surface on torch CUDA tensors.
 from ._lib import (DeviceError, DeviceTimeout, InvalidArgument, InvalidDimension, InvalidShape,
                    ModelFormat, NonContiguousTensor, NotReserved, OutOfBlocks, PositionOutOfRange,
                    ShapeMismatch, TinyError, UnsupportedDType, load)
-from .attention import DecodeWorkspace, auto_splits, gqa_decode, merge_lse, paged_kv_from_tensors
+from .attention import (DecodeWorkspace, auto_splits, gqa_decode, gqa_prefill, merge_lse,
+                        paged_kv_from_tensors, prefill_status)
 from .kv_cache import KvCache, LayerKvCache, PagedKvCache
 from .tensor_ops import (attention_core, attention_scale_mask, batched_matmul, concat_sequence,
                          gqa_pv_matmul, gqa_qk_matmul, kv_cache_write, repeat_kv, rope,
@@ -16,7 +17,8 @@ __all__ = [
     "TinyError", "InvalidArgument", "InvalidShape", "ShapeMismatch", "InvalidDimension",
     "UnsupportedDType", "NonContiguousTensor", "PositionOutOfRange", "ModelFormat",
     "DeviceError", "OutOfBlocks", "DeviceTimeout", "NotReserved", "load",
-    "DecodeWorkspace", "auto_splits", "gqa_decode", "merge_lse", "paged_kv_from_tensors",
+    "DecodeWorkspace", "auto_splits", "gqa_decode", "gqa_prefill", "merge_lse",
+    "paged_kv_from_tensors", "prefill_status",
     "KvCache", "LayerKvCache", "PagedKvCache",
     "attention_core", "attention_scale_mask", "batched_matmul", "concat_sequence",
     "gqa_pv_matmul", "gqa_qk_matmul", "kv_cache_write", "repeat_kv", "rope", "rope_tables",

@@ -141,6 +141,9 @@ _PROTOS = {
                                    C.POINTER(DecodeOpts), vp, sz, vp]),
     "tmllm_gqa_decode_noalloc": (C.c_int, [C.POINTER(PagedKV), vp, vp, vp, vp, vp, i32,
                                            C.POINTER(DecodeOpts), vp]),
+    "tmllm_gqa_prefill": (C.c_int, [C.POINTER(PagedKV), vp, vp, vp, vp, i32, i32, i32, vp, i32,
+                                    C.POINTER(DecodeOpts), vp]),
+    "tmllm_prefill_status": (C.c_int, [C.POINTER(i32)]),
     "tmllm_merge_lse": (C.c_int, [vp, vp, i32, i32, i32, i64, i64, vp, i32, vp, vp]),
     "tmllm_exchange_create": (C.c_int, [i32, i32, i32, i32, i32, C.POINTER(vp), vp]),
     "tmllm_exchange_connect": (C.c_int, [vp, vp]),
@@ -164,6 +167,8 @@ _PROTOS = {
     "tmllm_cache_gather": (C.c_int, [vp, i32, i32, vp, vp, vp]),
     "tmllm_cache_decode": (C.c_int, [vp, i32, vp, vp, vp, vp, vp, i32, C.POINTER(DecodeOpts),
                                      vp]),
+    "tmllm_cache_prefill": (C.c_int, [vp, i32, vp, vp, vp, i64, vp, i32, C.POINTER(DecodeOpts),
+                                      vp]),
 }
 
 _lib = None

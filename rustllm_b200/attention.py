@@ -91,6 +91,67 @@ def merge_packed(parts: torch.Tensor, rows: int, head_dim: int, *, out: torch.Te
     return out
 
 
+def _row_stride(t: torch.Tensor, heads: int, d: int, what: str) -> int:
+    """Elements between consecutive rows of a [rows, heads, D] tensor whose last two
+    dimensions are packed (a view into a wider fused projection is fine)."""
+    if t.dim() != 3 or t.shape[1] != heads or t.shape[2] != d:
+        raise _lib.ModelFormat(f"{what} must be [rows, {heads}, {d}], got {list(t.shape)}")
+    if t.stride(2) != 1 or t.stride(1) != d:
+        raise _lib.NonContiguousTensor(f"{what} heads must be packed rows of {d} elements")
+    return t.stride(0)
+
+
+def gqa_prefill(kv: PagedKV, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, *,
+                q_start: torch.Tensor | None = None, rows_per_seq: int = 0, max_rows: int = 0,
+                out: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
+                scale: float = 0.0, rope=None, rope_pos_offset: int = 0,
+                variant: int = 0) -> torch.Tensor:
+    """Fused KV-append + causal prefill attention (``tmllm_gqa_prefill``).
+
+    q [rows, Hq, D], k_new / v_new [rows, Hkv, D] (row-strided views allowed), rows grouped
+    by sequence: ``q_start`` int32 [num_seqs + 1] row offsets on the device, or None with
+    ``rows_per_seq`` rows per sequence.  Row i of sequence s is appended at seq_lens[s] + i
+    and attends keys [0, seq_lens[s] + i].  Returns out [rows, Hq, D]."""
+    rows, hq, d = q.shape
+    hkv = kv.num_kv_heads
+    qs = _row_stride(q, hq, d, "q")
+    ks = _row_stride(k_new, hkv, d, "k_new")
+    if _row_stride(v_new, hkv, d, "v_new") != ks or k_new.shape[0] != rows or v_new.shape[0] != rows:
+        raise _lib.ShapeMismatch("k_new and v_new must have q's rows and the same row stride")
+    if out is None:
+        out = torch.empty((rows, hq, d), dtype=out_dtype or q.dtype, device=q.device)
+    if (out.dtype not in (q.dtype, torch.float32) or tuple(out.shape) != (rows, hq, d)
+            or not out.is_contiguous()):
+        raise _lib.InvalidArgument("out must be a contiguous [rows, Hq, D] tensor in the cache "
+                                   "dtype or F32")
+    opts = DecodeOpts(scale=scale, out_f32=int(out.dtype == torch.float32),
+                      rope_pos_offset=rope_pos_offset, variant=variant, q_seq_stride=qs,
+                      kv_seq_stride=ks)
+    if rope is not None:
+        cos, sin = rope
+        opts.rope_cos, opts.rope_sin, opts.rope_len = cos.data_ptr(), sin.data_ptr(), cos.shape[0]
+    if q_start is not None:
+        if q_start.dtype != torch.int32 or q_start.numel() != kv.num_seqs + 1:
+            raise _lib.InvalidArgument("q_start must be int32 [num_seqs + 1]")
+        if max_rows <= 0:
+            max_rows = int((q_start[1:] - q_start[:-1]).max())
+        qp = q_start.data_ptr()
+    else:
+        if rows_per_seq * kv.num_seqs != rows:
+            raise _lib.ShapeMismatch(f"{rows} rows are not {kv.num_seqs} x {rows_per_seq}")
+        qp = None
+    call("tmllm_gqa_prefill", C.byref(kv), q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), qp,
+         rows_per_seq, max_rows, rows, out.data_ptr(), hq, C.byref(opts), stream_ptr(q.device))
+    return out
+
+
+def prefill_status() -> int:
+    """Reads and clears the prefill kernel's wait status (0, or the TMLLM_TIMEOUT code)."""
+    st = C.c_int32()
+    call("tmllm_prefill_status", C.byref(st))
+    return st.value
+
+
 def paged_kv_from_tensors(k_arena: torch.Tensor, v_arena: torch.Tensor,
                           block_table: torch.Tensor, seq_lens: torch.Tensor) -> PagedKV:
     """A ``PagedKV`` over caller-owned tensors: arenas [num_blocks, Hkv, block_size, D],

@@ -14,7 +14,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libtmllm_b200.so")
 SOURCES = ["api.cu", "ops.cu", "decode.cu", "cache.cu", "noalloc.cu", "exchange.cu",
-           "decoder.cu"]
+           "decoder.cu", "prefill.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -21,6 +21,10 @@ int decode_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, cons
                 cudaStream_t stream);
 size_t decode_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t splits);
 int32_t decode_auto_splits(int64_t B, int64_t Hkv, int64_t max_len);
+int prefill_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, const void* v_new,
+                 const int32_t* q_start, int32_t rows_per_seq, int32_t max_rows,
+                 int32_t total_rows, void* out, int32_t q_heads, const tmllm_decode_opts* opts,
+                 cudaStream_t stream);
 
 namespace {
 
@@ -526,6 +530,54 @@ int tmllm_cache_decode(tmllm_cache* cache, int32_t layer, const void* q, const v
     const int64_t hint = std::max<int64_t>(max_len, o.max_len_hint);
     return decode_impl(&view, q, k_new, v_new, out, lse, q_heads, &o, cache->ws, cache->ws_bytes,
                        hint, s);
+}
+
+int tmllm_cache_prefill(tmllm_cache* cache, int32_t layer, const void* q, const void* k_new,
+                        const void* v_new, int64_t n, void* out, int32_t q_heads,
+                        const tmllm_decode_opts* opts, tmllm_stream stream) {
+    clear_error();
+    if (int st = check_cache(cache)) return st;
+    if (int st = check_layer(cache, layer)) return st;
+    if (q_heads <= 0 || q_heads % cache->cfg.num_kv_heads != 0)
+        return fail(TMLLM_MODEL_FORMAT, "Q heads %d must be divisible by non-zero KV heads %d",
+                    q_heads, cache->cfg.num_kv_heads);
+    if (n < 0) return fail(TMLLM_INVALID_ARGUMENT, "negative token count %lld",
+                           static_cast<long long>(n));
+    if (n == 0) return TMLLM_OK;
+    if (!k_new || !v_new) return fail(TMLLM_INVALID_ARGUMENT, "prefill needs k_new and v_new");
+    if (n > INT32_MAX / std::max(1, cache->cfg.num_seqs))
+        return fail(TMLLM_INVALID_SHAPE, "prefill rows exceed i32");
+    int64_t need_total = 0;
+    for (int i = 0; i < cache->cfg.num_seqs; ++i) {
+        const int64_t len = cache->h_lens[i];
+        if (n > cache->cfg.max_seq_len - len)  // kv_cache.rs:40-51
+            return fail(TMLLM_POSITION_OUT_OF_RANGE,
+                        "position range [%lld, %lld) exceeds max sequence length %d",
+                        static_cast<long long>(len), static_cast<long long>(len + n),
+                        cache->cfg.max_seq_len);
+        need_total += blocks_needed(cache, i, len + n);
+    }
+    if (need_total > static_cast<int64_t>(cache->free_ids.size()))
+        return fail(TMLLM_OUT_OF_BLOCKS, "KV block pool exhausted");
+    tmllm_decode_opts o{};
+    if (opts) o = *opts;
+    if (o.rope_cos) {
+        for (int i = 0; i < cache->cfg.num_seqs; ++i) {
+            const int64_t lo = cache->h_lens[i] + o.rope_pos_offset, hi = lo + n - 1;
+            if (lo < 0 || hi >= o.rope_len)
+                return fail(TMLLM_POSITION_OUT_OF_RANGE,
+                            "RoPE positions [%lld, %lld] outside the %d-entry table",
+                            static_cast<long long>(lo), static_cast<long long>(hi), o.rope_len);
+        }
+    }
+    DeviceGuard guard(cache->cfg.device);
+    auto s = reinterpret_cast<cudaStream_t>(stream);
+    for (int i = 0; i < cache->cfg.num_seqs; ++i)
+        if (int st = assign_blocks(cache, i, cache->h_lens[i] + n, s)) return st;
+    tmllm_paged_kv view;
+    tmllm_cache_view(cache, layer, &view);
+    return prefill_impl(&view, q, k_new, v_new, nullptr, static_cast<int32_t>(n), 0, 0, out,
+                        q_heads, &o, s);
 }
 
 }  // extern "C"

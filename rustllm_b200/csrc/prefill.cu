@@ -1,0 +1,886 @@
+// Prefill: a chunk of new tokens per sequence is appended to the paged KV cache and attends
+// causally over everything the sequence has cached, in two launches:
+//
+//   prefill_append_kernel   RoPE on the new keys, storage rounding, scatter of K and V rows
+//                           into the paged arena (kernels/rope.metal:57-63 and
+//                           kernels/kv_cache_write.metal:13-18 over the block table);
+//   prefill_tc_kernel<D>    flash attention on the 5th-generation tensor cores: one CTA per
+//                           (128 query rows, query head, sequence).  Q·Kᵀ and P·V are
+//                           tcgen05.mma (F16 operands in 128-byte-swizzled shared memory, F32
+//                           accumulators in tensor memory); K and V pages arrive by TMA
+//                           straight from the paged arena; the online softmax runs in four
+//                           warps, one thread per query row, reading S out of tensor memory.
+//
+// The attention equals the reference's chain for S > 1 new tokens
+// (nn/attention.rs:216-247 with start = cached length, :303-315): scores = Q·Kᵀ, scale,
+// causal mask j > start + i -> -inf (kernels/attention_scale_mask.metal:21-41), softmax over
+// the row (kernels/softmax.metal), P·V (kernels/gqa_matmul.metal:323-629), with the F32
+// accumulation of those kernels and one F16 rounding of P before the second product.
+// F32 caches, other head sizes and small pages run a CUDA-core kernel with the same
+// semantics (prefill_generic_kernel).
+#include <cuda.h>  // CUtensorMap and its enums; the encoder is fetched from the driver at run time
+
+#include <cmath>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace tmllm {
+
+namespace {
+
+constexpr float kLog2eP = 1.4426950408889634f;
+constexpr int kTile = 128;            // query rows per CTA and keys per tile
+constexpr int kSoftmaxThreads = 128;  // warps 0-3: one thread per query row
+constexpr int kPrefillThreads = 160;  // + warp 4: TMA producer and MMA issuer (one lane)
+constexpr unsigned long long kWaitLimitNs = 1000000000ull;  // bounded waits: 1 s
+
+// Status word of the bounded waits (TMLLM_TIMEOUT after an expired wait); read and cleared by
+// tmllm_prefill_status.
+__device__ int g_prefill_status;
+
+struct PrefillArgs {
+    const void* q;
+    const void* k_new;
+    const void* v_new;
+    void* k_cache;
+    void* v_cache;
+    void* out;
+    const int32_t* block_table;
+    const int32_t* seq_lens;  // cached length of each sequence before this chunk
+    const int32_t* q_start;   // [num_seqs + 1] row offsets, or null: uniform rows per sequence
+    const float* rope_cos;
+    const float* rope_sin;
+    int64_t num_blocks;
+    int64_t arena_rows;  // rows of D elements in one arena (TMA coordinate bound)
+    int64_t q_stride;    // elements between consecutive rows of q
+    int64_t kv_stride;   // elements between consecutive rows of k_new / v_new
+    int64_t out_stride;  // elements between consecutive rows of out (q_heads * D)
+    int32_t uniform_rows, num_seqs, total_rows;
+    int32_t q_heads, kv_heads, group, head_dim, block_size, bs_shift, max_blocks;
+    int32_t rope_len, rope_off, out_f32;
+    float scale_log2;
+};
+
+__device__ __forceinline__ int seq_rows(const PrefillArgs& a, int s, int* row0) {
+    if (a.q_start) {
+        *row0 = a.q_start[s];
+        return a.q_start[s + 1] - a.q_start[s];
+    }
+    *row0 = s * a.uniform_rows;
+    return a.uniform_rows;
+}
+
+// Sequence owning packed row `row` (rows are grouped by sequence in order).
+__device__ __forceinline__ int seq_of_row(const PrefillArgs& a, int row) {
+    if (!a.q_start) return row / a.uniform_rows;
+    int lo = 0, hi = a.num_seqs - 1;
+    while (lo < hi) {  // last s with q_start[s] <= row
+        const int mid = (lo + hi + 1) >> 1;
+        if (a.q_start[mid] <= row) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
+
+// Physical block of position `pos` of sequence `s`, or -1 outside the table / pool.
+__device__ __forceinline__ int64_t page_of(const PrefillArgs& a, int s, int pos) {
+    const int idx = a.bs_shift >= 0 ? (pos >> a.bs_shift) : (pos / a.block_size);
+    if (pos < 0 || idx >= a.max_blocks) return -1;
+    const int64_t blk = a.block_table[static_cast<int64_t>(s) * a.max_blocks + idx];
+    return (blk >= 0 && blk < a.num_blocks) ? blk : -1;
+}
+
+__device__ __forceinline__ int in_page(const PrefillArgs& a, int pos) {
+    return a.bs_shift >= 0 ? (pos & (a.block_size - 1)) : (pos % a.block_size);
+}
+
+// kernels/rope.metal:57-63 without contraction; identity outside the table.
+__device__ __forceinline__ void rope_rotate(const PrefillArgs& a, int pos, int i, int half,
+                                            float& x1, float& x2) {
+    if (a.rope_cos == nullptr || pos < 0 || pos >= a.rope_len) return;
+    const float c = __ldg(&a.rope_cos[static_cast<int64_t>(pos) * half + i]);
+    const float s = __ldg(&a.rope_sin[static_cast<int64_t>(pos) * half + i]);
+    const float y1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+    const float y2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+    x1 = y1;
+    x2 = y2;
+}
+
+// ---- append: one thread per (row, KV head, rotation pair) -----------------------------
+template <typename T>
+__global__ void prefill_append_kernel(const PrefillArgs a) {
+    const int half = a.head_dim / 2;
+    const int64_t total = static_cast<int64_t>(a.total_rows) * a.kv_heads * half;
+    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int i = static_cast<int>(idx % half);
+        const int64_t t = idx / half;
+        const int kvh = static_cast<int>(t % a.kv_heads);
+        const int row = static_cast<int>(t / a.kv_heads);
+        const int s = seq_of_row(a, row);
+        int row0;
+        seq_rows(a, s, &row0);
+        const int pos = a.seq_lens[s] + (row - row0);
+        const int64_t blk = page_of(a, s, pos);
+        if (blk < 0) continue;
+        const int64_t src = static_cast<int64_t>(row) * a.kv_stride +
+                            static_cast<int64_t>(kvh) * a.head_dim;
+        const int64_t dst =
+            ((blk * a.kv_heads + kvh) * a.block_size + in_page(a, pos)) * a.head_dim;
+        const T* kn = static_cast<const T*>(a.k_new) + src;
+        const T* vn = static_cast<const T*>(a.v_new) + src;
+        float x1 = to_f32<T>(kn[i]), x2 = to_f32<T>(kn[i + half]);
+        rope_rotate(a, pos + a.rope_off, i, half, x1, x2);
+        T* kd = static_cast<T*>(a.k_cache) + dst;
+        T* vd = static_cast<T*>(a.v_cache) + dst;
+        kd[i] = from_f32<T>(x1);
+        kd[i + half] = from_f32<T>(x2);
+        vd[i] = vn[i];
+        vd[i + half] = vn[i + half];
+    }
+}
+
+// ---- PTX wrappers: mbarrier, TMA, tcgen05 ----------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Waits for the phase of parity `parity` of barrier `bar` to complete.  Gives up (false)
+// when another thread of the CTA already gave up or after kWaitLimitNs, recording
+// TMLLM_TIMEOUT; nothing in a correct run waits longer than microseconds.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned long long t0) {
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_test(bar, parity)) return true;
+        if ((it & 63u) == 63u) {
+            if (*abort_flag) return false;
+            if (global_ns() - t0 > kWaitLimitNs) {
+                *abort_flag = 1;
+                atomicExch(&g_prefill_status, TMLLM_TIMEOUT);
+                return false;
+            }
+        }
+    }
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     bar)
+                 : "memory");
+}
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (F16 operands, F32 accumulator).
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// 32 consecutive F32 columns of this thread's tensor-memory lane, load and wait in one
+// statement so no use of the registers can be scheduled before the data is there.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+        "%28, %29, %30, %31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+        "%28, %29, %30, %31, %32};\n\t"
+        "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Shared-memory matrix descriptor of a K-major or MN-major operand stored as rows of
+// 128 bytes with the 128-byte swizzle (16-byte chunk c of row r at c ^ (r & 7), 8-row groups
+// 1024 bytes apart).  lbo/sbo in bytes: the leading- and stride-dimension offsets.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+    d |= 1ull << 46;  // descriptor version of the 5th-generation tensor cores
+    d |= 2ull << 61;  // 128-byte swizzle
+    return d;
+}
+// Instruction descriptor of kind::f16 with F16 A/B, F32 accumulator, K-major A.
+constexpr uint32_t f16_idesc(int m, int n, bool b_mn_major) {
+    return (1u << 4) | ((b_mn_major ? 1u : 0u) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+template <int D>
+struct TcCfg {
+    static constexpr int BLK = 16384;               // one 64-column block of a 128-row tile
+    static constexpr int NB = D / 64;               // 64-column blocks per row
+    static constexpr int TILE = NB * BLK;           // Q, K or V tile
+    static constexpr int OFF_Q = 0;
+    static constexpr int OFF_K = TILE;              // 2 stages
+    static constexpr int OFF_V = 3 * TILE;          // 2 stages
+    static constexpr int OFF_P = 5 * TILE;          // 128 x 128 F16, two 64-key blocks
+    static constexpr int OFF_BAR = OFF_P + 2 * BLK;
+    static constexpr int SMEM = OFF_BAR + 128;
+    static constexpr int TMEM_COLS = 256;           // S: columns [0,128), O: [128, 128 + D)
+    static constexpr int MIN_BLOCKS = D == 64 ? 2 : 1;
+};
+
+// Barrier slots (8 bytes each) after the tiles, then the tensor-memory address and flags.
+enum : int { BAR_Q = 0, BAR_K0 = 1, BAR_V0 = 3, BAR_S = 5, BAR_P = 6, BAR_O = 7, NBARS = 8 };
+
+template <int D>
+__global__ void __launch_bounds__(kPrefillThreads, TcCfg<D>::MIN_BLOCKS)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
+                      const __grid_constant__ CUtensorMap vmap, const PrefillArgs a) {
+    using Cfg = TcCfg<D>;
+    extern __shared__ __align__(1024) unsigned char smem[];
+    const int tid = threadIdx.x;
+    const int h = blockIdx.x % a.q_heads;
+    const int s = blockIdx.x / a.q_heads;
+    const int tile = gridDim.y - 1 - blockIdx.y;  // the longest tiles start first
+    int row0;
+    const int nrows_seq = seq_rows(a, s, &row0);
+    const int q_lo = tile * kTile;
+    if (q_lo >= nrows_seq) return;  // uniform for the CTA: nothing allocated yet
+    const int rows = min(kTile, nrows_seq - q_lo);
+    const int cached = a.seq_lens[s];
+    const int kv_len = cached + q_lo + rows;  // keys seen by the last row of this tile
+    const int nt = (kv_len + kTile - 1) / kTile;
+    const int kvh = h / a.group;
+
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t bars = sbase + Cfg::OFF_BAR;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::OFF_BAR + NBARS * 8);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::OFF_BAR + NBARS * 8 + 4);
+    auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
+
+    if ((sbase & 1023u) != 0) {  // the swizzle atoms need 1024-byte alignment
+        if (tid == 0) atomicExch(&g_prefill_status, TMLLM_INVALID_ARGUMENT);
+        return;
+    }
+    if (tid == 0) {
+        mbar_init(bar(BAR_Q), kSoftmaxThreads);
+        mbar_init(bar(BAR_K0), 1);
+        mbar_init(bar(BAR_K0 + 1), 1);
+        mbar_init(bar(BAR_V0), 1);
+        mbar_init(bar(BAR_V0 + 1), 1);
+        mbar_init(bar(BAR_S), 1);
+        mbar_init(bar(BAR_P), kSoftmaxThreads);
+        mbar_init(bar(BAR_O), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (tid < 32) {  // warp 0 owns the tensor-memory allocation
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(Cfg::TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tmem_s = tmem;
+    const uint32_t tmem_o = tmem + 128;
+    const unsigned long long t0 = global_ns();
+
+    if (tid == kSoftmaxThreads) {
+        // ================= producer + MMA issuer (one thread) =================
+        const int box_rows = a.block_size < kTile ? a.block_size : kTile;
+        const int nbox = kTile / box_rows;
+        const uint32_t box_bytes = static_cast<uint32_t>(box_rows) * 128u;
+        // Every box of a tile is loaded: a box past the keys or without a page reads rows
+        // beyond the arena, which TMA fills with zeros, so masked keys never meet stale
+        // shared memory (P = 0 times a non-finite V would not be 0).
+        const uint32_t tile_bytes = static_cast<uint32_t>(nbox) * box_bytes * Cfg::NB;
+        auto issue_tile = [&](int t, int st) {
+            const int base = t * kTile;
+            mbar_arrive_tx(bar(BAR_K0 + st), tile_bytes);
+            mbar_arrive_tx(bar(BAR_V0 + st), tile_bytes);
+            const uint32_t kdst = sbase + Cfg::OFF_K + st * Cfg::TILE;
+            const uint32_t vdst = sbase + Cfg::OFF_V + st * Cfg::TILE;
+            for (int b = 0; b < nbox; ++b) {
+                const int pos = base + b * box_rows;
+                const int64_t blk = pos < kv_len ? page_of(a, s, pos) : -1;
+                const int y = blk < 0 ? static_cast<int>(a.arena_rows)
+                                      : static_cast<int>((blk * a.kv_heads + kvh) * a.block_size +
+                                                         in_page(a, pos));
+#pragma unroll
+                for (int c = 0; c < Cfg::NB; ++c) {
+                    const uint32_t off = c * Cfg::BLK + b * box_bytes;
+                    tma_load_2d(kdst + off, &kmap, c * 64, y, bar(BAR_K0 + st));
+                    tma_load_2d(vdst + off, &vmap, c * 64, y, bar(BAR_V0 + st));
+                }
+            }
+        };
+        constexpr uint32_t IDESC_QK = f16_idesc(128, 128, false);
+        constexpr uint32_t IDESC_PV = f16_idesc(128, D, true);
+        auto issue_qk = [&](int st) {
+            const uint32_t qa = sbase + Cfg::OFF_Q, ka = sbase + Cfg::OFF_K + st * Cfg::TILE;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+                const uint32_t off = (kk >> 2) * Cfg::BLK + (kk & 3) * 32;
+                tc_mma(tmem_s, sw128_desc(qa + off, 16, 1024), sw128_desc(ka + off, 16, 1024),
+                       IDESC_QK, kk > 0);
+            }
+        };
+        auto issue_pv = [&](int st, bool acc) {
+            const uint32_t pa = sbase + Cfg::OFF_P, va = sbase + Cfg::OFF_V + st * Cfg::TILE;
+#pragma unroll
+            for (int kk = 0; kk < kTile / 16; ++kk) {
+                const uint32_t aoff = (kk >> 2) * Cfg::BLK + (kk & 3) * 32;
+                tc_mma(tmem_o, sw128_desc(pa + aoff, 16, 1024),
+                       sw128_desc(va + kk * 2048, Cfg::BLK, 1024), IDESC_PV, acc || kk > 0);
+            }
+        };
+        bool ok = true;
+        issue_tile(0, 0);
+        if (nt > 1) issue_tile(1, 1);
+        ok = mbar_wait(bar(BAR_Q), 0, abort_flag, t0) && mbar_wait(bar(BAR_K0), 0, abort_flag, t0);
+        if (ok) {
+            tc_fence_after();
+            issue_qk(0);
+            tc_commit(bar(BAR_S));
+        }
+        for (int j = 0; ok && j < nt; ++j) {
+            const int st = j & 1;
+            ok = mbar_wait(bar(BAR_P), j & 1, abort_flag, t0) &&
+                 mbar_wait(bar(BAR_V0 + st), (j >> 1) & 1, abort_flag, t0);
+            if (!ok) break;
+            tc_fence_after();
+            issue_pv(st, j > 0);
+            tc_commit(bar(BAR_O));
+            if (j + 1 < nt) {
+                ok = mbar_wait(bar(BAR_K0 + (st ^ 1)), ((j + 1) >> 1) & 1, abort_flag, t0);
+                if (!ok) break;
+                tc_fence_after();
+                issue_qk(st ^ 1);
+                tc_commit(bar(BAR_S));
+            }
+            if (j + 2 < nt) {  // stage st is free once P_j V_j has completed
+                ok = mbar_wait(bar(BAR_O), j & 1, abort_flag, t0);
+                if (!ok) break;
+                issue_tile(j + 2, st);
+            }
+        }
+    } else if (tid < kSoftmaxThreads) {
+        // ================= softmax warps: thread r owns query row r =================
+        const int r = tid;
+        const int warp = tid >> 5;
+        const int half = D / 2;
+        const bool live = r < rows;
+        const int prow = row0 + q_lo + (live ? r : rows - 1);
+        const int qpos = cached + q_lo + (live ? r : rows - 1);  // keys 0..qpos are visible
+        // Q row: rotate, round to F16, store swizzled (row r of every 64-column block)
+        {
+            const __half* qr = static_cast<const __half*>(a.q) + static_cast<int64_t>(prow) * a.q_stride +
+                               static_cast<int64_t>(h) * D;
+            unsigned char* qs = smem + Cfg::OFF_Q + r * 128;
+#pragma unroll
+            for (int c = 0; c < D / 16; ++c) {  // chunk c of the first half pairs with c + D/16
+                uint4 u1 = make_uint4(0, 0, 0, 0), u2 = make_uint4(0, 0, 0, 0);
+                if (live) {
+                    u1 = *reinterpret_cast<const uint4*>(qr + c * 8);
+                    u2 = *reinterpret_cast<const uint4*>(qr + half + c * 8);
+                    __half2* h1 = reinterpret_cast<__half2*>(&u1);
+                    __half2* h2 = reinterpret_cast<__half2*>(&u2);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        float2 f1 = __half22float2(h1[e]), f2 = __half22float2(h2[e]);
+                        rope_rotate(a, qpos + a.rope_off, c * 8 + 2 * e, half, f1.x, f2.x);
+                        rope_rotate(a, qpos + a.rope_off, c * 8 + 2 * e + 1, half, f1.y, f2.y);
+                        h1[e] = __floats2half2_rn(f1.x, f1.y);
+                        h2[e] = __floats2half2_rn(f2.x, f2.y);
+                    }
+                }
+                const int c2 = c + D / 16;
+                *reinterpret_cast<uint4*>(qs + (c >> 3) * Cfg::BLK + (((c & 7) ^ (r & 7)) << 4)) = u1;
+                *reinterpret_cast<uint4*>(qs + (c2 >> 3) * Cfg::BLK + (((c2 & 7) ^ (r & 7)) << 4)) = u2;
+            }
+        }
+        fence_async_smem();
+        mbar_arrive(bar(BAR_Q));
+
+        const uint32_t lane_s = tmem_s + (static_cast<uint32_t>(warp * 32) << 16);
+        const uint32_t lane_o = tmem_o + (static_cast<uint32_t>(warp * 32) << 16);
+        unsigned char* prow_s = smem + Cfg::OFF_P + r * 128;
+        float m_used = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nt; ++j) {
+            ok = mbar_wait(bar(BAR_S), j & 1, abort_flag, t0);
+            if (!ok) break;
+            tc_fence_after();
+            const int lim = qpos - j * kTile;  // columns 0..lim of this tile are visible
+            float mx = -INFINITY;
+            float v[32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                tmem_ld32(lane_s + c * 32, v);
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    if (c * 32 + i <= lim) mx = fmaxf(mx, v[i]);
+            }
+            const float mt = mx * a.scale_log2;
+            if (j > 0) {  // P_{j-1} V_{j-1} done: P buffer free, O settled
+                ok = mbar_wait(bar(BAR_O), (j - 1) & 1, abort_flag, t0);
+                if (!ok) break;
+                tc_fence_after();
+            }
+            // Rescale only when the running maximum grew by more than 2^8; otherwise keep
+            // the stale maximum (P stays below 2^8 and the final 1/l makes it exact).  The
+            // tensor-memory accesses are warp-wide, so a warp rescales when any row needs it
+            // (alpha = 1 for the others).
+            const bool need = j > 0 && mt > m_used + 8.f;
+            float alpha = 1.f;
+            if (need) {
+                alpha = fast_exp2(m_used - mt);
+                l *= alpha;
+                m_used = mt;
+            }
+            if (j == 0) m_used = mt;
+            if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+                for (int c = 0; c < D / 32; ++c) {
+                    float o[32];
+                    tmem_ld32(lane_o + c * 32, o);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                    tmem_st32(lane_o + c * 32, o);
+                }
+            }
+            const float neg = -m_used;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                tmem_ld32(lane_s + c * 32, v);
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {  // 8 keys -> one 16-byte chunk of P
+                    uint32_t pk[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int i0 = g * 8 + 2 * e;
+                        const float p0 = (c * 32 + i0 <= lim)
+                                             ? fast_exp2(fmaf(v[i0], a.scale_log2, neg)) : 0.f;
+                        const float p1 = (c * 32 + i0 + 1 <= lim)
+                                             ? fast_exp2(fmaf(v[i0 + 1], a.scale_log2, neg)) : 0.f;
+                        l += p0 + p1;
+                        __half2 hp = __floats2half2_rn(p0, p1);
+                        pk[e] = *reinterpret_cast<uint32_t*>(&hp);
+                    }
+                    const int cc = c * 4 + g;  // chunk 0..15 along the keys
+                    *reinterpret_cast<uint4*>(prow_s + (cc >> 3) * Cfg::BLK +
+                                              (((cc & 7) ^ (r & 7)) << 4)) =
+                        make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            mbar_arrive(bar(BAR_P));
+        }
+        if (ok) ok = mbar_wait(bar(BAR_O), (nt - 1) & 1, abort_flag, t0);
+        if (ok) {
+            tc_fence_after();
+            const float inv = 1.f / l;
+            const int64_t orow = static_cast<int64_t>(prow) * a.out_stride +
+                                 static_cast<int64_t>(h) * D;
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+                float o[32];
+                tmem_ld32(lane_o + c * 32, o);  // warp-wide: every lane loads, live rows store
+                if (live) {
+                    if (a.out_f32) {
+                        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + orow + c * 32);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+                            dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv,
+                                                 o[4 * i + 2] * inv, o[4 * i + 3] * inv);
+                    } else {
+                        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + orow + c * 32);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            uint32_t pk[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                __half2 hv = __floats2half2_rn(o[8 * i + 2 * e] * inv,
+                                                               o[8 * i + 2 * e + 1] * inv);
+                                pk[e] = *reinterpret_cast<uint32_t*>(&hv);
+                            }
+                            dst[i] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (tid < 32) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(Cfg::TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// ---- CUDA-core prefill: one warp per (query row, query head) ---------------------------
+template <typename T>
+__global__ void __launch_bounds__(128) prefill_generic_kernel(const PrefillArgs a) {
+    constexpr int MAXP = 8;  // rotation pairs per lane: head_dim <= 512
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= a.total_rows * a.q_heads) return;
+    const int h = warp % a.q_heads;
+    const int row = warp / a.q_heads;
+    const int s = seq_of_row(a, row);
+    int row0;
+    seq_rows(a, s, &row0);
+    const int qpos = a.seq_lens[s] + (row - row0);
+    const int D = a.head_dim, half = D / 2, kvh = h / a.group;
+    float q1[MAXP], q2[MAXP], o1[MAXP], o2[MAXP];
+    const T* qr = static_cast<const T*>(a.q) + static_cast<int64_t>(row) * a.q_stride +
+                  static_cast<int64_t>(h) * D;
+#pragma unroll
+    for (int k = 0; k < MAXP; ++k) {
+        const int i = lane + 32 * k;
+        q1[k] = q2[k] = o1[k] = o2[k] = 0.f;
+        if (i < half) {
+            float x1 = to_f32<T>(qr[i]), x2 = to_f32<T>(qr[i + half]);
+            rope_rotate(a, qpos + a.rope_off, i, half, x1, x2);
+            q1[k] = round_store<T>(x1);
+            q2[k] = round_store<T>(x2);
+        }
+    }
+    float m = -INFINITY, l = 0.f;
+    for (int j = 0; j <= qpos; ++j) {
+        const int64_t blk = page_of(a, s, j);
+        if (blk < 0) continue;
+        const int64_t off = ((blk * a.kv_heads + kvh) * a.block_size + in_page(a, j)) * D;
+        const T* kr = static_cast<const T*>(a.k_cache) + off;
+        const T* vr = static_cast<const T*>(a.v_cache) + off;
+        float dot = 0.f;
+#pragma unroll
+        for (int k = 0; k < MAXP; ++k) {
+            const int i = lane + 32 * k;
+            if (i < half) dot += q1[k] * to_f32<T>(kr[i]) + q2[k] * to_f32<T>(kr[i + half]);
+        }
+        dot = warp_sum(dot) * a.scale_log2;
+        const float mn = fmaxf(m, dot);
+        const float corr = exp2f(m - mn), p = exp2f(dot - mn);
+        l = l * corr + p;
+        m = mn;
+#pragma unroll
+        for (int k = 0; k < MAXP; ++k) {
+            const int i = lane + 32 * k;
+            if (i < half) {
+                o1[k] = o1[k] * corr + p * to_f32<T>(vr[i]);
+                o2[k] = o2[k] * corr + p * to_f32<T>(vr[i + half]);
+            }
+        }
+    }
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const int64_t orow = static_cast<int64_t>(row) * a.out_stride + static_cast<int64_t>(h) * D;
+#pragma unroll
+    for (int k = 0; k < MAXP; ++k) {
+        const int i = lane + 32 * k;
+        if (i >= half) continue;
+        if (a.out_f32) {
+            static_cast<float*>(a.out)[orow + i] = o1[k] * inv;
+            static_cast<float*>(a.out)[orow + i + half] = o2[k] * inv;
+        } else {
+            static_cast<T*>(a.out)[orow + i] = from_f32<T>(o1[k] * inv);
+            static_cast<T*>(a.out)[orow + i + half] = from_f32<T>(o2[k] * inv);
+        }
+    }
+}
+
+// ---- host ----------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000,
+                                             cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        cudaGetLastError();
+    });
+    return fn;
+}
+
+// 2-D map over one arena viewed as rows of D halves; boxes of 64 columns x box_rows rows,
+// 128-byte swizzle (the layout the tensor-core descriptors read).
+int make_arena_map(CUtensorMap* map, void* arena, int64_t rows, int D, int box_rows) {
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return fail(TMLLM_DEVICE_ERROR, "cuTensorMapEncodeTiled is not available");
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(D) * 2};
+    const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, arena, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(TMLLM_DEVICE_ERROR, "tensor map encoding failed (CUresult %d)", static_cast<int>(r));
+    return TMLLM_OK;
+}
+
+template <int D>
+int launch_tc(const PrefillArgs& a, int64_t arena_rows, int max_rows, cudaStream_t s) {
+    using Cfg = TcCfg<D>;
+    const int box_rows = a.block_size < kTile ? a.block_size : kTile;
+    CUtensorMap kmap, vmap;
+    if (int st = make_arena_map(&kmap, a.k_cache, arena_rows, D, box_rows)) return st;
+    if (int st = make_arena_map(&vmap, a.v_cache, arena_rows, D, box_rows)) return st;
+    static std::once_flag once[64];
+    int dev = 0;
+    TMLLM_CUDA_TRY(cudaGetDevice(&dev));
+    cudaError_t attr = cudaSuccess;
+    std::call_once(once[dev & 63], [&] {
+        attr = cudaFuncSetAttribute(prefill_tc_kernel<D>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    });
+    if (attr != cudaSuccess) return cuda_fail(attr, "prefill shared-memory attribute");
+    dim3 grid(static_cast<unsigned>(a.q_heads * a.num_seqs),
+              static_cast<unsigned>((max_rows + kTile - 1) / kTile));
+    prefill_tc_kernel<D><<<grid, kPrefillThreads, Cfg::SMEM, s>>>(kmap, vmap, a);
+    TMLLM_LAUNCH_TRY();
+    return TMLLM_OK;
+}
+
+}  // namespace
+
+int prefill_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, const void* v_new,
+                 const int32_t* q_start, int32_t rows_per_seq, int32_t max_rows,
+                 int32_t total_rows, void* out, int32_t q_heads, const tmllm_decode_opts* opts,
+                 cudaStream_t stream) {
+    if (!kv) return fail(TMLLM_INVALID_ARGUMENT, "null paged KV descriptor");
+    if (!valid_dtype(kv->dtype)) return fail(TMLLM_UNSUPPORTED_DTYPE, "unknown cache dtype");
+    const int D = kv->head_dim, Hkv = kv->num_kv_heads, B = kv->num_seqs;
+    if (B <= 0 || Hkv <= 0 || D <= 0 || kv->block_size <= 0 || kv->max_blocks_per_seq <= 0 ||
+        kv->num_blocks <= 0)
+        return fail(TMLLM_INVALID_SHAPE, "paged KV dimensions must be positive");
+    if (D % 2 != 0 || D > 512)
+        return fail(TMLLM_INVALID_SHAPE, "head_dim must be even and <= 512, got %d", D);
+    if (q_heads <= 0 || q_heads % Hkv != 0)
+        return fail(TMLLM_MODEL_FORMAT, "Q heads %d must be divisible by non-zero KV heads %d",
+                    q_heads, Hkv);
+    if (rows_per_seq < 0 || max_rows < 0 || total_rows < 0)
+        return fail(TMLLM_INVALID_SHAPE, "row counts must be non-negative");
+    if (!q_start) {
+        int64_t tot;
+        if (!mul_ok(rows_per_seq, B, &tot) || tot > INT32_MAX)
+            return fail(TMLLM_INVALID_SHAPE, "total rows exceed i32");
+        total_rows = static_cast<int32_t>(tot);
+        max_rows = rows_per_seq;
+    }
+    if (total_rows == 0 || max_rows == 0) return TMLLM_OK;
+    if (!q || !k_new || !v_new || !out || !kv->k_cache || !kv->v_cache || !kv->block_table ||
+        !kv->seq_lens)
+        return fail(TMLLM_INVALID_ARGUMENT, "null tensor pointer");
+    tmllm_decode_opts o{};
+    if (opts) o = *opts;
+    if (o.variant < 0 || o.variant > 2)
+        return fail(TMLLM_INVALID_ARGUMENT, "unknown prefill variant %d", o.variant);
+    if (o.out_f32 != 0 && o.out_f32 != 1)
+        return fail(TMLLM_INVALID_ARGUMENT, "out_f32 must be 0 or 1");
+    if (o.rope_cos && (!o.rope_sin || o.rope_len <= 0))
+        return fail(TMLLM_INVALID_ARGUMENT, "RoPE needs both tables and a positive length");
+    const float scale = o.scale > 0.f ? o.scale : 1.0f / sqrtf(static_cast<float>(D));
+    if (!std::isfinite(scale))
+        return fail(TMLLM_INVALID_SHAPE, "attention scale must be positive and finite");
+    if (o.q_seq_stride < 0 || o.kv_seq_stride < 0 ||
+        (o.q_seq_stride > 0 && o.q_seq_stride < static_cast<int64_t>(q_heads) * D) ||
+        (o.kv_seq_stride > 0 && o.kv_seq_stride < static_cast<int64_t>(Hkv) * D))
+        return fail(TMLLM_INVALID_SHAPE, "row strides of q / k_new must cover a row");
+    const size_t es = dtype_size(kv->dtype);
+    auto misaligned = [es](const void* p) { return (reinterpret_cast<uintptr_t>(p) % es) != 0; };
+    if (misaligned(kv->k_cache) || misaligned(kv->v_cache) || misaligned(q) ||
+        misaligned(k_new) || misaligned(v_new) || misaligned(out))
+        return fail(TMLLM_INVALID_ARGUMENT, "tensor pointers must be aligned to their element size");
+
+    int bs_shift = -1;
+    if ((kv->block_size & (kv->block_size - 1)) == 0) {
+        bs_shift = 0;
+        while ((1 << bs_shift) < kv->block_size) ++bs_shift;
+    }
+    PrefillArgs a{};
+    a.q = q;
+    a.k_new = k_new;
+    a.v_new = v_new;
+    a.k_cache = kv->k_cache;
+    a.v_cache = kv->v_cache;
+    a.out = out;
+    a.block_table = kv->block_table;
+    a.seq_lens = kv->seq_lens;
+    a.q_start = q_start;
+    a.rope_cos = o.rope_cos;
+    a.rope_sin = o.rope_sin;
+    a.num_blocks = kv->num_blocks;
+    a.q_stride = o.q_seq_stride > 0 ? o.q_seq_stride : static_cast<int64_t>(q_heads) * D;
+    a.kv_stride = o.kv_seq_stride > 0 ? o.kv_seq_stride : static_cast<int64_t>(Hkv) * D;
+    a.out_stride = static_cast<int64_t>(q_heads) * D;
+    a.uniform_rows = rows_per_seq;
+    a.num_seqs = B;
+    a.total_rows = total_rows;
+    a.q_heads = q_heads;
+    a.kv_heads = Hkv;
+    a.group = q_heads / Hkv;
+    a.head_dim = D;
+    a.block_size = kv->block_size;
+    a.bs_shift = bs_shift;
+    a.max_blocks = kv->max_blocks_per_seq;
+    a.rope_len = o.rope_len;
+    a.rope_off = o.rope_pos_offset;
+    a.out_f32 = o.out_f32 || kv->dtype == TMLLM_F32;
+    a.scale_log2 = scale * kLog2eP;
+
+    // the attention path, decided before anything is enqueued
+    int64_t arena_rows = 0;
+    const bool rows_fit = mul_ok(kv->num_blocks, static_cast<int64_t>(Hkv) * kv->block_size,
+                                 &arena_rows) && arena_rows <= INT32_MAX - kTile;
+    const bool tc_shape = kv->dtype == TMLLM_F16 && (D == 64 || D == 128) && bs_shift >= 4 &&
+                          rows_fit && aligned16(kv->k_cache) && aligned16(kv->v_cache) &&
+                          aligned16(q) && aligned16(out) && (a.q_stride % 8) == 0 &&
+                          o.variant != 1;
+    if (o.variant == 2 && !tc_shape)
+        return fail(TMLLM_INVALID_ARGUMENT,
+                    "the tensor-core prefill needs F16, head_dim 64/128, power-of-two pages of "
+                    ">= 16 positions and 16-byte aligned q/out/arenas");
+    // 1. append (rotated keys, values) at each sequence's cached length
+    {
+        const int64_t work = static_cast<int64_t>(total_rows) * Hkv * (D / 2);
+        int64_t blocks = (work + 255) / 256;
+        const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
+        if (blocks > cap) blocks = cap;
+        if (kv->dtype == TMLLM_F16)
+            prefill_append_kernel<__half><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
+        else
+            prefill_append_kernel<float><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
+        TMLLM_LAUNCH_TRY();
+    }
+    // 2. attention over the cache, new rows included
+    if (tc_shape) {
+        a.arena_rows = arena_rows;
+        const int64_t ctas = static_cast<int64_t>(q_heads) * B;
+        if (ctas > INT32_MAX) return fail(TMLLM_INVALID_SHAPE, "too many sequences x heads");
+        return D == 64 ? launch_tc<64>(a, arena_rows, max_rows, stream)
+                       : launch_tc<128>(a, arena_rows, max_rows, stream);
+    }
+    const int64_t warps = static_cast<int64_t>(total_rows) * q_heads;
+    if (warps > INT32_MAX) return fail(TMLLM_INVALID_SHAPE, "too many rows x heads");
+    const unsigned blocks = static_cast<unsigned>((warps + 3) / 4);
+    if (kv->dtype == TMLLM_F16)
+        prefill_generic_kernel<__half><<<blocks, 128, 0, stream>>>(a);
+    else
+        prefill_generic_kernel<float><<<blocks, 128, 0, stream>>>(a);
+    TMLLM_LAUNCH_TRY();
+    return TMLLM_OK;
+}
+
+}  // namespace tmllm
+
+using namespace tmllm;
+
+extern "C" {
+
+int tmllm_gqa_prefill(const tmllm_paged_kv* kv, const void* q, const void* k_new,
+                      const void* v_new, const int32_t* q_start, int32_t rows_per_seq,
+                      int32_t max_rows, int32_t total_rows, void* out, int32_t q_heads,
+                      const tmllm_decode_opts* opts, tmllm_stream stream) {
+    clear_error();
+    return prefill_impl(kv, q, k_new, v_new, q_start, rows_per_seq, max_rows, total_rows, out,
+                        q_heads, opts, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int tmllm_prefill_status(int32_t* status) {
+    clear_error();
+    if (!status) return fail(TMLLM_INVALID_ARGUMENT, "null status pointer");
+    int v = 0, zero = 0;
+    TMLLM_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_prefill_status, sizeof(int)));
+    TMLLM_CUDA_TRY(cudaMemcpyToSymbol(g_prefill_status, &zero, sizeof(int)));
+    *status = v;
+    return TMLLM_OK;
+}
+
+}  // extern "C"

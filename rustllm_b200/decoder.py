@@ -190,8 +190,57 @@ class Decoder:
             raise _lib.InvalidArgument(f"token id outside the vocabulary of {self.cfg.vocab_size}")
 
     def prefill(self, prompts: torch.Tensor) -> torch.Tensor:
-        """Feeds prompts [B, S] token by token (each position through the fused decode
-        path, which is exact causal attention), returns the greedy token after the prompt."""
+        """Runs prompts [B, S] through the model in one pass per layer (the reference's
+        forward_with_cache with S new tokens, transformer/cache.rs:59-70): every GEMM takes
+        all B*S rows, and attention is the fused append + causal prefill kernel
+        (tmllm_cache_prefill).  Fills the cache, advances every length by S and returns the
+        greedy token after each prompt (logits of the last row, ``self.logits``)."""
+        self.check_ids(prompts)
+        B, S = prompts.shape
+        if B != self.B:
+            raise _lib.ShapeMismatch(f"prefill expects {self.B} prompts, got {B}")
+        cfg, w = self.cfg, self.w
+        T = B * S
+        h, d = cfg.hidden_size, cfg.head_dim
+        hq, hkv = cfg.num_heads, cfg.num_kv_heads
+        e = dict(dtype=self.dtype, device=self.device)
+        ids = prompts.reshape(-1).to(device=self.device, dtype=torch.int32).contiguous()
+        x, hn = torch.empty((T, h), **e), torch.empty((T, h), **e)
+        qkv = torch.empty((T, (hq + 2 * hkv) * d), **e)
+        attn, o = torch.empty((T, hq, d), **e), torch.empty((T, h), **e)
+        gu = torch.empty((T, 2 * cfg.intermediate_size), **e)
+        act = torch.empty((T, cfg.intermediate_size), **e)
+        down = torch.empty((T, h), **e)
+        sp = stream_ptr(self.device)
+        call("tmllm_embedding", self.dt, w.embedding.data_ptr(), ids.data_ptr(), x.data_ptr(),
+             T, h, cfg.vocab_size, self.bad.data_ptr(), sp)
+        residual = None
+        for li, L in enumerate(w.layers):
+            self._norm(x, residual, L["attn_norm"], hn, x)
+            torch.matmul(hn, L["wqkv"], out=qkv)
+            self.cache.prefill(li, qkv[:, :hq * d].view(T, hq, d),
+                               qkv[:, hq * d:(hq + hkv) * d].view(T, hkv, d),
+                               qkv[:, (hq + hkv) * d:].view(T, hkv, d), out=attn, rope=self.rope)
+            torch.matmul(attn.view(T, -1), L["wo"], out=o)
+            self._norm(x, o, L["mlp_norm"], hn, x)
+            torch.matmul(hn, L["wgu"], out=gu)
+            call("tmllm_swiglu", self.dt, gu.data_ptr(), act.data_ptr(), T,
+                 cfg.intermediate_size, sp)
+            torch.matmul(act, L["wd"], out=down)
+            residual = down
+        # only each prompt's last row reaches the head
+        last = torch.arange(S - 1, T, S, device=self.device)
+        self.x.copy_(x.index_select(0, last))
+        self._norm(self.x, down.index_select(0, last), w.final_norm, self.hn, None)
+        torch.matmul(self.hn, w.lm_head, out=self.logits)
+        call("tmllm_argmax", self.dt, self.logits.data_ptr(), self.next_ids.data_ptr(), self.B,
+             cfg.vocab_size, sp)
+        self.cache.advance(S)
+        return self.next_ids.clone()
+
+    def prefill_stepwise(self, prompts: torch.Tensor) -> torch.Tensor:
+        """Feeds prompts [B, S] token by token through the decode step (each position is
+        one fused decode call); the same result as ``prefill`` up to F16 rounding."""
         self.check_ids(prompts)
         B, S = prompts.shape
         self.max_len_hint = max(self.cache.lens()) + S

@@ -195,6 +195,50 @@ class PagedKvCache:
         return (out, lse) if (want_lse or lse is not None) else out
 
 
+    def prefill(self, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, *,
+                out: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
+                scale: float = 0.0, rope=None, rope_pos_offset: int = 0, variant: int = 0):
+        """Fused append + causal attention of ``n`` new tokens for every sequence.
+
+        q [num_seqs, n, Hq, D]; k_new, v_new [num_seqs, n, Hkv, D] (or the same as
+        [num_seqs * n, heads, D] row-strided views).  Token i of sequence s is appended at
+        its length + i and attends positions [0, length + i].  Returns out
+        [num_seqs * n, Hq, D].  Lengths are not advanced; call ``advance(n)`` after the last
+        layer."""
+        if q.dtype != self.dtype:
+            raise _lib.UnsupportedDType(
+                f"SelfAttention/cache dtype mismatch: attention={q.dtype}, cache={self.dtype}")
+        if q.dim() == 4:
+            q, k_new, v_new = (t.reshape(-1, t.shape[2], t.shape[3]) for t in (q, k_new, v_new))
+        rows, hq, d = q.shape
+        if rows % self.num_seqs or d != self.head_dim:
+            raise _lib.ModelFormat(f"prefill expects [num_seqs * n, Hq, {self.head_dim}] rows, "
+                                   f"got {list(q.shape)}")
+        n = rows // self.num_seqs
+        from .attention import _row_stride
+        qs = _row_stride(q, hq, d, "q")
+        ks = _row_stride(k_new, self.num_kv_heads, d, "k_new")
+        if (_row_stride(v_new, self.num_kv_heads, d, "v_new") != ks or k_new.dtype != self.dtype
+                or v_new.dtype != self.dtype or k_new.shape[0] != rows or v_new.shape[0] != rows):
+            raise _lib.ModelFormat("k_new/v_new must be [rows, Hkv, D] in the cache dtype with "
+                                   "one row stride")
+        if out is None:
+            out = torch.empty((rows, hq, d), dtype=out_dtype or self.dtype, device=self.device)
+        if out.dtype not in (self.dtype, torch.float32) or tuple(out.shape) != (
+                rows, hq, d) or not out.is_contiguous():
+            raise _lib.InvalidArgument("out must be a contiguous [rows, Hq, D] tensor in the "
+                                       "cache dtype or F32")
+        opts = DecodeOpts(scale=scale, out_f32=int(out.dtype == torch.float32),
+                          rope_pos_offset=rope_pos_offset, variant=variant, q_seq_stride=qs,
+                          kv_seq_stride=ks)
+        if rope is not None:
+            cos, sin = rope
+            opts.rope_cos, opts.rope_sin, opts.rope_len = cos.data_ptr(), sin.data_ptr(), cos.shape[0]
+        call("tmllm_cache_prefill", self._h, layer, q.data_ptr(), k_new.data_ptr(),
+             v_new.data_ptr(), n, out.data_ptr(), hq, C.byref(opts), self._stream())
+        return out
+
+
 class LayerKvCache:
     """src/model/kv_cache.rs:9-143 — one layer, one sequence.
 

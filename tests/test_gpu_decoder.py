@@ -135,3 +135,35 @@ def test_invalid_prompt_token_rejected(cuda):
     dec = Decoder(TINY, w, 1, device=cuda)
     with pytest.raises(rb.InvalidArgument):
         dec.prefill(torch.tensor([[1, TINY.vocab_size]], device=cuda))
+
+
+def test_prefill_logits_match_float32_model(cuda):
+    """Whole-prompt prefill (one pass per layer through the fused prefill attention) of two
+    prompts of 150 tokens: the last row's logits equal the float32 model's."""
+    w = DecoderWeights(TINY, device=cuda, seed=7, std=0.08)
+    g = torch.Generator().manual_seed(8)
+    prompts = torch.randint(0, TINY.vocab_size, (2, 150), generator=g)
+    dec = Decoder(TINY, w, 2, device=cuda, max_seq_len=160, shuffle_seed=4)
+    nxt = dec.prefill(prompts.to(cuda))
+    assert dec.cache.lens() == [150, 150]
+    for s in range(2):
+        want = reference_forward(TINY, w, prompts[s].to(cuda))[-1]
+        assert rel(dec.logits[s], want) < 3e-2
+        assert int(nxt[s]) == int(dec.logits[s].float().argmax())
+
+
+def test_prefill_then_decode_matches_stepwise(cuda):
+    """Decoding after a whole-prompt prefill gives the logits of decoding after a
+    token-by-token prefill."""
+    w = DecoderWeights(TINY, device=cuda, seed=11, std=0.08)
+    prompts = torch.randint(0, TINY.vocab_size, (2, 40), generator=torch.Generator().manual_seed(12))
+    a = Decoder(TINY, w, 2, device=cuda)
+    b = Decoder(TINY, w, 2, device=cuda)
+    a.prefill(prompts.to(cuda))
+    b.prefill_stepwise(prompts.to(cuda))
+    assert rel(a.logits, b.logits) < 2e-2
+    nxt = torch.tensor([3, 5], dtype=torch.int32, device=cuda)
+    for dec in (a, b):
+        dec.ids.copy_(nxt)
+        dec.forward_step()
+    assert rel(a.logits, b.logits) < 2e-2
