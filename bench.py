@@ -418,6 +418,7 @@ def run_decoder(args) -> None:
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     preset, total_seqs, prompt, steps, desc = DECODER_WORKLOADS[args.workload]
+    prefill_ms = None
     cfg = PRESETS[preset]
     gen = torch.Generator().manual_seed(1234)
     if args.workload == "cfg3":
@@ -444,7 +445,15 @@ def run_decoder(args) -> None:
         first = torch.randint(0, cfg.vocab_size, (B,), generator=gen).to(dev, torch.int32)
     else:
         prompts = torch.randint(0, cfg.vocab_size, (B, prompt), generator=gen).to(dev)
-        first = dec.prefill(prompts)
+        first = dec.prefill(prompts)  # warm-up (library heuristics, allocations)
+        torch.cuda.synchronize()
+        dec.cache.reset()
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record()
+        first = dec.prefill(prompts)  # whole-prompt prefill of every sequence, all layers
+        p1.record()
+        torch.cuda.synchronize()
+        prefill_ms = p0.elapsed_time(p1)
     dec.ids.copy_(first)
     runner = GraphedDecoder(dec, args.warmup + steps)
     for _ in range(args.warmup):
@@ -495,6 +504,204 @@ def run_decoder(args) -> None:
                          "scope": "whole decode step on rank 0: weights + K/V read per step"},
             "clocks": clocks,
         }
+        if prefill_ms is not None:
+            line["prefill"] = {"ms": prefill_ms, "tok_s": B * prompt / (prefill_ms * 1e-3),
+                               "scope": f"{B} prompts x {prompt} tokens, whole model (GEMMs "
+                                        f"+ fused prefill attention), one pass per layer"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------------------------
+# Prefill workload (BASELINE config 5's prompt phase): the tensor-core prefill attention
+# ------------------------------------------------------------------------------------
+
+P_SEQS, P_LEN, P_HEADS, P_D, P_LAYERS = 16, 512, 12, 64, 12
+
+
+def prefill_flops(seqs: int = P_SEQS, n: int = P_LEN, heads: int = P_HEADS, d: int = P_D,
+                  cached: int = 0) -> float:
+    """Algorithmic FLOPs of one causal prefill launch: query row i attends cached + i + 1
+    keys; each (query, key) pair costs 2*D for Q.K and 2*D for P.V."""
+    pairs = n * cached + n * (n + 1) // 2
+    return 4.0 * d * pairs * heads * seqs
+
+
+def run_prefill(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import rustllm_b200 as rb
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    B, S, H, d, NL = P_SEQS, P_LEN, P_HEADS, P_D, P_LAYERS
+    T = B * S
+    cache = rb.PagedKvCache(NL, B, S, H, d, dtype=torch.float16, block_size=16,
+                            shuffle_seed=31 + rank, device=dev)
+    for s in range(B):
+        cache.reserve(s, S)
+    rope = rb.rope_tables(d, S + 1, 10000.0, device=dev)
+    g = torch.Generator(device=dev).manual_seed(500 + rank)
+    # per-layer inputs (3 x 12.6 MB each, 453 MB over the 12 layers: larger than L2)
+    qs = [torch.randn((T, H, d), generator=g, device=dev).half() for _ in range(NL)]
+    ks = [torch.randn((T, H, d), generator=g, device=dev).half() for _ in range(NL)]
+    vs = [torch.randn((T, H, d), generator=g, device=dev).half() for _ in range(NL)]
+    outs = [torch.empty((T, H, d), dtype=torch.float16, device=dev) for _ in range(NL)]
+    views = [cache.view(li) for li in range(NL)]
+    stream = torch.cuda.current_stream(dev)
+    # the C entry point with arguments prepared once (the Python wrapper's checks would
+    # otherwise keep the GPU waiting on the host between these ~10 us launches)
+    import ctypes as C
+
+    from rustllm_b200 import _lib
+    lib = _lib.load()
+    opts = _lib.DecodeOpts(rope_cos=rope[0].data_ptr(), rope_sin=rope[1].data_ptr(),
+                           rope_len=rope[0].shape[0], q_seq_stride=H * d, kv_seq_stride=H * d)
+    sp = stream.cuda_stream
+    calls = [(C.byref(views[li]), qs[li].data_ptr(), ks[li].data_ptr(), vs[li].data_ptr(),
+              outs[li].data_ptr()) for li in range(NL)]
+    fn = lib.tmllm_gqa_prefill
+
+    def launch(li, append=True):
+        kv, q, k, v, o = calls[li]
+        rc = fn(kv, q, k if append else None, v if append else None, None, S, 0, 0, o, H,
+                C.byref(opts), sp)
+        if rc:
+            _lib.check(rc)
+
+    def step(append=True):  # lengths stay 0: every step rewrites the same positions
+        for li in range(NL):
+            launch(li, append)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if rb.prefill_status() != 0:
+        raise SystemExit("prefill kernel reported an expired wait")
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    # (1) the hot path as a step: append + attention for all 12 layers
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall0 = time.time()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    # (2) the attention kernel alone, per launch (attend-only calls)
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps * NL)]
+    i = 0
+    for _ in range(args.steps):
+        for li in range(NL):
+            kev[i][0].record(stream)
+            launch(li, append=False)
+            kev[i][1].record(stream)
+            i += 1
+    torch.cuda.synchronize()
+    wall1 = time.time()
+    clocks = sampler.stop(wall0, wall1) if sampler else None
+    ms = e0.elapsed_time(e1)
+    k_ms = sum(a.elapsed_time(b) for a, b in kev) / len(kev)
+    t = torch.tensor([ms, k_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, k_ms = float(t[0]), float(t[1])
+    ms_step = ms / args.steps
+    step_flops = prefill_flops() * NL
+    value = step_flops * world / (ms_step * 1e-3) / 1e12
+    achieved = prefill_flops() / (k_ms * 1e-3) / 1e12
+
+    # e2e: per-layer q/k/v from pinned host memory, outputs back to the host
+    hq = [x.cpu().pin_memory() for x in qs[:2]]
+    hk = [x.cpu().pin_memory() for x in ks[:2]]
+    hv = [x.cpu().pin_memory() for x in vs[:2]]
+    ho = torch.empty((T, H, d), dtype=torch.float16).pin_memory()
+    dq, dk, dv = torch.empty_like(qs[0]), torch.empty_like(ks[0]), torch.empty_like(vs[0])
+
+    def e2e_step():
+        for li in range(NL):
+            dq.copy_(hq[li % 2], non_blocking=True)
+            dk.copy_(hk[li % 2], non_blocking=True)
+            dv.copy_(hv[li % 2], non_blocking=True)
+            rb.gqa_prefill(views[li], dq, dk, dv, rows_per_seq=S, out=outs[li], rope=rope)
+            ho.copy_(outs[li], non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    e_steps = max(1, min(args.steps, 20))
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(e_steps):
+        e2e_step()
+    f1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([f0.elapsed_time(f1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e = step_flops * world * e_steps / (float(te[0]) * 1e-3) / 1e12
+    if rb.prefill_status() != 0:
+        raise SystemExit("prefill kernel reported an expired wait")
+
+    if rank == 0:
+        peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+        peak, src = 1590.0, "fallback"
+        if os.path.exists(peaks_path):
+            with open(peaks_path) as f:
+                peak, src = float(json.load(f)["bf16_tflops"]), "measured (burst)"
+        line = {
+            "metric": "prefill attention TFLOP/s (fused append + causal tcgen05 attention)",
+            "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded N(0,1) q, k, v per layer)",
+            "config": {"workload": "cfg5 prompt phase: TinyStories-110M attention shape, 16 "
+                                   "prompts x 512 tokens, 12 layers (MHA 12 heads, D=64), "
+                                   "16-token pages",
+                       "tokens_per_step": T, "layers": NL,
+                       "parallelism": f"replicas{world}" if world > 1 else "1gpu",
+                       "l2": "per-layer inputs, 453 MB per step: larger than L2"},
+            "prefill_tok_s": T * world / (ms_step * 1e-3),
+            "gpu_launches": args.steps * NL * 2,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "peak_source": src,
+                         "traffic": None, "kernel": "prefill_tc_kernel<64>",
+                         "kernel_ms": k_ms, "flops_per_launch": prefill_flops()},
+            "e2e": {"value": e2e, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": NL * 3 * T * H * d * 2,
+                    "d2h_bytes_per_step": NL * T * H * d * 2},
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu:
+            from oracle import oracle as orc
+            orc.build()
+            threads = os.cpu_count() or 1
+            qn = qs[0][:S].float().cpu().numpy().transpose(1, 0, 2)[None].astype("float16")
+            kn = ks[0][:S].float().cpu().numpy().transpose(1, 0, 2)[None].astype("float16")
+            vn = vs[0][:S].float().cpu().numpy().transpose(1, 0, 2)[None].astype("float16")
+            import numpy as np
+            qn, kn, vn = (np.ascontiguousarray(x) for x in (qn, kn, vn))
+            n_done, c0 = 0, time.perf_counter()
+            while time.perf_counter() - c0 < args.cpu_budget:
+                orc.attention_core(qn, kn, vn, S, 0, threads=threads)
+                n_done += 1
+            secs = time.perf_counter() - c0
+            cpu_tflops = prefill_flops(seqs=1) * n_done / secs / 1e12
+            line["cpu_baseline"] = {
+                "value": cpu_tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                "sample": f"{n_done} one-sequence one-layer prefills (12 heads x 512 rows, the "
+                          f"reference's faithful F16 op chain), time-boxed to "
+                          f"{args.cpu_budget:.0f} s"}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -510,8 +717,10 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--ref-budget", type=float, default=60.0)
-    ap.add_argument("--workload", choices=["cfg4", "cfg2", "cfg3", "cfg5"], default="cfg4",
-                    help="cfg4 (default): the fused attention op; cfg2/3/5: whole-model decode")
+    ap.add_argument("--workload", choices=["cfg4", "cfg2", "cfg3", "cfg5", "cfg5p"],
+                    default="cfg4",
+                    help="cfg4 (default): the fused attention op; cfg2/3/5: whole-model "
+                         "decode; cfg5p: config 5's prefill attention")
     ap.add_argument("--variant", type=int, default=0,
                     help="decode kernel: 0 auto (tensor-core for F16), 1 CUDA-core, 2 tensor-core")
     ap.add_argument("--splits", type=int, default=0, help="split count (0 = automatic)")
@@ -526,6 +735,8 @@ def main() -> None:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "cfg5p":
+        run_prefill(args)
     elif args.workload != "cfg4":
         run_decoder(args)
     else:

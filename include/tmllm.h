@@ -270,7 +270,8 @@ int tmllm_gqa_decode_noalloc(const tmllm_paged_kv* kv, const void* q, const void
  * [0, seq_lens[s] + i] (attention_scale_mask.metal:21-41).
  *   q      [total_rows, q_heads, head_dim]       (cache dtype; row stride opts->q_seq_stride)
  *   k_new  [total_rows, num_kv_heads, head_dim]  appended at seq_lens[s] + i
- *   v_new  [total_rows, num_kv_heads, head_dim]  (row stride opts->kv_seq_stride)
+ *   v_new  [total_rows, num_kv_heads, head_dim]  (row stride opts->kv_seq_stride); both
+ *          NULL = attend only: those positions already hold the rows
  *   out    [total_rows, q_heads, head_dim]       (cache dtype, or F32 if opts->out_f32)
  * Rows are grouped by sequence.  q_start (device, int32 [num_seqs + 1]) gives each
  * sequence's first row; with q_start == NULL every sequence has rows_per_seq rows and

@@ -101,7 +101,8 @@ def _row_stride(t: torch.Tensor, heads: int, d: int, what: str) -> int:
     return t.stride(0)
 
 
-def gqa_prefill(kv: PagedKV, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, *,
+def gqa_prefill(kv: PagedKV, q: torch.Tensor, k_new: torch.Tensor | None,
+                v_new: torch.Tensor | None, *,
                 q_start: torch.Tensor | None = None, rows_per_seq: int = 0, max_rows: int = 0,
                 out: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
                 scale: float = 0.0, rope=None, rope_pos_offset: int = 0,
@@ -111,13 +112,19 @@ def gqa_prefill(kv: PagedKV, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.
     q [rows, Hq, D], k_new / v_new [rows, Hkv, D] (row-strided views allowed), rows grouped
     by sequence: ``q_start`` int32 [num_seqs + 1] row offsets on the device, or None with
     ``rows_per_seq`` rows per sequence.  Row i of sequence s is appended at seq_lens[s] + i
-    and attends keys [0, seq_lens[s] + i].  Returns out [rows, Hq, D]."""
+    and attends keys [0, seq_lens[s] + i]; with k_new = v_new = None nothing is appended
+    (those positions already hold the rows).  Returns out [rows, Hq, D]."""
     rows, hq, d = q.shape
     hkv = kv.num_kv_heads
     qs = _row_stride(q, hq, d, "q")
-    ks = _row_stride(k_new, hkv, d, "k_new")
-    if _row_stride(v_new, hkv, d, "v_new") != ks or k_new.shape[0] != rows or v_new.shape[0] != rows:
-        raise _lib.ShapeMismatch("k_new and v_new must have q's rows and the same row stride")
+    ks = 0
+    if (k_new is None) != (v_new is None):
+        raise _lib.InvalidArgument("k_new and v_new must both be given or both be None")
+    if k_new is not None:
+        ks = _row_stride(k_new, hkv, d, "k_new")
+        if (_row_stride(v_new, hkv, d, "v_new") != ks or k_new.shape[0] != rows
+                or v_new.shape[0] != rows):
+            raise _lib.ShapeMismatch("k_new and v_new must have q's rows and the same row stride")
     if out is None:
         out = torch.empty((rows, hq, d), dtype=out_dtype or q.dtype, device=q.device)
     if (out.dtype not in (q.dtype, torch.float32) or tuple(out.shape) != (rows, hq, d)
@@ -140,7 +147,9 @@ def gqa_prefill(kv: PagedKV, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.
         if rows_per_seq * kv.num_seqs != rows:
             raise _lib.ShapeMismatch(f"{rows} rows are not {kv.num_seqs} x {rows_per_seq}")
         qp = None
-    call("tmllm_gqa_prefill", C.byref(kv), q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), qp,
+    call("tmllm_gqa_prefill", C.byref(kv), q.data_ptr(),
+         k_new.data_ptr() if k_new is not None else None,
+         v_new.data_ptr() if v_new is not None else None, qp,
          rows_per_seq, max_rows, rows, out.data_ptr(), hq, C.byref(opts), stream_ptr(q.device))
     return out
 

@@ -32,7 +32,7 @@ namespace {
 constexpr float kLog2eP = 1.4426950408889634f;
 constexpr int kTile = 128;            // query rows per CTA and keys per tile
 constexpr int kSoftmaxThreads = 128;  // warps 0-3: one thread per query row
-constexpr int kPrefillThreads = 160;  // + warp 4: TMA producer and MMA issuer (one lane)
+constexpr int kPrefillThreads = 192;  // + warp 4: TMA producer, warp 5: MMA issuer
 constexpr unsigned long long kWaitLimitNs = 1000000000ull;  // bounded waits: 1 s
 
 // Status word of the bounded waits (TMLLM_TIMEOUT after an expired wait); read and cleared by
@@ -59,6 +59,8 @@ struct PrefillArgs {
     int32_t uniform_rows, num_seqs, total_rows;
     int32_t q_heads, kv_heads, group, head_dim, block_size, bs_shift, max_blocks;
     int32_t rope_len, rope_off, out_f32;
+    int32_t rope_vec;  // tables 16-byte aligned: 8 entries per two vector loads
+    int32_t rope_tma;  // head_dim 64: a unit's 128 table rows are staged by TMA
     float scale_log2;
 };
 
@@ -241,6 +243,39 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+// All 128 F32 columns of this thread's lane in one load (and its wait).
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, float (&v)[128]) {
+    uint32_t r[128];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x128.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, %64, %65, %66, %67, %68, %69, %70, %71, %72, %73, %74, %75, %76, %77, %78, %79, %80, %81, %82, %83, %84, %85, %86, %87, %88, %89, %90, %91, %92, %93, %94, %95, %96, %97, %98, %99, %100, %101, %102, %103, %104, %105, %106, %107, %108, %109, %110, %111, %112, %113, %114, %115, %116, %117, %118, %119, %120, %121, %122, %123, %124, %125, %126, %127}, [%128];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+          "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+          "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]),
+          "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+          "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]),
+          "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]),
+          "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+          "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]),
+          "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]),
+          "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]), "=r"(r[64]), "=r"(r[65]),
+          "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]),
+          "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]),
+          "=r"(r[78]), "=r"(r[79]), "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]),
+          "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]), "=r"(r[88]), "=r"(r[89]),
+          "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]),
+          "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]),
+          "=r"(r[102]), "=r"(r[103]), "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]),
+          "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]), "=r"(r[112]), "=r"(r[113]),
+          "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]),
+          "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]),
+          "=r"(r[126]), "=r"(r[127])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 128; ++i) v[i] = __uint_as_float(r[i]);
+}
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
@@ -299,33 +334,62 @@ struct TcCfg {
     static constexpr int MIN_BLOCKS = D == 64 ? 2 : 1;
 };
 
-// Barrier slots (8 bytes each) after the tiles, then the tensor-memory address and flags.
-enum : int { BAR_Q = 0, BAR_K0 = 1, BAR_V0 = 3, BAR_S = 5, BAR_P = 6, BAR_O = 7, NBARS = 8 };
+// mbarriers (8 bytes each) after the tiles, then the tensor-memory address and the abort
+// flag.  Full/empty pairs form the rings between the roles:
+//   QL  raw Q tile landed (TMA)            Q   rotated Q written (softmax warps)
+//   QE  Q tile no longer read (MMA)        KF/VF[st]  K/V stage loaded (TMA)
+//   KE[st] K/V stage no longer read (MMA)  S   S = Q K^T done (MMA)
+//   F   S copied to registers (softmax)    P   P tile written (softmax)
+//   O   O += P V done (MMA)                E   O copied out by the epilogue (softmax)
+//   RL  the unit's RoPE table rows landed in the P buffer (TMA, head_dim 64)
+enum : int {
+    BAR_QL = 0, BAR_Q = 1, BAR_QE = 2, BAR_KF = 3, BAR_VF = 5, BAR_KE = 7, BAR_S = 9,
+    BAR_F = 10, BAR_P = 11, BAR_O = 12, BAR_E = 13, BAR_RL = 14, NBARS = 15
+};
+
+// One unit of work: 128 query rows of one (query head, sequence).  Units are numbered
+// longest first (last row tile of every head/sequence, then the one before, ...) and dealt
+// to the persistent CTAs in a snake order, so every CTA gets a similar number of key tiles.
+struct Unit {
+    int h, s, kvh, row0, rows, q_lo, cached, kv_len, nt;
+};
+__device__ __forceinline__ bool unit_of(const PrefillArgs& a, int k, int num_units,
+                                        int row_tiles, Unit& u) {
+    const int G = gridDim.x;
+    const int idx = (k & 1) ? (k + 1) * G - 1 - static_cast<int>(blockIdx.x)
+                            : k * G + static_cast<int>(blockIdx.x);
+    if (idx >= num_units) return false;
+    const int hb = a.q_heads * a.num_seqs;
+    const int tile = row_tiles - 1 - idx / hb;
+    u.h = (idx % hb) % a.q_heads;
+    u.s = (idx % hb) / a.q_heads;
+    u.kvh = u.h / a.group;
+    const int n = seq_rows(a, u.s, &u.row0);
+    u.q_lo = tile * kTile;
+    u.rows = n - u.q_lo < kTile ? n - u.q_lo : kTile;  // <= 0: nothing to do
+    u.cached = a.seq_lens[u.s];
+    u.kv_len = u.cached + u.q_lo + u.rows;
+    u.nt = u.rows > 0 ? (u.kv_len + kTile - 1) / kTile : 0;
+    return true;
+}
 
 template <int D>
 __global__ void __launch_bounds__(kPrefillThreads, TcCfg<D>::MIN_BLOCKS)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
-                      const __grid_constant__ CUtensorMap vmap, const PrefillArgs a) {
+                      const __grid_constant__ CUtensorMap vmap,
+                      const __grid_constant__ CUtensorMap qmap,
+                      const __grid_constant__ CUtensorMap cmap,
+                      const __grid_constant__ CUtensorMap smap, const PrefillArgs a,
+                      int num_units, int row_tiles) {
     using Cfg = TcCfg<D>;
     extern __shared__ __align__(1024) unsigned char smem[];
     const int tid = threadIdx.x;
-    const int h = blockIdx.x % a.q_heads;
-    const int s = blockIdx.x / a.q_heads;
-    const int tile = gridDim.y - 1 - blockIdx.y;  // the longest tiles start first
-    int row0;
-    const int nrows_seq = seq_rows(a, s, &row0);
-    const int q_lo = tile * kTile;
-    if (q_lo >= nrows_seq) return;  // uniform for the CTA: nothing allocated yet
-    const int rows = min(kTile, nrows_seq - q_lo);
-    const int cached = a.seq_lens[s];
-    const int kv_len = cached + q_lo + rows;  // keys seen by the last row of this tile
-    const int nt = (kv_len + kTile - 1) / kTile;
-    const int kvh = h / a.group;
-
+    const int warp = tid >> 5, lane = tid & 31;
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bars = sbase + Cfg::OFF_BAR;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::OFF_BAR + NBARS * 8);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::OFF_BAR + NBARS * 8 + 4);
+    volatile int* abort_flag =
+        reinterpret_cast<volatile int*>(smem + Cfg::OFF_BAR + NBARS * 8 + 4);
     auto bar = [&](int i) { return bars + 8u * static_cast<uint32_t>(i); };
 
     if ((sbase & 1023u) != 0) {  // the swizzle atoms need 1024-byte alignment
@@ -333,18 +397,24 @@ __global__ void __launch_bounds__(kPrefillThreads, TcCfg<D>::MIN_BLOCKS)
         return;
     }
     if (tid == 0) {
+        mbar_init(bar(BAR_QL), 1);
         mbar_init(bar(BAR_Q), kSoftmaxThreads);
-        mbar_init(bar(BAR_K0), 1);
-        mbar_init(bar(BAR_K0 + 1), 1);
-        mbar_init(bar(BAR_V0), 1);
-        mbar_init(bar(BAR_V0 + 1), 1);
+        mbar_init(bar(BAR_QE), 1);
+        for (int st = 0; st < 2; ++st) {
+            mbar_init(bar(BAR_KF + st), 1);
+            mbar_init(bar(BAR_VF + st), 1);
+            mbar_init(bar(BAR_KE + st), 1);
+        }
         mbar_init(bar(BAR_S), 1);
+        mbar_init(bar(BAR_F), kSoftmaxThreads);
         mbar_init(bar(BAR_P), kSoftmaxThreads);
         mbar_init(bar(BAR_O), 1);
+        mbar_init(bar(BAR_E), kSoftmaxThreads);
+        mbar_init(bar(BAR_RL), 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (tid < 32) {  // warp 0 owns the tensor-memory allocation
+    if (warp == 0) {  // warp 0 owns the tensor-memory allocation
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tmem_slot)),
                      "r"(Cfg::TMEM_COLS)
@@ -358,237 +428,345 @@ __global__ void __launch_bounds__(kPrefillThreads, TcCfg<D>::MIN_BLOCKS)
     const uint32_t tmem_s = tmem;
     const uint32_t tmem_o = tmem + 128;
     const unsigned long long t0 = global_ns();
+    constexpr unsigned FULL = 0xffffffffu;
 
-    if (tid == kSoftmaxThreads) {
-        // ================= producer + MMA issuer (one thread) =================
+    if (warp == 4) {
+        // ================= producer: raw Q tiles and K/V pages by TMA =================
         const int box_rows = a.block_size < kTile ? a.block_size : kTile;
-        const int nbox = kTile / box_rows;
+        const int nbox = kTile / box_rows;  // <= 8: pages are >= 16 positions
         const uint32_t box_bytes = static_cast<uint32_t>(box_rows) * 128u;
         // Every box of a tile is loaded: a box past the keys or without a page reads rows
         // beyond the arena, which TMA fills with zeros, so masked keys never meet stale
         // shared memory (P = 0 times a non-finite V would not be 0).
         const uint32_t tile_bytes = static_cast<uint32_t>(nbox) * box_bytes * Cfg::NB;
-        auto issue_tile = [&](int t, int st) {
-            const int base = t * kTile;
-            mbar_arrive_tx(bar(BAR_K0 + st), tile_bytes);
-            mbar_arrive_tx(bar(BAR_V0 + st), tile_bytes);
-            const uint32_t kdst = sbase + Cfg::OFF_K + st * Cfg::TILE;
-            const uint32_t vdst = sbase + Cfg::OFF_V + st * Cfg::TILE;
-            for (int b = 0; b < nbox; ++b) {
-                const int pos = base + b * box_rows;
-                const int64_t blk = pos < kv_len ? page_of(a, s, pos) : -1;
-                const int y = blk < 0 ? static_cast<int>(a.arena_rows)
-                                      : static_cast<int>((blk * a.kv_heads + kvh) * a.block_size +
-                                                         in_page(a, pos));
-#pragma unroll
-                for (int c = 0; c < Cfg::NB; ++c) {
-                    const uint32_t off = c * Cfg::BLK + b * box_bytes;
-                    tma_load_2d(kdst + off, &kmap, c * 64, y, bar(BAR_K0 + st));
-                    tma_load_2d(vdst + off, &vmap, c * 64, y, bar(BAR_V0 + st));
-                }
-            }
-        };
-        constexpr uint32_t IDESC_QK = f16_idesc(128, 128, false);
-        constexpr uint32_t IDESC_PV = f16_idesc(128, D, true);
-        auto issue_qk = [&](int st) {
-            const uint32_t qa = sbase + Cfg::OFF_Q, ka = sbase + Cfg::OFF_K + st * Cfg::TILE;
-#pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-                const uint32_t off = (kk >> 2) * Cfg::BLK + (kk & 3) * 32;
-                tc_mma(tmem_s, sw128_desc(qa + off, 16, 1024), sw128_desc(ka + off, 16, 1024),
-                       IDESC_QK, kk > 0);
-            }
-        };
-        auto issue_pv = [&](int st, bool acc) {
-            const uint32_t pa = sbase + Cfg::OFF_P, va = sbase + Cfg::OFF_V + st * Cfg::TILE;
-#pragma unroll
-            for (int kk = 0; kk < kTile / 16; ++kk) {
-                const uint32_t aoff = (kk >> 2) * Cfg::BLK + (kk & 3) * 32;
-                tc_mma(tmem_o, sw128_desc(pa + aoff, 16, 1024),
-                       sw128_desc(va + kk * 2048, Cfg::BLK, 1024), IDESC_PV, acc || kk > 0);
-            }
-        };
         bool ok = true;
-        issue_tile(0, 0);
-        if (nt > 1) issue_tile(1, 1);
-        ok = mbar_wait(bar(BAR_Q), 0, abort_flag, t0) && mbar_wait(bar(BAR_K0), 0, abort_flag, t0);
-        if (ok) {
-            tc_fence_after();
-            issue_qk(0);
-            tc_commit(bar(BAR_S));
-        }
-        for (int j = 0; ok && j < nt; ++j) {
-            const int st = j & 1;
-            ok = mbar_wait(bar(BAR_P), j & 1, abort_flag, t0) &&
-                 mbar_wait(bar(BAR_V0 + st), (j >> 1) & 1, abort_flag, t0);
-            if (!ok) break;
-            tc_fence_after();
-            issue_pv(st, j > 0);
-            tc_commit(bar(BAR_O));
-            if (j + 1 < nt) {
-                ok = mbar_wait(bar(BAR_K0 + (st ^ 1)), ((j + 1) >> 1) & 1, abort_flag, t0);
-                if (!ok) break;
-                tc_fence_after();
-                issue_qk(st ^ 1);
-                tc_commit(bar(BAR_S));
-            }
-            if (j + 2 < nt) {  // stage st is free once P_j V_j has completed
-                ok = mbar_wait(bar(BAR_O), j & 1, abort_flag, t0);
-                if (!ok) break;
-                issue_tile(j + 2, st);
-            }
-        }
-    } else if (tid < kSoftmaxThreads) {
-        // ================= softmax warps: thread r owns query row r =================
-        const int r = tid;
-        const int warp = tid >> 5;
-        const int half = D / 2;
-        const bool live = r < rows;
-        const int prow = row0 + q_lo + (live ? r : rows - 1);
-        const int qpos = cached + q_lo + (live ? r : rows - 1);  // keys 0..qpos are visible
-        // Q row: rotate, round to F16, store swizzled (row r of every 64-column block)
-        {
-            const __half* qr = static_cast<const __half*>(a.q) + static_cast<int64_t>(prow) * a.q_stride +
-                               static_cast<int64_t>(h) * D;
-            unsigned char* qs = smem + Cfg::OFF_Q + r * 128;
-#pragma unroll
-            for (int c = 0; c < D / 16; ++c) {  // chunk c of the first half pairs with c + D/16
-                uint4 u1 = make_uint4(0, 0, 0, 0), u2 = make_uint4(0, 0, 0, 0);
-                if (live) {
-                    u1 = *reinterpret_cast<const uint4*>(qr + c * 8);
-                    u2 = *reinterpret_cast<const uint4*>(qr + half + c * 8);
-                    __half2* h1 = reinterpret_cast<__half2*>(&u1);
-                    __half2* h2 = reinterpret_cast<__half2*>(&u2);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        float2 f1 = __half22float2(h1[e]), f2 = __half22float2(h2[e]);
-                        rope_rotate(a, qpos + a.rope_off, c * 8 + 2 * e, half, f1.x, f2.x);
-                        rope_rotate(a, qpos + a.rope_off, c * 8 + 2 * e + 1, half, f1.y, f2.y);
-                        h1[e] = __floats2half2_rn(f1.x, f1.y);
-                        h2[e] = __floats2half2_rn(f2.x, f2.y);
+        int g = 0, it = 0;
+        Unit u;
+        for (int k = 0; ok && unit_of(a, k, num_units, row_tiles, u); ++k) {
+            if (u.nt == 0) continue;
+            if (lane == 0) {
+                if (it > 0) ok = mbar_wait(bar(BAR_QE), (it - 1) & 1, abort_flag, t0);
+                if (ok) mbar_arrive_tx(bar(BAR_QL), static_cast<uint32_t>(Cfg::TILE));
+                // the RoPE rows go to the P buffer, free once the last P V has completed
+                if (ok && a.rope_tma) {
+                    if (it > 0) ok = mbar_wait(bar(BAR_O), (g - 1) & 1, abort_flag, t0);
+                    if (ok) {
+                        mbar_arrive_tx(bar(BAR_RL), 2u * Cfg::BLK);
+                        const int y = u.cached + u.q_lo + a.rope_off;
+                        tma_load_2d(sbase + Cfg::OFF_P, &cmap, 0, y, bar(BAR_RL));
+                        tma_load_2d(sbase + Cfg::OFF_P + Cfg::BLK, &smap, 0, y, bar(BAR_RL));
                     }
                 }
-                const int c2 = c + D / 16;
-                *reinterpret_cast<uint4*>(qs + (c >> 3) * Cfg::BLK + (((c & 7) ^ (r & 7)) << 4)) = u1;
-                *reinterpret_cast<uint4*>(qs + (c2 >> 3) * Cfg::BLK + (((c2 & 7) ^ (r & 7)) << 4)) = u2;
             }
+            ok = __shfl_sync(FULL, ok, 0);
+            if (!ok) break;
+            if (lane < Cfg::NB)
+                tma_load_2d(sbase + Cfg::OFF_Q + lane * Cfg::BLK, &qmap, u.h * D + lane * 64,
+                            u.row0 + u.q_lo, bar(BAR_QL));
+            for (int j = 0; j < u.nt; ++j, ++g) {
+                const int st = g & 1;
+                // arena row of box `lane` of this tile (all block-table reads in flight)
+                const int pos = j * kTile + lane * box_rows;
+                const int64_t blk = (lane < nbox && pos < u.kv_len) ? page_of(a, u.s, pos) : -1;
+                const int y = blk < 0 ? static_cast<int>(a.arena_rows)
+                                      : static_cast<int>((blk * a.kv_heads + u.kvh) * a.block_size +
+                                                         in_page(a, pos));
+                if (lane == 0) {
+                    if (g >= 2) ok = mbar_wait(bar(BAR_KE + st), ((g >> 1) - 1) & 1, abort_flag, t0);
+                    if (ok) {
+                        mbar_arrive_tx(bar(BAR_KF + st), tile_bytes);
+                        mbar_arrive_tx(bar(BAR_VF + st), tile_bytes);
+                    }
+                }
+                ok = __shfl_sync(FULL, ok, 0);
+                if (!ok) break;
+                if (lane < nbox) {
+                    const uint32_t kdst = sbase + Cfg::OFF_K + st * Cfg::TILE + lane * box_bytes;
+                    const uint32_t vdst = sbase + Cfg::OFF_V + st * Cfg::TILE + lane * box_bytes;
+#pragma unroll
+                    for (int c = 0; c < Cfg::NB; ++c) {
+                        tma_load_2d(kdst + c * Cfg::BLK, &kmap, c * 64, y, bar(BAR_KF + st));
+                        tma_load_2d(vdst + c * Cfg::BLK, &vmap, c * 64, y, bar(BAR_VF + st));
+                    }
+                }
+            }
+            ++it;
         }
-        fence_async_smem();
-        mbar_arrive(bar(BAR_Q));
-
+    } else if (warp == 5) {
+        // ================= MMA issuer (one lane) =================
+        if (lane == 0) {
+            constexpr uint32_t IDESC_QK = f16_idesc(128, 128, false);
+            constexpr uint32_t IDESC_PV = f16_idesc(128, D, true);
+            auto issue_qk = [&](int st) {
+                const uint32_t qa = sbase + Cfg::OFF_Q, ka = sbase + Cfg::OFF_K + st * Cfg::TILE;
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * Cfg::BLK + (kk & 3) * 32;
+                    tc_mma(tmem_s, sw128_desc(qa + off, 16, 1024), sw128_desc(ka + off, 16, 1024),
+                           IDESC_QK, kk > 0);
+                }
+            };
+            auto issue_pv = [&](int st, bool acc) {
+                const uint32_t pa = sbase + Cfg::OFF_P, va = sbase + Cfg::OFF_V + st * Cfg::TILE;
+#pragma unroll
+                for (int kk = 0; kk < kTile / 16; ++kk) {
+                    const uint32_t aoff = (kk >> 2) * Cfg::BLK + (kk & 3) * 32;
+                    tc_mma(tmem_o, sw128_desc(pa + aoff, 16, 1024),
+                           sw128_desc(va + kk * 2048, Cfg::BLK, 1024), IDESC_PV, acc || kk > 0);
+                }
+            };
+            bool ok = true;
+            int g = 0, it = 0;
+            Unit u;
+            for (int k = 0; ok && unit_of(a, k, num_units, row_tiles, u); ++k) {
+                if (u.nt == 0) continue;
+                // S is free: the previous tile's P arrived, which follows its S copy
+                ok = mbar_wait(bar(BAR_Q), it & 1, abort_flag, t0) &&
+                     mbar_wait(bar(BAR_KF + (g & 1)), (g >> 1) & 1, abort_flag, t0);
+                if (!ok) break;
+                tc_fence_after();
+                issue_qk(g & 1);
+                tc_commit(bar(BAR_S));
+                for (int j = 0; j < u.nt; ++j, ++g) {
+                    const int st = g & 1;
+                    if (j + 1 < u.nt) {
+                        // S_{g+1} = Q K^T as soon as the softmax warps hold S_g in
+                        // registers, so it runs while they exponentiate tile g
+                        ok = mbar_wait(bar(BAR_F), g & 1, abort_flag, t0) &&
+                             mbar_wait(bar(BAR_KF + (st ^ 1)), ((g + 1) >> 1) & 1, abort_flag, t0);
+                        if (!ok) break;
+                        tc_fence_after();
+                        issue_qk(st ^ 1);
+                        tc_commit(bar(BAR_S));
+                    } else {
+                        tc_commit(bar(BAR_QE));  // the Q tile is free once these QKs finish
+                    }
+                    ok = mbar_wait(bar(BAR_P), g & 1, abort_flag, t0) &&
+                         mbar_wait(bar(BAR_VF + st), (g >> 1) & 1, abort_flag, t0);
+                    if (ok && j == 0 && it > 0)  // O is free once the last epilogue read it
+                        ok = mbar_wait(bar(BAR_E), (it - 1) & 1, abort_flag, t0);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_pv(st, j > 0);
+                    tc_commit(bar(BAR_O));
+                    tc_commit(bar(BAR_KE + st));
+                }
+                ++it;
+            }
+            // every MMA and its barrier arrivals done before the CTA releases its memory
+            if (ok && g > 0) mbar_wait(bar(BAR_KE + ((g - 1) & 1)), ((g - 1) >> 1) & 1, abort_flag, t0);
+        }
+    } else {
+        // ================= softmax warps: thread r owns query row r =================
+        const int r = tid;
+        const int half = D / 2;
         const uint32_t lane_s = tmem_s + (static_cast<uint32_t>(warp * 32) << 16);
         const uint32_t lane_o = tmem_o + (static_cast<uint32_t>(warp * 32) << 16);
         unsigned char* prow_s = smem + Cfg::OFF_P + r * 128;
-        float m_used = -INFINITY, l = 0.f;
+        unsigned char* qrow_s = smem + Cfg::OFF_Q + r * 128;
         bool ok = true;
-        for (int j = 0; j < nt; ++j) {
-            ok = mbar_wait(bar(BAR_S), j & 1, abort_flag, t0);
+        int g = 0, it = 0;
+        Unit u;
+        for (int k = 0; ok && unit_of(a, k, num_units, row_tiles, u); ++k) {
+            if (u.nt == 0) continue;
+            const bool live = r < u.rows;
+            const int qpos = u.cached + u.q_lo + (live ? r : u.rows - 1);  // keys 0..qpos
+            // ---- Q: the raw tile arrives by TMA; rotate this row in place
+            const int rpos = qpos + a.rope_off;
+            const bool rot = live && a.rope_cos != nullptr && rpos >= 0 && rpos < a.rope_len;
+            ok = mbar_wait(bar(BAR_QL), it & 1, abort_flag, t0);
+            ok = __all_sync(FULL, ok);
             if (!ok) break;
-            tc_fence_after();
-            const int lim = qpos - j * kTile;  // columns 0..lim of this tile are visible
-            float mx = -INFINITY;
-            float v[32];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                tmem_ld32(lane_s + c * 32, v);
-#pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    if (c * 32 + i <= lim) mx = fmaxf(mx, v[i]);
-            }
-            const float mt = mx * a.scale_log2;
-            if (j > 0) {  // P_{j-1} V_{j-1} done: P buffer free, O settled
-                ok = mbar_wait(bar(BAR_O), (j - 1) & 1, abort_flag, t0);
+            if (a.rope_tma) {  // the table rows of this unit, staged in the P buffer
+                ok = mbar_wait(bar(BAR_RL), it & 1, abort_flag, t0);
+                ok = __all_sync(FULL, ok);
                 if (!ok) break;
-                tc_fence_after();
             }
-            // Rescale only when the running maximum grew by more than 2^8; otherwise keep
-            // the stale maximum (P stays below 2^8 and the final 1/l makes it exact).  The
-            // tensor-memory accesses are warp-wide, so a warp rescales when any row needs it
-            // (alpha = 1 for the others).
-            const bool need = j > 0 && mt > m_used + 8.f;
-            float alpha = 1.f;
-            if (need) {
-                alpha = fast_exp2(m_used - mt);
-                l *= alpha;
-                m_used = mt;
-            }
-            if (j == 0) m_used = mt;
-            if (__any_sync(0xffffffffu, need)) {
+            if (rot) {
+                const float* ct = a.rope_cos + static_cast<int64_t>(rpos) * half;
+                const float* stb = a.rope_sin + static_cast<int64_t>(rpos) * half;
+                const unsigned char* cst = smem + Cfg::OFF_P + r * 128;  // 32 floats, swizzled
+                const unsigned char* sst = cst + Cfg::BLK;
 #pragma unroll
-                for (int c = 0; c < D / 32; ++c) {
-                    float o[32];
-                    tmem_ld32(lane_o + c * 32, o);
+                for (int c0 = 0; c0 < D / 16; c0 += 4) {  // chunk c pairs with chunk c + D/16
+                    float cs[32], sn[32];
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                    tmem_st32(lane_o + c * 32, o);
-                }
-            }
-            const float neg = -m_used;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                tmem_ld32(lane_s + c * 32, v);
-#pragma unroll
-                for (int g = 0; g < 4; ++g) {  // 8 keys -> one 16-byte chunk of P
-                    uint32_t pk[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int i0 = g * 8 + 2 * e;
-                        const float p0 = (c * 32 + i0 <= lim)
-                                             ? fast_exp2(fmaf(v[i0], a.scale_log2, neg)) : 0.f;
-                        const float p1 = (c * 32 + i0 + 1 <= lim)
-                                             ? fast_exp2(fmaf(v[i0 + 1], a.scale_log2, neg)) : 0.f;
-                        l += p0 + p1;
-                        __half2 hp = __floats2half2_rn(p0, p1);
-                        pk[e] = *reinterpret_cast<uint32_t*>(&hp);
+                    for (int q4 = 0; q4 < 8; ++q4) {
+                        float4 cv, sv;
+                        if (a.rope_tma) {
+                            cv = *reinterpret_cast<const float4*>(cst + ((q4 ^ (r & 7)) << 4));
+                            sv = *reinterpret_cast<const float4*>(sst + ((q4 ^ (r & 7)) << 4));
+                        } else if (a.rope_vec) {
+                            cv = __ldg(reinterpret_cast<const float4*>(ct + c0 * 8) + q4);
+                            sv = __ldg(reinterpret_cast<const float4*>(stb + c0 * 8) + q4);
+                        } else {
+                            const float* cp = ct + c0 * 8 + 4 * q4;
+                            const float* sp = stb + c0 * 8 + 4 * q4;
+                            cv = make_float4(__ldg(cp), __ldg(cp + 1), __ldg(cp + 2), __ldg(cp + 3));
+                            sv = make_float4(__ldg(sp), __ldg(sp + 1), __ldg(sp + 2), __ldg(sp + 3));
+                        }
+                        cs[4 * q4] = cv.x; cs[4 * q4 + 1] = cv.y; cs[4 * q4 + 2] = cv.z; cs[4 * q4 + 3] = cv.w;
+                        sn[4 * q4] = sv.x; sn[4 * q4 + 1] = sv.y; sn[4 * q4 + 2] = sv.z; sn[4 * q4 + 3] = sv.w;
                     }
-                    const int cc = c * 4 + g;  // chunk 0..15 along the keys
-                    *reinterpret_cast<uint4*>(prow_s + (cc >> 3) * Cfg::BLK +
-                                              (((cc & 7) ^ (r & 7)) << 4)) =
-                        make_uint4(pk[0], pk[1], pk[2], pk[3]);
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        const int c = c0 + q4, c2 = c + D / 16;
+                        uint4* p1 = reinterpret_cast<uint4*>(qrow_s + (c >> 3) * Cfg::BLK +
+                                                             (((c & 7) ^ (r & 7)) << 4));
+                        uint4* p2 = reinterpret_cast<uint4*>(qrow_s + (c2 >> 3) * Cfg::BLK +
+                                                             (((c2 & 7) ^ (r & 7)) << 4));
+                        uint4 u1 = *p1, u2 = *p2;
+                        __half2* h1 = reinterpret_cast<__half2*>(&u1);
+                        __half2* h2 = reinterpret_cast<__half2*>(&u2);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            // kernels/rope.metal:57-63 without contraction, two pairs at once:
+                            // x1' = x1 c - x2 s, x2' = x2 c + x1 s (each product rounded)
+                            const float2 f1 = __half22float2(h1[e]), f2 = __half22float2(h2[e]);
+                            const int i0 = q4 * 8 + 2 * e;
+                            const float2 c2v = make_float2(cs[i0], cs[i0 + 1]);
+                            const float2 s2v = make_float2(sn[i0], sn[i0 + 1]);
+                            const float2 m1 = __fmul2_rn(f2, s2v), m2 = __fmul2_rn(f1, s2v);
+                            const float2 x = __fadd2_rn(__fmul2_rn(f1, c2v), make_float2(-m1.x, -m1.y));
+                            const float2 y = __fadd2_rn(__fmul2_rn(f2, c2v), m2);
+                            h1[e] = __floats2half2_rn(x.x, x.y);
+                            h2[e] = __floats2half2_rn(y.x, y.y);
+                        }
+                        *p1 = u1;
+                        *p2 = u2;
+                    }
                 }
             }
             fence_async_smem();
-            tc_fence_before();
-            mbar_arrive(bar(BAR_P));
-        }
-        if (ok) ok = mbar_wait(bar(BAR_O), (nt - 1) & 1, abort_flag, t0);
-        if (ok) {
+            mbar_arrive(bar(BAR_Q));
+
+            float m_used = -INFINITY, l = 0.f;
+            for (int j = 0; j < u.nt; ++j, ++g) {
+                ok = mbar_wait(bar(BAR_S), g & 1, abort_flag, t0);
+                ok = __all_sync(FULL, ok);
+                if (!ok) break;
+                tc_fence_after();
+                const int lim = qpos - j * kTile;  // columns 0..lim of this tile are visible
+                float v[128];
+                tmem_ld128(lane_s, v);
+                tc_fence_before();
+                mbar_arrive(bar(BAR_F));  // S may be overwritten by the next Q K^T
+                // On the diagonal, invisible columns become -inf once: the maximum then
+                // ignores them and their exponentials are exactly 0.  32-column chunks that
+                // no row of the warp can see are skipped altogether (warp-uniform).
+                const bool wfull = __all_sync(FULL, lim >= kTile - 1);
+                if (!wfull) {
+#pragma unroll
+                    for (int i = 0; i < 128; ++i) v[i] = i <= lim ? v[i] : -INFINITY;
+                }
+                float mx = -INFINITY;
+#pragma unroll
+                for (int i = 0; i < 128; ++i) mx = fmaxf(mx, v[i]);
+                const float mt = mx * a.scale_log2;
+                if (j > 0) {  // P_{g-1} V_{g-1} done: P buffer free, O settled
+                    ok = mbar_wait(bar(BAR_O), (g - 1) & 1, abort_flag, t0);
+                    ok = __all_sync(FULL, ok);
+                    if (!ok) break;
+                    tc_fence_after();
+                }
+                // Rescale only when the running maximum grew by more than 2^8; otherwise
+                // keep the stale maximum (P stays below 2^8 and the final 1/l makes it
+                // exact).  Tensor-memory accesses are warp-wide, so a warp rescales when
+                // any of its rows needs it (alpha = 1 for the others).
+                const bool need = j > 0 && mt > m_used + 8.f;
+                float alpha = 1.f;
+                if (need) {
+                    alpha = fast_exp2(m_used - mt);
+                    l *= alpha;
+                    m_used = mt;
+                }
+                if (j == 0) m_used = mt;
+                const float2 sc2 = make_float2(a.scale_log2, a.scale_log2);
+                const float2 neg2 = make_float2(-m_used, -m_used);
+                float2 l2 = make_float2(0.f, 0.f);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const bool dark = __all_sync(FULL, c * 32 > lim);
+#pragma unroll
+                    for (int gq = 0; gq < 4; ++gq) {  // 8 keys -> one 16-byte chunk of P
+                        uint32_t pk[4] = {0u, 0u, 0u, 0u};
+                        if (!dark) {
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const int i0 = c * 32 + gq * 8 + 2 * e;
+                                const float2 x = __ffma2_rn(make_float2(v[i0], v[i0 + 1]), sc2, neg2);
+                                const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+                                l2 = __fadd2_rn(l2, p);
+                                __half2 hp = __floats2half2_rn(p.x, p.y);
+                                pk[e] = *reinterpret_cast<uint32_t*>(&hp);
+                            }
+                        }
+                        const int cc = c * 4 + gq;  // chunk 0..15 along the keys
+                        *reinterpret_cast<uint4*>(prow_s + (cc >> 3) * Cfg::BLK +
+                                                  (((cc & 7) ^ (r & 7)) << 4)) =
+                            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    }
+                }
+                l += l2.x + l2.y;
+                if (__any_sync(FULL, need)) {  // after the exponentials: fewer live registers
+#pragma unroll
+                    for (int c = 0; c < D / 32; ++c) {
+                        float o[32];
+                        tmem_ld32(lane_o + c * 32, o);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                        tmem_st32(lane_o + c * 32, o);
+                    }
+                }
+                fence_async_smem();
+                tc_fence_before();
+                mbar_arrive(bar(BAR_P));
+            }
+            if (!ok) break;
+            // ---- epilogue: O of the unit's last tile, normalised, out to global
+            ok = mbar_wait(bar(BAR_O), (g - 1) & 1, abort_flag, t0);
+            ok = __all_sync(FULL, ok);
+            if (!ok) break;
             tc_fence_after();
             const float inv = 1.f / l;
-            const int64_t orow = static_cast<int64_t>(prow) * a.out_stride +
-                                 static_cast<int64_t>(h) * D;
+            const int64_t orow = static_cast<int64_t>(u.row0 + u.q_lo + (live ? r : 0)) *
+                                     a.out_stride + static_cast<int64_t>(u.h) * D;
 #pragma unroll
             for (int c = 0; c < D / 32; ++c) {
                 float o[32];
                 tmem_ld32(lane_o + c * 32, o);  // warp-wide: every lane loads, live rows store
-                if (live) {
-                    if (a.out_f32) {
-                        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + orow + c * 32);
+                if (c == D / 32 - 1) {
+                    tc_fence_before();
+                    mbar_arrive(bar(BAR_E));  // the next unit's first P V may overwrite O
+                }
+                if (!live) continue;
+                if (a.out_f32) {
+                    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + orow + c * 32);
 #pragma unroll
-                        for (int i = 0; i < 8; ++i)
-                            dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv,
-                                                 o[4 * i + 2] * inv, o[4 * i + 3] * inv);
-                    } else {
-                        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + orow + c * 32);
+                    for (int i = 0; i < 8; ++i)
+                        dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv,
+                                             o[4 * i + 2] * inv, o[4 * i + 3] * inv);
+                } else {
+                    uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + orow + c * 32);
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            uint32_t pk[4];
+                    for (int i = 0; i < 4; ++i) {
+                        uint32_t pk[4];
 #pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                __half2 hv = __floats2half2_rn(o[8 * i + 2 * e] * inv,
-                                                               o[8 * i + 2 * e + 1] * inv);
-                                pk[e] = *reinterpret_cast<uint32_t*>(&hv);
-                            }
-                            dst[i] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                        for (int e = 0; e < 4; ++e) {
+                            __half2 hv = __floats2half2_rn(o[8 * i + 2 * e] * inv,
+                                                           o[8 * i + 2 * e + 1] * inv);
+                            pk[e] = *reinterpret_cast<uint32_t*>(&hv);
                         }
+                        dst[i] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                     }
                 }
             }
+            ++it;
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (tid < 32) {
+    if (warp == 0) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "r"(Cfg::TMEM_COLS)
@@ -688,20 +866,25 @@ EncodeTiledFn encode_tiled() {
     return fn;
 }
 
-// 2-D map over one arena viewed as rows of D halves; boxes of 64 columns x box_rows rows,
-// 128-byte swizzle (the layout the tensor-core descriptors read).
-int make_arena_map(CUtensorMap* map, void* arena, int64_t rows, int D, int box_rows) {
+// 2-D map over `rows` rows of `inner` elements, `row_bytes` apart; boxes of 128 bytes (64 F16
+// or 32 F32 columns) x box_rows rows with the 128-byte swizzle (the layout the tensor-core
+// descriptors read).
+int make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t rows, int64_t row_bytes,
+             int box_rows, bool f32 = false) {
     EncodeTiledFn enc = encode_tiled();
     if (!enc) return fail(TMLLM_DEVICE_ERROR, "cuTensorMapEncodeTiled is not available");
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(D) * 2};
-    const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+    const cuuint32_t box[2] = {f32 ? 32u : 64u, static_cast<cuuint32_t>(box_rows)};
     const cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, arena, dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = enc(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                     2, const_cast<void*>(base), dims,
+                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
-        return fail(TMLLM_DEVICE_ERROR, "tensor map encoding failed (CUresult %d)", static_cast<int>(r));
+        return fail(TMLLM_DEVICE_ERROR, "tensor map encoding failed (CUresult %d)",
+                    static_cast<int>(r));
     return TMLLM_OK;
 }
 
@@ -709,9 +892,17 @@ template <int D>
 int launch_tc(const PrefillArgs& a, int64_t arena_rows, int max_rows, cudaStream_t s) {
     using Cfg = TcCfg<D>;
     const int box_rows = a.block_size < kTile ? a.block_size : kTile;
-    CUtensorMap kmap, vmap;
-    if (int st = make_arena_map(&kmap, a.k_cache, arena_rows, D, box_rows)) return st;
-    if (int st = make_arena_map(&vmap, a.v_cache, arena_rows, D, box_rows)) return st;
+    CUtensorMap kmap, vmap, qmap;
+    if (int st = make_map(&kmap, a.k_cache, D, arena_rows, D * 2, box_rows)) return st;
+    if (int st = make_map(&vmap, a.v_cache, D, arena_rows, D * 2, box_rows)) return st;
+    if (int st = make_map(&qmap, a.q, static_cast<int64_t>(a.q_heads) * D, a.total_rows,
+                          a.q_stride * 2, kTile))
+        return st;
+    CUtensorMap cmap = qmap, smap = qmap;  // placeholders when the tables are not staged
+    if (a.rope_tma) {
+        if (int st = make_map(&cmap, a.rope_cos, D / 2, a.rope_len, D * 2, kTile, true)) return st;
+        if (int st = make_map(&smap, a.rope_sin, D / 2, a.rope_len, D * 2, kTile, true)) return st;
+    }
     static std::once_flag once[64];
     int dev = 0;
     TMLLM_CUDA_TRY(cudaGetDevice(&dev));
@@ -721,9 +912,13 @@ int launch_tc(const PrefillArgs& a, int64_t arena_rows, int max_rows, cudaStream
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     });
     if (attr != cudaSuccess) return cuda_fail(attr, "prefill shared-memory attribute");
-    dim3 grid(static_cast<unsigned>(a.q_heads * a.num_seqs),
-              static_cast<unsigned>((max_rows + kTile - 1) / kTile));
-    prefill_tc_kernel<D><<<grid, kPrefillThreads, Cfg::SMEM, s>>>(kmap, vmap, a);
+    const int row_tiles = (max_rows + kTile - 1) / kTile;
+    const int64_t units = static_cast<int64_t>(row_tiles) * a.q_heads * a.num_seqs;
+    if (units > INT32_MAX) return fail(TMLLM_INVALID_SHAPE, "too many prefill tiles");
+    int64_t ctas = static_cast<int64_t>(device_sm_count()) * Cfg::MIN_BLOCKS;
+    if (ctas > units) ctas = units;
+    prefill_tc_kernel<D><<<static_cast<unsigned>(ctas), kPrefillThreads, Cfg::SMEM, s>>>(
+        kmap, vmap, qmap, cmap, smap, a, static_cast<int>(units), row_tiles);
     TMLLM_LAUNCH_TRY();
     return TMLLM_OK;
 }
@@ -755,8 +950,9 @@ int prefill_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, con
         max_rows = rows_per_seq;
     }
     if (total_rows == 0 || max_rows == 0) return TMLLM_OK;
-    if (!q || !k_new || !v_new || !out || !kv->k_cache || !kv->v_cache || !kv->block_table ||
-        !kv->seq_lens)
+    if ((k_new == nullptr) != (v_new == nullptr))
+        return fail(TMLLM_INVALID_ARGUMENT, "k_new and v_new must both be given or both be NULL");
+    if (!q || !out || !kv->k_cache || !kv->v_cache || !kv->block_table || !kv->seq_lens)
         return fail(TMLLM_INVALID_ARGUMENT, "null tensor pointer");
     tmllm_decode_opts o{};
     if (opts) o = *opts;
@@ -776,7 +972,7 @@ int prefill_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, con
     const size_t es = dtype_size(kv->dtype);
     auto misaligned = [es](const void* p) { return (reinterpret_cast<uintptr_t>(p) % es) != 0; };
     if (misaligned(kv->k_cache) || misaligned(kv->v_cache) || misaligned(q) ||
-        misaligned(k_new) || misaligned(v_new) || misaligned(out))
+        (k_new && misaligned(k_new)) || (v_new && misaligned(v_new)) || misaligned(out))
         return fail(TMLLM_INVALID_ARGUMENT, "tensor pointers must be aligned to their element size");
 
     int bs_shift = -1;
@@ -813,6 +1009,8 @@ int prefill_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, con
     a.rope_len = o.rope_len;
     a.rope_off = o.rope_pos_offset;
     a.out_f32 = o.out_f32 || kv->dtype == TMLLM_F32;
+    a.rope_vec = o.rope_cos && aligned16(o.rope_cos) && aligned16(o.rope_sin) && (D / 2) % 4 == 0;
+    a.rope_tma = a.rope_vec && D == 64 && kv->dtype == TMLLM_F16;
     a.scale_log2 = scale * kLog2eP;
 
     // the attention path, decided before anything is enqueued
@@ -828,7 +1026,7 @@ int prefill_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, con
                     "the tensor-core prefill needs F16, head_dim 64/128, power-of-two pages of "
                     ">= 16 positions and 16-byte aligned q/out/arenas");
     // 1. append (rotated keys, values) at each sequence's cached length
-    {
+    if (k_new) {
         const int64_t work = static_cast<int64_t>(total_rows) * Hkv * (D / 2);
         int64_t blocks = (work + 255) / 256;
         const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
