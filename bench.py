@@ -515,6 +515,103 @@ def run_decoder(args) -> None:
 
 
 # ------------------------------------------------------------------------------------
+# Config 1: the reference's own CPU-runnable case, a latency figure (no roofline claim)
+# ------------------------------------------------------------------------------------
+
+def run_cfg1(args) -> None:
+    import numpy as np
+    import torch
+
+    import rustllm_b200 as rb
+
+    world, rank, local = dist_env()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    hq, hkv, d, cached, theta = 9, 3, 64, 128, 100000.0
+    rng = np.random.default_rng(1234)
+    k = rng.standard_normal((hkv, cached, d)).astype(np.float32)
+    v = rng.standard_normal((hkv, cached, d)).astype(np.float32)
+    q = rng.standard_normal((1, hq, d)).astype(np.float32)
+    kn = rng.standard_normal((1, hkv, d)).astype(np.float32)
+    vn = rng.standard_normal((1, hkv, d)).astype(np.float32)
+    # the reference's layout: one [1, Hkv, max, D] buffer (block size = capacity)
+    cache = rb.PagedKvCache(1, 1, cached + 1, hkv, d, dtype=torch.float32,
+                            block_size=cached + 1, device=dev)
+    cache.append(0, 0, torch.from_numpy(k).to(dev), torch.from_numpy(v).to(dev))
+    cache.advance(cached, 0)
+    cache.reserve(0, 1)
+    rope = rb.rope_tables(d, cached + 2, theta, device=dev)
+    gq, gkn, gvn = (torch.from_numpy(x).to(dev) for x in (q, kn, vn))
+    out = torch.empty((1, hq, d), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    n = max(args.steps, 1)
+    for _ in range(max(args.warmup, 3)):
+        cache.decode(0, gq, gkn, gvn, out=out, rope=rope, scale=0.125)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(n)]
+    for a, b in ev:  # lengths are not advanced: every step appends at position 128
+        a.record(stream)
+        cache.decode(0, gq, gkn, gvn, out=out, rope=rope, scale=0.125)
+        b.record(stream)
+    torch.cuda.synchronize()
+    lat = sorted(a.elapsed_time(b) * 1e3 for a, b in ev)
+    med = lat[len(lat) // 2]
+    # end to end: pinned host q, k, v in, out back to the host, every step
+    hq_, hk_, hv_ = (torch.from_numpy(x).pin_memory() for x in (q, kn, vn))
+    hout = torch.empty((1, hq, d), dtype=torch.float32).pin_memory()
+    e_lat = []
+    for i in range(min(n, 1000) + 3):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        gq.copy_(hq_, non_blocking=True)
+        gkn.copy_(hk_, non_blocking=True)
+        gvn.copy_(hv_, non_blocking=True)
+        cache.decode(0, gq, gkn, gvn, out=out, rope=rope, scale=0.125)
+        hout.copy_(out, non_blocking=True)
+        b.record(stream)
+        b.synchronize()
+        if i >= 3:
+            e_lat.append(a.elapsed_time(b) * 1e3)
+    e_lat.sort()
+    line = {
+        "metric": "config 1 decode step latency (fused append + attention, F32)",
+        "value": med, "unit": "us", "n_gpus": 1, "steps": n, "warmup": max(args.warmup, 3),
+        "ms_per_step": med / 1e3, "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) cache of 128 positions, q, k, v)",
+        "config": {"workload": "cfg1 TinyLlama-like layer: Hq=9, Hkv=3, D=64, 128 cached + 1 "
+                               "appended, RoPE theta 1e5, scale 1/8, contiguous cache",
+                   "statistic": "median over steps of per-launch CUDA-event time"},
+        "p90_us": lat[int(len(lat) * 0.9)], "gpu_launches": n,
+        "e2e": {"value": e_lat[len(e_lat) // 2], "unit": "us",
+                "h2d_bytes_per_step": (q.size + kn.size + vn.size) * 4,
+                "d2h_bytes_per_step": hq * d * 4},
+        "roofline": None,
+    }
+    if not args.no_cpu:
+        from oracle import oracle as orc
+        orc.build()
+        cos, sin = orc.rope_tables(d, cached + 2, theta)
+        kc = np.zeros((1, hkv, cached + 1, d), np.float32)
+        vc = np.zeros_like(kc)
+        kc[0, :, :cached], vc[0, :, :cached] = k, v
+        cnt, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < min(args.cpu_budget, 5.0) and cnt < 20000:
+            orc.decode_step(q[:, :, None], kn[:, :, None], vn[:, :, None], kc, vc, cached,
+                            cos, sin, threads=1)
+            cnt += 1
+        secs = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": 1e6 * secs / cnt, "unit": "us", "cores": 1,
+                                "kind": "port",
+                                "sample": f"{cnt} config-1 steps of the single-thread oracle "
+                                          f"(RoPE, append, faithful F32 chain)"}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------
 # Prefill workload (BASELINE config 5's prompt phase): the tensor-core prefill attention
 # ------------------------------------------------------------------------------------
 
@@ -717,10 +814,10 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--ref-budget", type=float, default=60.0)
-    ap.add_argument("--workload", choices=["cfg4", "cfg2", "cfg3", "cfg5", "cfg5p"],
+    ap.add_argument("--workload", choices=["cfg4", "cfg1", "cfg2", "cfg3", "cfg5", "cfg5p"],
                     default="cfg4",
                     help="cfg4 (default): the fused attention op; cfg2/3/5: whole-model "
-                         "decode; cfg5p: config 5's prefill attention")
+                         "decode; cfg5p: config 5's prefill attention; cfg1: latency")
     ap.add_argument("--variant", type=int, default=0,
                     help="decode kernel: 0 auto (tensor-core for F16), 1 CUDA-core, 2 tensor-core")
     ap.add_argument("--splits", type=int, default=0, help="split count (0 = automatic)")
@@ -737,6 +834,8 @@ def main() -> None:
         run_reference(args)
     elif args.workload == "cfg5p":
         run_prefill(args)
+    elif args.workload == "cfg1":
+        run_cfg1(args)
     elif args.workload != "cfg4":
         run_decoder(args)
     else:

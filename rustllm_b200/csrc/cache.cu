@@ -21,6 +21,8 @@ int decode_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, cons
                 cudaStream_t stream);
 size_t decode_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t splits);
 int32_t decode_auto_splits(int64_t B, int64_t Hkv, int64_t max_len);
+int32_t decode_auto_splits_lens(const int64_t* lens, int64_t B, int64_t Hkv, int64_t hint,
+                                int per_sm);
 int prefill_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, const void* v_new,
                  const int32_t* q_start, int32_t rows_per_seq, int32_t max_rows,
                  int32_t total_rows, void* out, int32_t q_heads, const tmllm_decode_opts* opts,
@@ -503,10 +505,20 @@ int tmllm_cache_decode(tmllm_cache* cache, int32_t layer, const void* q, const v
                             static_cast<long long>(pos), o.rope_len);
         }
     }
-    const int32_t splits =
-        o.num_splits > 0 ? o.num_splits
-                         : decode_auto_splits(cache->cfg.num_seqs, cache->cfg.num_kv_heads,
-                                              std::max<int64_t>(max_len, o.max_len_hint));
+    int32_t splits = o.num_splits;
+    if (splits <= 0) {
+        // resident CTAs per SM of the kernel that will run: the tensor-core decode keeps
+        // four per SM at head_dim 64, every other configuration two
+        const int G = q_heads / cache->cfg.num_kv_heads;
+        const int per_sm = (cache->cfg.dtype == TMLLM_F16 && cache->cfg.head_dim == 64 &&
+                            o.variant != 1 && G <= 16) ? 4 : 2;
+        std::vector<int64_t> lens(cache->h_lens.begin(), cache->h_lens.end());
+        if (append)
+            for (auto& x : lens) ++x;
+        splits = decode_auto_splits_lens(lens.data(), cache->cfg.num_seqs,
+                                         cache->cfg.num_kv_heads,
+                                         std::max<int64_t>(max_len, o.max_len_hint), per_sm);
+    }
     o.num_splits = splits;
     const size_t need = decode_workspace_bytes(cache->cfg.num_seqs, q_heads,
                                                cache->cfg.num_kv_heads, cache->cfg.head_dim,

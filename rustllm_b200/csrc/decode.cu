@@ -648,7 +648,7 @@ struct MmaCfg {
 };
 
 template <int D, int STAGES>
-__global__ void __launch_bounds__(kDecodeThreads, 2) decode_mma_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(kDecodeThreads, D == 64 ? 4 : 2) decode_mma_kernel(const DecodeArgs a) {
     using Cfg = MmaCfg<D, STAGES>;
     constexpr int C = Cfg::C, ROW = Cfg::ROW, SUBB = Cfg::SUBB, QROW = Cfg::QROW;
     constexpr int KS = D / 16;  // k-steps of QK
@@ -1479,6 +1479,39 @@ int32_t decode_auto_splits(int64_t B, int64_t Hkv, int64_t max_len) {
 }
 
 int32_t decode_auto_splits_bound(int64_t B, int64_t Hkv) { return auto_splits_bound(B, Hkv); }
+
+// Split count for a batch whose lengths the host knows (the cache runtime): the largest count
+// whose CTAs -- ceil(len / chunk) per sequence and KV head, chunk as decode_impl_ex derives
+// it from `hint` -- still fit one wave of resident CTAs (`per_sm` per SM), so the long
+// sequences of a mixed batch are cut without pushing work into a second wave.  The CTA
+// count grows with the split count, so the largest fitting count is found by bisection.
+int32_t decode_auto_splits_lens(const int64_t* lens, int64_t B, int64_t Hkv, int64_t hint,
+                                int per_sm) {
+    const int64_t slots = static_cast<int64_t>(device_sm_count()) * per_sm;
+    if (hint < 1) hint = 1;
+    auto ctas = [&](int64_t s) {
+        int64_t chunk = (hint + s - 1) / s;
+        chunk = ((chunk + 127) / 128) * 128;
+        if (chunk < 128) chunk = 128;
+        int64_t n = 0;
+        for (int64_t b = 0; b < B; ++b) {
+            const int64_t L = lens[b] > 0 ? lens[b] : 1;
+            n += (L + chunk - 1) / chunk;
+        }
+        return n * Hkv;
+    };
+    int64_t hi = (hint + 255) / 256;  // never chunks under 256 positions
+    if (hi > 1024) hi = 1024;
+    if (hi < 1) hi = 1;
+    int64_t lo = 1;
+    if (ctas(1) > slots) return 1;
+    while (lo < hi) {  // largest s in [lo, hi] with ctas(s) <= slots
+        const int64_t mid = (lo + hi + 1) / 2;
+        if (ctas(mid) <= slots) lo = mid;
+        else hi = mid - 1;
+    }
+    return static_cast<int32_t>(lo);
+}
 
 }  // namespace tmllm
 
