@@ -128,6 +128,14 @@ class ClockSampler:
                 "power_w_max": max((num(r[3]) or 0.0) for r in inside)}
 
 
+def profile_region(on: bool) -> None:
+    """With TMLLM_PROFILE_REGION=1 the timed loop is bracketed by cudaProfilerStart/Stop, so
+    a profiler started with --profile-from-start off sees only the timed steps."""
+    if os.environ.get("TMLLM_PROFILE_REGION") == "1":
+        import torch
+        (torch.cuda.profiler.start if on else torch.cuda.profiler.stop)()
+
+
 def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -267,6 +275,7 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    profile_region(True)
     wall0 = time.time()
     t_start.record(stream)
     for i in range(args.steps):
@@ -281,6 +290,7 @@ def run_ours(args) -> None:
         kev[i][1].record(stream)
     t_end.record(stream)
     torch.cuda.synchronize()
+    profile_region(False)
     wall1 = time.time()
     if world > 1:
         dist.barrier()
@@ -418,6 +428,7 @@ def run_decoder(args) -> None:
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     preset, total_seqs, prompt, steps, desc = DECODER_WORKLOADS[args.workload]
+    steps = min(steps, args.steps)  # the config's token count unless fewer are asked for
     prefill_ms = None
     cfg = PRESETS[preset]
     gen = torch.Generator().manual_seed(1234)
@@ -466,12 +477,14 @@ def run_decoder(args) -> None:
     if sampler:
         sampler.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    profile_region(True)
     wall0 = time.time()
     e0.record()
     for _ in range(steps):
         runner.step()
     e1.record()
     torch.cuda.synchronize()
+    profile_region(False)
     wall1 = time.time()
     ms = e0.elapsed_time(e1)
     clocks = sampler.stop(wall0, wall1) if sampler else None
@@ -689,11 +702,13 @@ def run_prefill(args) -> None:
         sampler.start()
     # (1) the hot path as a step: append + attention for all 12 layers
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    profile_region(True)
     wall0 = time.time()
     e0.record(stream)
     for _ in range(args.steps):
         step()
     e1.record(stream)
+    profile_region(False)
     # (2) the attention kernel alone, per launch (attend-only calls)
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps * NL)]

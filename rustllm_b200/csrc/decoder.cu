@@ -76,6 +76,60 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(
     }
 }
 
+// The same operation with one warp per row (8 rows per 256-thread block), the row held in
+// registers as 16-byte chunks of 8 halves: one read of x and residual, one write of the sum
+// and of y, a shuffle reduction.  For F16 rows of hidden % 8 == 0 and hidden <= 2048.
+constexpr int kNormChunks = 8;  // chunks per lane: hidden <= 32 * 8 * 8
+__global__ void __launch_bounds__(256) add_rmsnorm_warp_kernel(
+    const __half* x, const __half* __restrict__ residual, const __half* __restrict__ w,
+    __half* __restrict__ y, __half* sum_out, int64_t rows, int64_t hidden, float eps) {
+    const int64_t row = blockIdx.x * 8LL + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int nc = static_cast<int>(hidden / 8);
+    const uint4* xr = reinterpret_cast<const uint4*>(x + row * hidden);
+    const uint4* rr = residual ? reinterpret_cast<const uint4*>(residual + row * hidden) : nullptr;
+    float v[kNormChunks][8];
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < kNormChunks; ++k) {
+        const int c = lane + 32 * k;
+        if (c >= nc) break;
+        Chunk<__half>::unpack(xr[c], v[k]);
+        if (rr) {
+            float r8[8];
+            Chunk<__half>::unpack(rr[c], r8);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[k][e] = round_store<__half>(__fadd_rn(v[k][e], r8[e]));
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc = fmaf(v[k][e], v[k][e], acc);
+    }
+    acc = warp_sum(acc);
+    const float inv = rsqrtf(acc / static_cast<float>(hidden) + eps);
+    uint4* so = sum_out ? reinterpret_cast<uint4*>(sum_out + row * hidden) : nullptr;
+    uint4* yr = reinterpret_cast<uint4*>(y + row * hidden);
+    const uint4* wr = reinterpret_cast<const uint4*>(w);
+#pragma unroll
+    for (int k = 0; k < kNormChunks; ++k) {
+        const int c = lane + 32 * k;
+        if (c >= nc) break;
+        float w8[8];
+        Chunk<__half>::unpack(wr[c], w8);
+        uint4 ys, ss;
+        __half2* yh = reinterpret_cast<__half2*>(&ys);
+        __half2* sh = reinterpret_cast<__half2*>(&ss);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            yh[e] = __floats2half2_rn(v[k][2 * e] * inv * w8[2 * e],
+                                      v[k][2 * e + 1] * inv * w8[2 * e + 1]);
+            sh[e] = __floats2half2_rn(v[k][2 * e], v[k][2 * e + 1]);
+        }
+        if (so) so[c] = ss;
+        yr[c] = ys;
+    }
+}
+
 // kernels/silu.metal:38-46 on a fused [gate | up] projection: out = half(silu(g) * u),
 // silu(g) = g / (1 + exp(-g)).
 template <typename T>
@@ -88,6 +142,29 @@ __global__ void swiglu_kernel(const T* __restrict__ gu, T* __restrict__ out, int
         const float g = to_f32<T>(gu[r * 2 * inter + c]);
         const float u = to_f32<T>(gu[r * 2 * inter + inter + c]);
         out[i] = from_f32<T>((g / (1.0f + expf(-g))) * u);
+    }
+}
+
+// swiglu_kernel on 8 F16 outputs per thread (16-byte loads of gate and up, one store).
+__global__ void swiglu_vec_kernel(const __half* __restrict__ gu, __half* __restrict__ out,
+                                  int64_t rows, int64_t inter) {
+    const int64_t per_row = inter / 8;
+    const int64_t total = rows * per_row;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / per_row, c = i - r * per_row;
+        const uint4 g4 = __ldg(reinterpret_cast<const uint4*>(gu + r * 2 * inter) + c);
+        const uint4 u4 = __ldg(reinterpret_cast<const uint4*>(gu + r * 2 * inter + inter) + c);
+        float g[8], u[8];
+        Chunk<__half>::unpack(g4, g);
+        Chunk<__half>::unpack(u4, u);
+        uint4 o;
+        __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            oh[e] = __floats2half2_rn((g[2 * e] / (1.0f + expf(-g[2 * e]))) * u[2 * e],
+                                      (g[2 * e + 1] / (1.0f + expf(-g[2 * e + 1]))) * u[2 * e + 1]);
+        reinterpret_cast<uint4*>(out + r * inter)[c] = o;
     }
 }
 
@@ -180,7 +257,15 @@ int tmllm_add_rmsnorm(tmllm_dtype dtype, const void* x, const void* residual, co
     if (rows > 0x7fffffffull) return fail(TMLLM_INVALID_SHAPE, "too many rows");
     if (!x || !weight || !out) return fail(TMLLM_INVALID_ARGUMENT, "null tensor pointer");
     auto s = reinterpret_cast<cudaStream_t>(stream);
-    if (dtype == TMLLM_F16)
+    if (dtype == TMLLM_F16 && hidden % 8 == 0 && hidden <= 32 * kNormChunks * 8 &&
+        aligned16(x) && aligned16(weight) && aligned16(out) &&
+        (!residual || aligned16(residual)) && (!sum_out || aligned16(sum_out))) {
+        add_rmsnorm_warp_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, s>>>(
+            static_cast<const __half*>(x), static_cast<const __half*>(residual),
+            static_cast<const __half*>(weight), static_cast<__half*>(out),
+            static_cast<__half*>(sum_out), static_cast<int64_t>(rows),
+            static_cast<int64_t>(hidden), eps);
+    } else if (dtype == TMLLM_F16)
         add_rmsnorm_kernel<__half><<<static_cast<unsigned>(rows), 256, 0, s>>>(
             static_cast<const __half*>(x), static_cast<const __half*>(residual),
             static_cast<const __half*>(weight), static_cast<__half*>(out),
@@ -202,7 +287,10 @@ int tmllm_swiglu(tmllm_dtype dtype, const void* gate_up, void* out, size_t rows,
     if (!gate_up || !out) return fail(TMLLM_INVALID_ARGUMENT, "null tensor pointer");
     auto s = reinterpret_cast<cudaStream_t>(stream);
     const int64_t total = static_cast<int64_t>(rows * inter);
-    if (dtype == TMLLM_F16)
+    if (dtype == TMLLM_F16 && inter % 8 == 0 && aligned16(gate_up) && aligned16(out))
+        swiglu_vec_kernel<<<grid_rows(total / 8, 256), 256, 0, s>>>(
+            static_cast<const __half*>(gate_up), static_cast<__half*>(out), rows, inter);
+    else if (dtype == TMLLM_F16)
         swiglu_kernel<__half><<<grid_rows(total, 256), 256, 0, s>>>(
             static_cast<const __half*>(gate_up), static_cast<__half*>(out), rows, inter);
     else

@@ -143,6 +143,70 @@ __global__ void prefill_append_kernel(const PrefillArgs a) {
     }
 }
 
+// Vectorised append: one thread per (row, KV head, 16-byte chunk of the first half), so
+// every load and store is 16 bytes (needs D/2 a multiple of a chunk and 16-byte aligned
+// rows, arenas and tables).  Same rotation and rounding as prefill_append_kernel.
+template <typename T>
+__global__ void prefill_append_vec_kernel(const PrefillArgs a) {
+    constexpr int EPC = 16 / sizeof(T);  // elements per chunk
+    const int half = a.head_dim / 2;
+    const int cph = half / EPC;  // chunks per half row
+    const int64_t total = static_cast<int64_t>(a.total_rows) * a.kv_heads * cph;
+    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(idx % cph);
+        const int64_t t = idx / cph;
+        const int kvh = static_cast<int>(t % a.kv_heads);
+        const int row = static_cast<int>(t / a.kv_heads);
+        const int s = seq_of_row(a, row);
+        int row0;
+        seq_rows(a, s, &row0);
+        const int pos = a.seq_lens[s] + (row - row0);
+        const int64_t blk = page_of(a, s, pos);
+        if (blk < 0) continue;
+        const int64_t src = static_cast<int64_t>(row) * a.kv_stride +
+                            static_cast<int64_t>(kvh) * a.head_dim + c * EPC;
+        const int64_t dst =
+            ((blk * a.kv_heads + kvh) * a.block_size + in_page(a, pos)) * a.head_dim + c * EPC;
+        const T* kn = static_cast<const T*>(a.k_new) + src;
+        const T* vn = static_cast<const T*>(a.v_new) + src;
+        T* kd = static_cast<T*>(a.k_cache) + dst;
+        T* vd = static_cast<T*>(a.v_cache) + dst;
+        const uint4 k1 = __ldg(reinterpret_cast<const uint4*>(kn));
+        const uint4 k2 = __ldg(reinterpret_cast<const uint4*>(kn + half));
+        const uint4 v1 = __ldg(reinterpret_cast<const uint4*>(vn));
+        const uint4 v2 = __ldg(reinterpret_cast<const uint4*>(vn + half));
+        float x1[EPC], x2[EPC];
+        Chunk<T>::unpack(k1, x1);
+        Chunk<T>::unpack(k2, x2);
+        const int rp = pos + a.rope_off;
+        if (a.rope_cos != nullptr && rp >= 0 && rp < a.rope_len) {
+            const float* cp = a.rope_cos + static_cast<int64_t>(rp) * half + c * EPC;
+            const float* sp = a.rope_sin + static_cast<int64_t>(rp) * half + c * EPC;
+#pragma unroll
+            for (int e = 0; e < EPC; ++e) {  // kernels/rope.metal:57-63 without contraction
+                const float cs = __ldg(cp + e), sn = __ldg(sp + e);
+                const float y1 = __fsub_rn(__fmul_rn(x1[e], cs), __fmul_rn(x2[e], sn));
+                const float y2 = __fadd_rn(__fmul_rn(x2[e], cs), __fmul_rn(x1[e], sn));
+                x1[e] = y1;
+                x2[e] = y2;
+            }
+        }
+        uint4 o1, o2;
+        T* p1 = reinterpret_cast<T*>(&o1);
+        T* p2 = reinterpret_cast<T*>(&o2);
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) {
+            p1[e] = from_f32<T>(x1[e]);
+            p2[e] = from_f32<T>(x2[e]);
+        }
+        *reinterpret_cast<uint4*>(kd) = o1;
+        *reinterpret_cast<uint4*>(kd + half) = o2;
+        *reinterpret_cast<uint4*>(vd) = v1;
+        *reinterpret_cast<uint4*>(vd + half) = v2;
+    }
+}
+
 // ---- PTX wrappers: mbarrier, TMA, tcgen05 ----------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -1027,14 +1091,23 @@ int prefill_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, con
                     ">= 16 positions and 16-byte aligned q/out/arenas");
     // 1. append (rotated keys, values) at each sequence's cached length
     if (k_new) {
-        const int64_t work = static_cast<int64_t>(total_rows) * Hkv * (D / 2);
+        const int epc = static_cast<int>(16 / es);
+        const bool vec = (D / 2) % epc == 0 && aligned16(k_new) && aligned16(v_new) &&
+                         aligned16(kv->k_cache) && aligned16(kv->v_cache) &&
+                         (a.kv_stride * static_cast<int64_t>(es)) % 16 == 0;
+        const int64_t work = static_cast<int64_t>(total_rows) * Hkv * (D / 2) / (vec ? epc : 1);
         int64_t blocks = (work + 255) / 256;
         const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
         if (blocks > cap) blocks = cap;
-        if (kv->dtype == TMLLM_F16)
-            prefill_append_kernel<__half><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
+        const unsigned nb = static_cast<unsigned>(blocks);
+        if (vec && kv->dtype == TMLLM_F16)
+            prefill_append_vec_kernel<__half><<<nb, 256, 0, stream>>>(a);
+        else if (vec)
+            prefill_append_vec_kernel<float><<<nb, 256, 0, stream>>>(a);
+        else if (kv->dtype == TMLLM_F16)
+            prefill_append_kernel<__half><<<nb, 256, 0, stream>>>(a);
         else
-            prefill_append_kernel<float><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
+            prefill_append_kernel<float><<<nb, 256, 0, stream>>>(a);
         TMLLM_LAUNCH_TRY();
     }
     // 2. attention over the cache, new rows included

@@ -44,17 +44,19 @@ def test_embedding_gathers_rows(cuda):
     assert int(bad) == 1 and torch.count_nonzero(out[2]) == 0
 
 
-@pytest.mark.parametrize("hidden", [576, 960, 100])
+@pytest.mark.parametrize("hidden", [576, 960, 100, 2048, 2056])
 def test_add_rmsnorm_matches_float32(cuda, hidden):
-    x = torch.randn((3, hidden), device=cuda).half()
-    r = torch.randn((3, hidden), device=cuda).half()
+    """Warp-per-row kernel (hidden % 8 == 0, <= 2048) and the block-per-row kernel."""
+    rows = 17
+    x = torch.randn((rows, hidden), device=cuda).half()
+    r = torch.randn((rows, hidden), device=cuda).half()
     w = (torch.rand(hidden, device=cuda) + 0.5).half()
     out = torch.empty_like(x)
     s = (x.float() + r.float()).half()
     want = s.float() * torch.rsqrt((s.float() ** 2).mean(-1, keepdim=True) + 1e-5) * w.float()
     xs = x.clone()
     _lib.call("tmllm_add_rmsnorm", 1, xs.data_ptr(), r.data_ptr(), w.data_ptr(), out.data_ptr(),
-              xs.data_ptr(), 3, hidden, 1e-5, stream(cuda))  # in-place residual update
+              xs.data_ptr(), rows, hidden, 1e-5, stream(cuda))  # in-place residual update
     assert torch.equal(xs, s)
     assert rel(out, want) < 1e-2
     with pytest.raises(rb.InvalidShape):
@@ -62,11 +64,13 @@ def test_add_rmsnorm_matches_float32(cuda, hidden):
                   3, hidden, 0.0, stream(cuda))
 
 
-def test_swiglu_matches_float32(cuda):
-    gu = torch.randn((4, 2 * 300), device=cuda).half()
-    out = torch.empty((4, 300), dtype=torch.float16, device=cuda)
-    _lib.call("tmllm_swiglu", 1, gu.data_ptr(), out.data_ptr(), 4, 300, stream(cuda))
-    g, u = gu[:, :300].float(), gu[:, 300:].float()
+@pytest.mark.parametrize("inter", [300, 320])
+def test_swiglu_matches_float32(cuda, inter):
+    """Scalar (300) and 16-byte vector (320) kernels."""
+    gu = torch.randn((4, 2 * inter), device=cuda).half()
+    out = torch.empty((4, inter), dtype=torch.float16, device=cuda)
+    _lib.call("tmllm_swiglu", 1, gu.data_ptr(), out.data_ptr(), 4, inter, stream(cuda))
+    g, u = gu[:, :inter].float(), gu[:, inter:].float()
     assert rel(out, g * torch.sigmoid(g) * u) < 1e-2
 
 
