@@ -528,6 +528,75 @@ def run_decoder(args) -> None:
 
 
 # ------------------------------------------------------------------------------------
+# Config 3's attention op alone: batched paged decode over mixed lengths
+# ------------------------------------------------------------------------------------
+
+def run_cfg3_attention(args) -> None:
+    import torch
+
+    import rustllm_b200 as rb
+
+    world, rank, local = dist_env()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B, hq, hkv, d, layers = 64, 15, 5, 64, 4
+    gen = torch.Generator().manual_seed(1234)
+    lens = torch.randint(256, 2049, (B,), generator=gen).tolist()  # config 3's contexts
+    cache = rb.PagedKvCache(layers, B, max(lens) + 2, hkv, d, dtype=torch.float16,
+                            block_size=16, shuffle_seed=11, device=dev)
+    g = torch.Generator(device=dev).manual_seed(100)
+    for layer in range(layers):
+        for s, n in enumerate(lens):
+            cache.append(layer, s, torch.randn((hkv, n, d), generator=g, device=dev).half(),
+                         torch.randn((hkv, n, d), generator=g, device=dev).half())
+    for s, n in enumerate(lens):
+        cache.advance(n, s)
+    q = torch.randn((B, hq, d), generator=g, device=dev).half()
+    kn = torch.randn((B, hkv, d), generator=g, device=dev).half()
+    vn = torch.randn((B, hkv, d), generator=g, device=dev).half()
+    out = torch.empty((B, hq, d), dtype=torch.float16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for i in range(max(args.warmup, 3)):
+        cache.decode(i % layers, q, kn, vn, out=out)
+    torch.cuda.synchronize()
+    n = max(args.steps, 1)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(n)]
+    profile_region(True)
+    for i, (a, b) in enumerate(ev):  # lengths stay put: every step is the same op
+        a.record(stream)
+        cache.decode(i % layers, q, kn, vn, out=out)
+        b.record(stream)
+    torch.cuda.synchronize()
+    profile_region(False)
+    k_ms = sum(a.elapsed_time(b) for a, b in ev) / n
+    L = [x + 1 for x in lens]
+    launch_bytes = sum(2 * hkv * x * d * 2 for x in L) + B * (2 * hq * d + 4 * hkv * d) * 2
+    peaks = load_peaks()
+    achieved = launch_bytes / (k_ms * 1e-3) / 1e9
+    line = {
+        "metric": "batched decode attention tok/s (fused append + paged GQA attention)",
+        "value": B / (k_ms * 1e-3), "unit": "tok/s", "n_gpus": 1, "steps": n,
+        "warmup": max(args.warmup, 3), "ms_per_step": k_ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded N(0,1) K/V, q; random block permutation)",
+        "config": {"workload": "cfg3 attention op: 64 sequences, contexts U[256,2048] (seeded), "
+                               "Hq 15 / Hkv 5 / D 64, 16-token pages, one appended token each",
+                   "l2": f"{layers} layers cycled: {layers * launch_bytes / 1e6:.0f} MB of K/V "
+                         f"per cycle vs 126 MB L2"},
+        "gpu_launches": n,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                     "peak_source": peaks["source"], "traffic": None,
+                     "kernel": "decode_mma_kernel<64,3>", "kernel_ms": k_ms,
+                     "bytes_per_launch": launch_bytes},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------
 # Config 1: the reference's own CPU-runnable case, a latency figure (no roofline claim)
 # ------------------------------------------------------------------------------------
 
@@ -829,10 +898,12 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--ref-budget", type=float, default=60.0)
-    ap.add_argument("--workload", choices=["cfg4", "cfg1", "cfg2", "cfg3", "cfg5", "cfg5p"],
+    ap.add_argument("--workload",
+                    choices=["cfg4", "cfg1", "cfg2", "cfg3", "cfg3a", "cfg5", "cfg5p"],
                     default="cfg4",
                     help="cfg4 (default): the fused attention op; cfg2/3/5: whole-model "
-                         "decode; cfg5p: config 5's prefill attention; cfg1: latency")
+                         "decode; cfg3a: config 3's attention op; cfg5p: config 5's prefill "
+                         "attention; cfg1: latency")
     ap.add_argument("--variant", type=int, default=0,
                     help="decode kernel: 0 auto (tensor-core for F16), 1 CUDA-core, 2 tensor-core")
     ap.add_argument("--splits", type=int, default=0, help="split count (0 = automatic)")
@@ -851,6 +922,8 @@ def main() -> None:
         run_prefill(args)
     elif args.workload == "cfg1":
         run_cfg1(args)
+    elif args.workload == "cfg3a":
+        run_cfg3_attention(args)
     elif args.workload != "cfg4":
         run_decoder(args)
     else:
