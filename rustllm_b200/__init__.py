@@ -4,8 +4,9 @@ The compute lives in ``libtmllm_b200.so`` (C ABI: ``include/tmllm.h``); this pac
 host-side mirror of the reference's Rust call surface on torch CUDA tensors.
 """
 from ._lib import (DeviceError, DeviceTimeout, InvalidArgument, InvalidDimension, InvalidShape,
-                   ModelFormat, NonContiguousTensor, NotReserved, OutOfBlocks, PositionOutOfRange,
-                   ShapeMismatch, TinyError, UnsupportedDType, load)
+                   IoError, MissingWeight, ModelFormat, NonContiguousTensor, NotReserved,
+                   OutOfBlocks, PositionOutOfRange, ShapeMismatch, TinyError, UnsupportedDType,
+                   load)
 from .attention import (DecodeWorkspace, auto_splits, gqa_decode, gqa_prefill, merge_lse,
                         paged_kv_from_tensors, prefill_status)
 from .kv_cache import KvCache, LayerKvCache, PagedKvCache
@@ -16,7 +17,8 @@ from .tensor_ops import (attention_core, attention_scale_mask, batched_matmul, c
 __all__ = [
     "TinyError", "InvalidArgument", "InvalidShape", "ShapeMismatch", "InvalidDimension",
     "UnsupportedDType", "NonContiguousTensor", "PositionOutOfRange", "ModelFormat",
-    "DeviceError", "OutOfBlocks", "DeviceTimeout", "NotReserved", "load",
+    "DeviceError", "OutOfBlocks", "DeviceTimeout", "NotReserved", "IoError", "MissingWeight",
+    "load",
     "DecodeWorkspace", "auto_splits", "gqa_decode", "gqa_prefill", "merge_lse",
     "paged_kv_from_tensors", "prefill_status",
     "KvCache", "LayerKvCache", "PagedKvCache",

@@ -82,6 +82,14 @@ class NotReserved(TinyError):
     status = 12
 
 
+class IoError(TinyError):
+    """TinyError::Io (src/error.rs:30): a file could not be read or written (host only)."""
+
+
+class MissingWeight(TinyError):
+    """TinyError::MissingWeight (src/error.rs:36): a weight the model needs is absent."""
+
+
 _BY_STATUS = {cls.status: cls for cls in (
     InvalidArgument, InvalidShape, ShapeMismatch, InvalidDimension, UnsupportedDType,
     NonContiguousTensor, PositionOutOfRange, ModelFormat, DeviceError, OutOfBlocks,

@@ -48,16 +48,29 @@ class ModelConfig:
         return self.hidden_size // self.num_heads
 
     def validate(self) -> None:
-        """src/model/config.rs:24-105."""
-        if min(self.vocab_size, self.hidden_size, self.intermediate_size, self.num_layers,
-               self.num_heads, self.num_kv_heads, self.max_seq_len) <= 0:
-            raise _lib.InvalidShape("model dimensions must be positive")
-        if self.hidden_size % self.num_heads or self.num_heads % self.num_kv_heads:
-            raise _lib.InvalidShape("hidden size must divide into heads and heads into KV heads")
+        """src/model/config.rs:24-105, same checks, order, error kinds and messages."""
+        for value, what in ((self.vocab_size, "vocab size"), (self.hidden_size, "hidden size"),
+                            (self.intermediate_size, "intermediate size"),
+                            (self.num_layers, "number of layers"),
+                            (self.num_heads, "number of attention heads"),
+                            (self.num_kv_heads, "number of key/value attention heads")):
+            if value <= 0:
+                raise _lib.InvalidShape(f"{what} cannot be zero")
+        if self.hidden_size % self.num_heads:
+            raise _lib.InvalidShape(f"hidden size {self.hidden_size} must be divisible by "
+                                    f"num_heads {self.num_heads}")
         if self.head_dim % 2:
-            raise _lib.InvalidShape("RoPE needs an even head dimension")
-        if not (self.rms_norm_eps > 0) or not (self.rope_theta > 0):
-            raise _lib.InvalidShape("rms_norm_eps and rope_theta must be positive")
+            raise _lib.InvalidShape(f"RoPE requires an even head dimension, got {self.head_dim}")
+        if self.max_seq_len <= 0:
+            raise _lib.InvalidShape("max sequence length cannot be zero")
+        if not math.isfinite(self.rms_norm_eps) or self.rms_norm_eps <= 0:
+            raise _lib.InvalidShape("RMSNorm epsilon must be positive and finite, got "
+                                    f"{self.rms_norm_eps}")
+        if not math.isfinite(self.rope_theta) or self.rope_theta <= 0:
+            raise _lib.InvalidShape(f"RoPE theta must be positive and finite, got {self.rope_theta}")
+        if self.num_heads % self.num_kv_heads:
+            raise _lib.ModelFormat(f"num_heads {self.num_heads} must be divisible by "
+                                   f"num_kv_heads {self.num_kv_heads}")
 
     def weight_params(self) -> int:
         h, i, d = self.hidden_size, self.intermediate_size, self.head_dim
@@ -103,6 +116,82 @@ class DecoderWeights:
         self.final_norm = torch.ones(h, dtype=dtype, device=dev)
         self.lm_head = rnd(h, cfg.vocab_size)
         self.dtype = dtype
+
+    @classmethod
+    def from_weights(cls, cfg: ModelConfig, weights, *, device=None,
+                     dtype=None) -> "DecoderWeights":
+        """Transformer::from_weights (src/model/transformer.rs:203-318): the reference's
+        tensor names and [in, out] shapes, each checked as take_tensor / take_linear do
+        (:333-398); q/k/v and gate/up are concatenated along `out` into the fused matrices.
+        ``weights`` is a ``rustllm_b200.weights.ModelWeights`` (consumed).  INT8 linears
+        (the reference's QuantizedLinear path) are not supported by this decoder."""
+        import numpy as np
+        cfg.validate()
+        dev = torch.device(device or "cuda")
+        dtype = dtype or torch.float16
+        h, i = cfg.hidden_size, cfg.intermediate_size
+        qp, kvp = cfg.num_heads * cfg.head_dim, cfg.num_kv_heads * cfg.head_dim
+
+        def take(name, shape):
+            t = weights.take(name)
+            if tuple(t.shape) != tuple(shape):
+                raise _lib.InvalidShape(f"weight {name} has shape {list(t.shape)}, expected "
+                                        f"{list(shape)}")
+            if t.data.dtype == np.int8:
+                raise _lib.ModelFormat(f"INT8 weight {name}: quantized linear layers are not "
+                                       "supported by this decoder")
+            return torch.from_numpy(np.ascontiguousarray(t.data)).to(dev, dtype)
+
+        self = cls.__new__(cls)
+        self.embedding = take("token_embedding.weight", (cfg.vocab_size, h))
+        self.layers = []
+        for li in range(cfg.num_layers):
+            p = f"layers.{li}"
+            wq = take(f"{p}.attention.q_proj.weight", (h, qp))
+            wk = take(f"{p}.attention.k_proj.weight", (h, kvp))
+            wv = take(f"{p}.attention.v_proj.weight", (h, kvp))
+            wo = take(f"{p}.attention.out_proj.weight", (qp, h))
+            an = take(f"{p}.attention_norm.weight", (h,))
+            mn = take(f"{p}.mlp_norm.weight", (h,))
+            wg = take(f"{p}.mlp.gate_proj.weight", (h, i))
+            wu = take(f"{p}.mlp.up_proj.weight", (h, i))
+            wd = take(f"{p}.mlp.down_proj.weight", (i, h))
+            self.layers.append({"attn_norm": an, "wqkv": torch.cat([wq, wk, wv], 1).contiguous(),
+                                "wo": wo, "mlp_norm": mn,
+                                "wgu": torch.cat([wg, wu], 1).contiguous(), "wd": wd})
+        self.final_norm = take("final_norm.weight", (h,))
+        self.lm_head = take("lm_head.weight", (h, cfg.vocab_size))
+        self.dtype = dtype
+        return self
+
+    def to_weights(self, cfg: ModelConfig):
+        """The inverse of ``from_weights``: a ModelWeights with the reference's names
+        (F16 tensors when the decoder is F16, F32 otherwise), e.g. to write a model.bin."""
+        from .weights import ModelWeights
+        qp, kvp = cfg.num_heads * cfg.head_dim, cfg.num_kv_heads * cfg.head_dim
+        i = cfg.intermediate_size
+        out = ModelWeights()
+        put = out.insert_f16 if self.dtype == torch.float16 else out.insert_f32
+
+        def add(name, t):
+            a = t.detach().cpu()
+            put(name, tuple(a.shape), a.numpy())
+
+        add("token_embedding.weight", self.embedding)
+        for li, L in enumerate(self.layers):
+            p = f"layers.{li}"
+            add(f"{p}.attention.q_proj.weight", L["wqkv"][:, :qp])
+            add(f"{p}.attention.k_proj.weight", L["wqkv"][:, qp:qp + kvp])
+            add(f"{p}.attention.v_proj.weight", L["wqkv"][:, qp + kvp:])
+            add(f"{p}.attention.out_proj.weight", L["wo"])
+            add(f"{p}.attention_norm.weight", L["attn_norm"])
+            add(f"{p}.mlp_norm.weight", L["mlp_norm"])
+            add(f"{p}.mlp.gate_proj.weight", L["wgu"][:, :i])
+            add(f"{p}.mlp.up_proj.weight", L["wgu"][:, i:])
+            add(f"{p}.mlp.down_proj.weight", L["wd"])
+        add("final_norm.weight", self.final_norm)
+        add("lm_head.weight", self.lm_head)
+        return out
 
 
 class Decoder:

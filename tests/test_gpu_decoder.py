@@ -171,3 +171,23 @@ def test_prefill_then_decode_matches_stepwise(cuda):
         dec.ids.copy_(nxt)
         dec.forward_step()
     assert rel(a.logits, b.logits) < 2e-2
+
+
+def test_model_dir_round_trip_gives_identical_logits(cuda, tmp_path):
+    """A model written as the reference's model.bin + config.json and loaded back
+    (Transformer::load, transformer.rs:193-201) decodes exactly like the original."""
+    from rustllm_b200.weights import load_model_dir, save_config_json
+    w = DecoderWeights(TINY, device=cuda, seed=13, std=0.08)
+    w.to_weights(TINY).save(tmp_path / "model.bin")
+    save_config_json(TINY, tmp_path / "config.json")
+    cfg, w2 = load_model_dir(tmp_path, device=cuda)
+    assert cfg == TINY
+    prompts = torch.randint(0, TINY.vocab_size, (2, 20), generator=torch.Generator().manual_seed(14))
+    a, b = Decoder(TINY, w, 2, device=cuda), Decoder(cfg, w2, 2, device=cuda)
+    assert torch.equal(a.prefill(prompts.to(cuda)), b.prefill(prompts.to(cuda)))
+    assert torch.equal(a.logits, b.logits)
+    with pytest.raises(rb.InvalidShape, match="has shape"):
+        bad = w.to_weights(TINY)
+        bad["lm_head.weight"].data = bad["lm_head.weight"].data[:, :10].copy()
+        bad["lm_head.weight"].shape = (TINY.hidden_size, 10)
+        DecoderWeights.from_weights(TINY, bad, device=cuda)
