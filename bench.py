@@ -748,10 +748,14 @@ def run_prefill(args) -> None:
               outs[li].data_ptr()) for li in range(NL)]
     fn = lib.tmllm_gqa_prefill
 
-    def launch(li, append=True):
+    # RoPE off: the call is the attention kernel alone (with RoPE and an F16 output the
+    # query rotation runs in the append kernel first), used to time that kernel by itself
+    opts_plain = _lib.DecodeOpts(q_seq_stride=H * d, kv_seq_stride=H * d)
+
+    def launch(li, append=True, rope_on=True):
         kv, q, k, v, o = calls[li]
         rc = fn(kv, q, k if append else None, v if append else None, None, S, 0, 0, o, H,
-                C.byref(opts), sp)
+                C.byref(opts if rope_on else opts_plain), sp)
         if rc:
             _lib.check(rc)
 
@@ -778,14 +782,15 @@ def run_prefill(args) -> None:
         step()
     e1.record(stream)
     profile_region(False)
-    # (2) the attention kernel alone, per launch (attend-only calls)
+    # (2) the attention kernel alone, per launch (attend-only calls without RoPE: the same
+    # kernel and work, and no other launch inside the events)
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps * NL)]
     i = 0
     for _ in range(args.steps):
         for li in range(NL):
             kev[i][0].record(stream)
-            launch(li, append=False)
+            launch(li, append=False, rope_on=False)
             kev[i][1].record(stream)
             i += 1
     torch.cuda.synchronize()

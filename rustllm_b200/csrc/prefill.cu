@@ -46,6 +46,7 @@ struct PrefillArgs {
     void* k_cache;
     void* v_cache;
     void* out;
+    void* q_rot;  // when set, the append kernel also writes RoPE'd q here ([rows, Hq*D] F16)
     const int32_t* block_table;
     const int32_t* seq_lens;  // cached length of each sequence before this chunk
     const int32_t* q_start;   // [num_seqs + 1] row offsets, or null: uniform rows per sequence
@@ -145,37 +146,50 @@ __global__ void prefill_append_kernel(const PrefillArgs a) {
 
 // Vectorised append: one thread per (row, KV head, 16-byte chunk of the first half), so
 // every load and store is 16 bytes (needs D/2 a multiple of a chunk and 16-byte aligned
-// rows, arenas and tables).  Same rotation and rounding as prefill_append_kernel.
+// rows, arenas and tables).  Same rotation and rounding as prefill_append_kernel.  With
+// `q_rot` set it also rotates the query rows (one thread per row, query head and chunk)
+// into q_rot, so the attention kernel can load them rotated; without k_new it does only
+// that.
 template <typename T>
 __global__ void prefill_append_vec_kernel(const PrefillArgs a) {
     constexpr int EPC = 16 / sizeof(T);  // elements per chunk
     const int half = a.head_dim / 2;
     const int cph = half / EPC;  // chunks per half row
-    const int64_t total = static_cast<int64_t>(a.total_rows) * a.kv_heads * cph;
-    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int c = static_cast<int>(idx % cph);
-        const int64_t t = idx / cph;
-        const int kvh = static_cast<int>(t % a.kv_heads);
-        const int row = static_cast<int>(t / a.kv_heads);
+    const int64_t kv_items = a.k_new ? static_cast<int64_t>(a.total_rows) * a.kv_heads * cph : 0;
+    const int64_t q_items = a.q_rot ? static_cast<int64_t>(a.total_rows) * a.q_heads * cph : 0;
+    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+         idx < kv_items + q_items; idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const bool is_q = idx >= kv_items;
+        const int64_t id = is_q ? idx - kv_items : idx;
+        const int heads = is_q ? a.q_heads : a.kv_heads;
+        const int c = static_cast<int>(id % cph);
+        const int64_t t = id / cph;
+        const int hh = static_cast<int>(t % heads);
+        const int row = static_cast<int>(t / heads);
         const int s = seq_of_row(a, row);
         int row0;
         seq_rows(a, s, &row0);
         const int pos = a.seq_lens[s] + (row - row0);
-        const int64_t blk = page_of(a, s, pos);
-        if (blk < 0) continue;
-        const int64_t src = static_cast<int64_t>(row) * a.kv_stride +
-                            static_cast<int64_t>(kvh) * a.head_dim + c * EPC;
-        const int64_t dst =
-            ((blk * a.kv_heads + kvh) * a.block_size + in_page(a, pos)) * a.head_dim + c * EPC;
-        const T* kn = static_cast<const T*>(a.k_new) + src;
-        const T* vn = static_cast<const T*>(a.v_new) + src;
-        T* kd = static_cast<T*>(a.k_cache) + dst;
-        T* vd = static_cast<T*>(a.v_cache) + dst;
-        const uint4 k1 = __ldg(reinterpret_cast<const uint4*>(kn));
-        const uint4 k2 = __ldg(reinterpret_cast<const uint4*>(kn + half));
-        const uint4 v1 = __ldg(reinterpret_cast<const uint4*>(vn));
-        const uint4 v2 = __ldg(reinterpret_cast<const uint4*>(vn + half));
+        const T* src;
+        T* dst;
+        int64_t blk = 0;
+        if (is_q) {
+            src = static_cast<const T*>(a.q) + static_cast<int64_t>(row) * a.q_stride +
+                  static_cast<int64_t>(hh) * a.head_dim + c * EPC;
+            dst = static_cast<T*>(a.q_rot) +
+                  static_cast<int64_t>(row) * a.q_heads * a.head_dim +
+                  static_cast<int64_t>(hh) * a.head_dim + c * EPC;
+        } else {
+            blk = page_of(a, s, pos);
+            if (blk < 0) continue;
+            src = static_cast<const T*>(a.k_new) + static_cast<int64_t>(row) * a.kv_stride +
+                  static_cast<int64_t>(hh) * a.head_dim + c * EPC;
+            dst = static_cast<T*>(a.k_cache) +
+                  ((blk * a.kv_heads + hh) * a.block_size + in_page(a, pos)) * a.head_dim +
+                  c * EPC;
+        }
+        const uint4 k1 = __ldg(reinterpret_cast<const uint4*>(src));
+        const uint4 k2 = __ldg(reinterpret_cast<const uint4*>(src + half));
         float x1[EPC], x2[EPC];
         Chunk<T>::unpack(k1, x1);
         Chunk<T>::unpack(k2, x2);
@@ -200,10 +214,16 @@ __global__ void prefill_append_vec_kernel(const PrefillArgs a) {
             p1[e] = from_f32<T>(x1[e]);
             p2[e] = from_f32<T>(x2[e]);
         }
-        *reinterpret_cast<uint4*>(kd) = o1;
-        *reinterpret_cast<uint4*>(kd + half) = o2;
-        *reinterpret_cast<uint4*>(vd) = v1;
-        *reinterpret_cast<uint4*>(vd + half) = v2;
+        *reinterpret_cast<uint4*>(dst) = o1;
+        *reinterpret_cast<uint4*>(dst + half) = o2;
+        if (!is_q) {  // the value row is copied as it is
+            const int64_t vs = static_cast<int64_t>(row) * a.kv_stride +
+                               static_cast<int64_t>(hh) * a.head_dim + c * EPC;
+            const T* vn = static_cast<const T*>(a.v_new) + vs;
+            T* vd = static_cast<T*>(a.v_cache) + (dst - static_cast<T*>(a.k_cache));
+            *reinterpret_cast<uint4*>(vd) = __ldg(reinterpret_cast<const uint4*>(vn));
+            *reinterpret_cast<uint4*>(vd + half) = __ldg(reinterpret_cast<const uint4*>(vn + half));
+        }
     }
 }
 
@@ -393,8 +413,10 @@ struct TcCfg {
     static constexpr int OFF_V = 3 * TILE;          // 2 stages
     static constexpr int OFF_P = 5 * TILE;          // 128 x 128 F16, two 64-key blocks
     static constexpr int OFF_BAR = OFF_P + 2 * BLK;
-    static constexpr int SMEM = OFF_BAR + 128;
-    static constexpr int TMEM_COLS = 256;           // S: columns [0,128), O: [128, 128 + D)
+    static constexpr int SMEM = OFF_BAR + 256;
+    // S: columns [0, 128); two O buffers (consecutive units alternate): [128, 128 + D) and
+    // [128 + D, 128 + 2D)
+    static constexpr int TMEM_COLS = D == 64 ? 256 : 512;
     static constexpr int MIN_BLOCKS = D == 64 ? 2 : 1;
 };
 
@@ -404,11 +426,11 @@ struct TcCfg {
 //   QE  Q tile no longer read (MMA)        KF/VF[st]  K/V stage loaded (TMA)
 //   KE[st] K/V stage no longer read (MMA)  S   S = Q K^T done (MMA)
 //   F   S copied to registers (softmax)    P   P tile written (softmax)
-//   O   O += P V done (MMA)                E   O copied out by the epilogue (softmax)
+//   O[b] O_b += P V done (MMA)             E[b] O_b copied out by the epilogue (softmax)
 //   RL  the unit's RoPE table rows landed in the P buffer (TMA, head_dim 64)
 enum : int {
     BAR_QL = 0, BAR_Q = 1, BAR_QE = 2, BAR_KF = 3, BAR_VF = 5, BAR_KE = 7, BAR_S = 9,
-    BAR_F = 10, BAR_P = 11, BAR_O = 12, BAR_E = 13, BAR_RL = 14, NBARS = 15
+    BAR_F = 10, BAR_P = 11, BAR_O = 12, BAR_E = 14, BAR_RL = 16, NBARS = 17
 };
 
 // One unit of work: 128 query rows of one (query head, sequence).  Units are numbered
@@ -472,8 +494,10 @@ __global__ void __launch_bounds__(kPrefillThreads, TcCfg<D>::MIN_BLOCKS)
         mbar_init(bar(BAR_S), 1);
         mbar_init(bar(BAR_F), kSoftmaxThreads);
         mbar_init(bar(BAR_P), kSoftmaxThreads);
-        mbar_init(bar(BAR_O), 1);
-        mbar_init(bar(BAR_E), kSoftmaxThreads);
+        for (int ob = 0; ob < 2; ++ob) {
+            mbar_init(bar(BAR_O + ob), 1);
+            mbar_init(bar(BAR_E + ob), kSoftmaxThreads);
+        }
         mbar_init(bar(BAR_RL), 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -490,7 +514,7 @@ __global__ void __launch_bounds__(kPrefillThreads, TcCfg<D>::MIN_BLOCKS)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t tmem_s = tmem;
-    const uint32_t tmem_o = tmem + 128;
+    auto tmem_o = [&](int ob) { return tmem + 128u + static_cast<uint32_t>(ob * D); };
     const unsigned long long t0 = global_ns();
     constexpr unsigned FULL = 0xffffffffu;
 
@@ -505,15 +529,18 @@ __global__ void __launch_bounds__(kPrefillThreads, TcCfg<D>::MIN_BLOCKS)
         const uint32_t tile_bytes = static_cast<uint32_t>(nbox) * box_bytes * Cfg::NB;
         bool ok = true;
         int g = 0, it = 0;
+        int pv[2] = {0, 0};  // P V products issued into each O buffer by earlier units
         Unit u;
         for (int k = 0; ok && unit_of(a, k, num_units, row_tiles, u); ++k) {
             if (u.nt == 0) continue;
             if (lane == 0) {
                 if (it > 0) ok = mbar_wait(bar(BAR_QE), (it - 1) & 1, abort_flag, t0);
                 if (ok) mbar_arrive_tx(bar(BAR_QL), static_cast<uint32_t>(Cfg::TILE));
-                // the RoPE rows go to the P buffer, free once the last P V has completed
+                // the RoPE rows go to the P buffer, free once the previous unit's last P V
+                // (into the other O buffer) has completed
                 if (ok && a.rope_tma) {
-                    if (it > 0) ok = mbar_wait(bar(BAR_O), (g - 1) & 1, abort_flag, t0);
+                    const int pb = (it & 1) ^ 1;
+                    if (it > 0) ok = mbar_wait(bar(BAR_O + pb), (pv[pb] - 1) & 1, abort_flag, t0);
                     if (ok) {
                         mbar_arrive_tx(bar(BAR_RL), 2u * Cfg::BLK);
                         const int y = u.cached + u.q_lo + a.rope_off;
@@ -554,6 +581,7 @@ __global__ void __launch_bounds__(kPrefillThreads, TcCfg<D>::MIN_BLOCKS)
                     }
                 }
             }
+            pv[it & 1] += u.nt;
             ++it;
         }
     } else if (warp == 5) {
@@ -570,27 +598,42 @@ __global__ void __launch_bounds__(kPrefillThreads, TcCfg<D>::MIN_BLOCKS)
                            IDESC_QK, kk > 0);
                 }
             };
-            auto issue_pv = [&](int st, bool acc) {
+            auto issue_pv = [&](int st, bool acc, int ob) {
                 const uint32_t pa = sbase + Cfg::OFF_P, va = sbase + Cfg::OFF_V + st * Cfg::TILE;
 #pragma unroll
                 for (int kk = 0; kk < kTile / 16; ++kk) {
                     const uint32_t aoff = (kk >> 2) * Cfg::BLK + (kk & 3) * 32;
-                    tc_mma(tmem_o, sw128_desc(pa + aoff, 16, 1024),
+                    tc_mma(tmem_o(ob), sw128_desc(pa + aoff, 16, 1024),
                            sw128_desc(va + kk * 2048, Cfg::BLK, 1024), IDESC_PV, acc || kk > 0);
                 }
             };
+            // Without RoPE in this kernel the raw Q tile is the operand, so its TMA barrier
+            // (QL) is enough, and a unit's first Q K^T is issued during the previous unit's
+            // last softmax (as soon as S is copied out), not after its P.
+            const bool q_by_tma = a.rope_cos == nullptr;
+            const int qbar = q_by_tma ? BAR_QL : BAR_Q;
             bool ok = true;
             int g = 0, it = 0;
-            Unit u;
-            for (int k = 0; ok && unit_of(a, k, num_units, row_tiles, u); ++k) {
-                if (u.nt == 0) continue;
-                // S is free: the previous tile's P arrived, which follows its S copy
-                ok = mbar_wait(bar(BAR_Q), it & 1, abort_flag, t0) &&
-                     mbar_wait(bar(BAR_KF + (g & 1)), (g >> 1) & 1, abort_flag, t0);
-                if (!ok) break;
-                tc_fence_after();
-                issue_qk(g & 1);
-                tc_commit(bar(BAR_S));
+            bool qk0_issued = false;  // the current unit's first Q K^T is already issued
+            Unit u, nxt;
+            int kn = 0;  // unit search position for the look-ahead
+            auto next_unit = [&](int from, Unit& out) -> int {  // index of the next non-empty unit
+                for (int kk = from; unit_of(a, kk, num_units, row_tiles, out); ++kk)
+                    if (out.nt > 0) return kk;
+                return -1;
+            };
+            for (int k = next_unit(0, u); ok && k >= 0; k = kn) {
+                kn = next_unit(k + 1, nxt);
+                if (!qk0_issued) {
+                    // S is free: the previous tile's P arrived, which follows its S copy
+                    ok = mbar_wait(bar(qbar), it & 1, abort_flag, t0) &&
+                         mbar_wait(bar(BAR_KF + (g & 1)), (g >> 1) & 1, abort_flag, t0);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_qk(g & 1);
+                    tc_commit(bar(BAR_S));
+                }
+                qk0_issued = false;
                 for (int j = 0; j < u.nt; ++j, ++g) {
                     const int st = g & 1;
                     if (j + 1 < u.nt) {
@@ -604,18 +647,31 @@ __global__ void __launch_bounds__(kPrefillThreads, TcCfg<D>::MIN_BLOCKS)
                         tc_commit(bar(BAR_S));
                     } else {
                         tc_commit(bar(BAR_QE));  // the Q tile is free once these QKs finish
+                        if (q_by_tma && kn >= 0) {  // the next unit's first Q K^T, early
+                            ok = mbar_wait(bar(BAR_F), g & 1, abort_flag, t0) &&
+                                 mbar_wait(bar(BAR_QL), (it + 1) & 1, abort_flag, t0) &&
+                                 mbar_wait(bar(BAR_KF + (st ^ 1)), ((g + 1) >> 1) & 1, abort_flag, t0);
+                            if (!ok) break;
+                            tc_fence_after();
+                            issue_qk(st ^ 1);
+                            tc_commit(bar(BAR_S));
+                            qk0_issued = true;
+                        }
                     }
                     ok = mbar_wait(bar(BAR_P), g & 1, abort_flag, t0) &&
                          mbar_wait(bar(BAR_VF + st), (g >> 1) & 1, abort_flag, t0);
-                    if (ok && j == 0 && it > 0)  // O is free once the last epilogue read it
-                        ok = mbar_wait(bar(BAR_E), (it - 1) & 1, abort_flag, t0);
+                    // this unit's O buffer was last used two units ago: free once that
+                    // unit's epilogue has read it
+                    if (ok && j == 0 && it >= 2)
+                        ok = mbar_wait(bar(BAR_E + (it & 1)), ((it >> 1) - 1) & 1, abort_flag, t0);
                     if (!ok) break;
                     tc_fence_after();
-                    issue_pv(st, j > 0);
-                    tc_commit(bar(BAR_O));
+                    issue_pv(st, j > 0, it & 1);
+                    tc_commit(bar(BAR_O + (it & 1)));
                     tc_commit(bar(BAR_KE + st));
                 }
                 ++it;
+                u = nxt;
             }
             // every MMA and its barrier arrivals done before the CTA releases its memory
             if (ok && g > 0) mbar_wait(bar(BAR_KE + ((g - 1) & 1)), ((g - 1) >> 1) & 1, abort_flag, t0);
@@ -625,22 +681,71 @@ __global__ void __launch_bounds__(kPrefillThreads, TcCfg<D>::MIN_BLOCKS)
         const int r = tid;
         const int half = D / 2;
         const uint32_t lane_s = tmem_s + (static_cast<uint32_t>(warp * 32) << 16);
-        const uint32_t lane_o = tmem_o + (static_cast<uint32_t>(warp * 32) << 16);
+        auto lane_o = [&](int ob) { return tmem_o(ob) + (static_cast<uint32_t>(warp * 32) << 16); };
         unsigned char* prow_s = smem + Cfg::OFF_P + r * 128;
         unsigned char* qrow_s = smem + Cfg::OFF_Q + r * 128;
         bool ok = true;
         int g = 0, it = 0;
+        int pv[2] = {0, 0};  // P V products into each O buffer by earlier units
+        // The epilogue of a unit runs after the first tile of the next one, so the wait for
+        // its last P V and the next unit's first Q K^T overlap.  It needs the unit's output
+        // rows, its O buffer and each row's sum l.
+        Unit prev{};
+        float l_prev = 0.f;
+        bool has_prev = false;
+        auto epilogue = [&](const Unit& e, float le, int ob) {
+            const bool lv = r < e.rows;
+            const float inv = 1.f / le;
+            const int64_t orow = static_cast<int64_t>(e.row0 + e.q_lo + (lv ? r : 0)) *
+                                     a.out_stride + static_cast<int64_t>(e.h) * D;
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+                float o[32];
+                tmem_ld32(lane_o(ob) + c * 32, o);  // warp-wide: every lane loads, live rows store
+                if (c == D / 32 - 1) {
+                    tc_fence_before();
+                    mbar_arrive(bar(BAR_E + ob));  // the unit after next may overwrite O_ob
+                }
+                if (!lv) continue;
+                if (a.out_f32) {
+                    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + orow + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv,
+                                             o[4 * i + 2] * inv, o[4 * i + 3] * inv);
+                } else {
+                    uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + orow + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        uint32_t pk[4];
+#pragma unroll
+                        for (int e2 = 0; e2 < 4; ++e2) {
+                            __half2 hv = __floats2half2_rn(o[8 * i + 2 * e2] * inv,
+                                                           o[8 * i + 2 * e2 + 1] * inv);
+                            pk[e2] = *reinterpret_cast<uint32_t*>(&hv);
+                        }
+                        dst[i] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    }
+                }
+            }
+        };
         Unit u;
         for (int k = 0; ok && unit_of(a, k, num_units, row_tiles, u); ++k) {
             if (u.nt == 0) continue;
+            const int ob = it & 1;
             const bool live = r < u.rows;
             const int qpos = u.cached + u.q_lo + (live ? r : u.rows - 1);  // keys 0..qpos
-            // ---- Q: the raw tile arrives by TMA; rotate this row in place
+            // ---- Q: the raw tile arrives by TMA; with RoPE in this kernel each thread
+            // rotates its row in place (without, the MMA warp uses the tile as it lands and
+            // these warps never touch it)
             const int rpos = qpos + a.rope_off;
-            const bool rot = live && a.rope_cos != nullptr && rpos >= 0 && rpos < a.rope_len;
-            ok = mbar_wait(bar(BAR_QL), it & 1, abort_flag, t0);
-            ok = __all_sync(FULL, ok);
-            if (!ok) break;
+            const bool rope_here = a.rope_cos != nullptr;
+            const bool rot = live && rope_here && rpos >= 0 && rpos < a.rope_len;
+            if (rope_here) {
+                ok = mbar_wait(bar(BAR_QL), it & 1, abort_flag, t0);
+                ok = __all_sync(FULL, ok);
+                if (!ok) break;
+            }
             if (a.rope_tma) {  // the table rows of this unit, staged in the P buffer
                 ok = mbar_wait(bar(BAR_RL), it & 1, abort_flag, t0);
                 ok = __all_sync(FULL, ok);
@@ -701,8 +806,10 @@ __global__ void __launch_bounds__(kPrefillThreads, TcCfg<D>::MIN_BLOCKS)
                     }
                 }
             }
-            fence_async_smem();
-            mbar_arrive(bar(BAR_Q));
+            if (rope_here) {
+                fence_async_smem();
+                mbar_arrive(bar(BAR_Q));
+            }
 
             float m_used = -INFINITY, l = 0.f;
             for (int j = 0; j < u.nt; ++j, ++g) {
@@ -727,8 +834,12 @@ __global__ void __launch_bounds__(kPrefillThreads, TcCfg<D>::MIN_BLOCKS)
 #pragma unroll
                 for (int i = 0; i < 128; ++i) mx = fmaxf(mx, v[i]);
                 const float mt = mx * a.scale_log2;
-                if (j > 0) {  // P_{g-1} V_{g-1} done: P buffer free, O settled
-                    ok = mbar_wait(bar(BAR_O), (g - 1) & 1, abort_flag, t0);
+                // the previous P V done: the P buffer is free (and, within a unit, O settled);
+                // on a unit's first tile that is the previous unit's last P V, in its buffer
+                if (j > 0 || has_prev) {
+                    const int wb = j > 0 ? ob : (ob ^ 1);
+                    const int idx = j > 0 ? pv[ob] + j - 1 : pv[ob ^ 1] - 1;
+                    ok = mbar_wait(bar(BAR_O + wb), idx & 1, abort_flag, t0);
                     ok = __all_sync(FULL, ok);
                     if (!ok) break;
                     tc_fence_after();
@@ -776,56 +887,35 @@ __global__ void __launch_bounds__(kPrefillThreads, TcCfg<D>::MIN_BLOCKS)
 #pragma unroll
                     for (int c = 0; c < D / 32; ++c) {
                         float o[32];
-                        tmem_ld32(lane_o + c * 32, o);
+                        tmem_ld32(lane_o(ob) + c * 32, o);
 #pragma unroll
                         for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                        tmem_st32(lane_o + c * 32, o);
+                        tmem_st32(lane_o(ob) + c * 32, o);
                     }
                 }
                 fence_async_smem();
                 tc_fence_before();
                 mbar_arrive(bar(BAR_P));
-            }
-            if (!ok) break;
-            // ---- epilogue: O of the unit's last tile, normalised, out to global
-            ok = mbar_wait(bar(BAR_O), (g - 1) & 1, abort_flag, t0);
-            ok = __all_sync(FULL, ok);
-            if (!ok) break;
-            tc_fence_after();
-            const float inv = 1.f / l;
-            const int64_t orow = static_cast<int64_t>(u.row0 + u.q_lo + (live ? r : 0)) *
-                                     a.out_stride + static_cast<int64_t>(u.h) * D;
-#pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
-                float o[32];
-                tmem_ld32(lane_o + c * 32, o);  // warp-wide: every lane loads, live rows store
-                if (c == D / 32 - 1) {
-                    tc_fence_before();
-                    mbar_arrive(bar(BAR_E));  // the next unit's first P V may overwrite O
-                }
-                if (!live) continue;
-                if (a.out_f32) {
-                    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + orow + c * 32);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv,
-                                             o[4 * i + 2] * inv, o[4 * i + 3] * inv);
-                } else {
-                    uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + orow + c * 32);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        uint32_t pk[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            __half2 hv = __floats2half2_rn(o[8 * i + 2 * e] * inv,
-                                                           o[8 * i + 2 * e + 1] * inv);
-                            pk[e] = *reinterpret_cast<uint32_t*>(&hv);
-                        }
-                        dst[i] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                    }
+                if (j == 0 && has_prev) {  // the previous unit's O is final: write it out
+                    epilogue(prev, l_prev, ob ^ 1);
+                    has_prev = false;
                 }
             }
+            if (!ok) break;
+            pv[ob] += u.nt;
+            prev = u;
+            l_prev = l;
+            has_prev = true;
             ++it;
+        }
+        if (ok && has_prev) {  // the last unit: wait for its last P V, then write it out
+            const int ob = (it - 1) & 1;
+            ok = mbar_wait(bar(BAR_O + ob), (pv[ob] - 1) & 1, abort_flag, t0);
+            ok = __all_sync(FULL, ok);
+            if (ok) {
+                tc_fence_after();
+                epilogue(prev, l_prev, ob);
+            }
         }
     }
     tc_fence_before();
@@ -1089,26 +1179,48 @@ int prefill_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, con
         return fail(TMLLM_INVALID_ARGUMENT,
                     "the tensor-core prefill needs F16, head_dim 64/128, power-of-two pages of "
                     ">= 16 positions and 16-byte aligned q/out/arenas");
-    // 1. append (rotated keys, values) at each sequence's cached length
-    if (k_new) {
+    // 1. append (rotated keys, values) at each sequence's cached length.  On the tensor-core
+    // path with RoPE and an F16 output, the query rows are rotated here as well, into the
+    // output buffer: each unit of the attention kernel reads its own q rows from there (by
+    // TMA, already rotated) before it overwrites them with its result.
+    const bool pre_rotate = tc_shape && o.rope_cos != nullptr && !a.out_f32;
+    {
         const int epc = static_cast<int>(16 / es);
-        const bool vec = (D / 2) % epc == 0 && aligned16(k_new) && aligned16(v_new) &&
-                         aligned16(kv->k_cache) && aligned16(kv->v_cache) &&
-                         (a.kv_stride * static_cast<int64_t>(es)) % 16 == 0;
-        const int64_t work = static_cast<int64_t>(total_rows) * Hkv * (D / 2) / (vec ? epc : 1);
-        int64_t blocks = (work + 255) / 256;
-        const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
-        if (blocks > cap) blocks = cap;
-        const unsigned nb = static_cast<unsigned>(blocks);
-        if (vec && kv->dtype == TMLLM_F16)
-            prefill_append_vec_kernel<__half><<<nb, 256, 0, stream>>>(a);
-        else if (vec)
-            prefill_append_vec_kernel<float><<<nb, 256, 0, stream>>>(a);
-        else if (kv->dtype == TMLLM_F16)
-            prefill_append_kernel<__half><<<nb, 256, 0, stream>>>(a);
-        else
-            prefill_append_kernel<float><<<nb, 256, 0, stream>>>(a);
-        TMLLM_LAUNCH_TRY();
+        const bool vec = (D / 2) % epc == 0 && aligned16(kv->k_cache) && aligned16(kv->v_cache) &&
+                         (!k_new || (aligned16(k_new) && aligned16(v_new) &&
+                                     (a.kv_stride * static_cast<int64_t>(es)) % 16 == 0));
+        auto grid_for = [&](int64_t work) {
+            int64_t blocks = (work + 255) / 256;
+            const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
+            if (blocks > cap) blocks = cap;
+            return static_cast<unsigned>(blocks < 1 ? 1 : blocks);
+        };
+        PrefillArgs ap = a;
+        if (k_new && !vec) {  // scalar append of K and V, then (if asked) the q rotation
+            const unsigned nb = grid_for(static_cast<int64_t>(total_rows) * Hkv * (D / 2));
+            if (kv->dtype == TMLLM_F16)
+                prefill_append_kernel<__half><<<nb, 256, 0, stream>>>(a);
+            else
+                prefill_append_kernel<float><<<nb, 256, 0, stream>>>(a);
+            TMLLM_LAUNCH_TRY();
+            ap.k_new = ap.v_new = nullptr;
+        }
+        ap.q_rot = pre_rotate ? out : nullptr;
+        if (ap.k_new || ap.q_rot) {
+            const int64_t heads = (ap.k_new ? Hkv : 0) + (ap.q_rot ? q_heads : 0);
+            const unsigned nb = grid_for(static_cast<int64_t>(total_rows) * heads * (D / 2) / epc);
+            if (kv->dtype == TMLLM_F16)
+                prefill_append_vec_kernel<__half><<<nb, 256, 0, stream>>>(ap);
+            else
+                prefill_append_vec_kernel<float><<<nb, 256, 0, stream>>>(ap);
+            TMLLM_LAUNCH_TRY();
+        }
+    }
+    if (pre_rotate) {  // the attention kernel reads the rotated rows, without RoPE
+        a.q = out;
+        a.q_stride = static_cast<int64_t>(q_heads) * D;
+        a.rope_cos = a.rope_sin = nullptr;
+        a.rope_vec = a.rope_tma = 0;
     }
     // 2. attention over the cache, new rows included
     if (tc_shape) {
