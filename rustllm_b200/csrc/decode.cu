@@ -143,7 +143,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_split_kernel(const D
     T* knew_s = reinterpret_cast<T*>(smem + Cfg::OFF_NEW);            // [D]
     T* vnew_s = knew_s + D;                                           // [D]
 
-    const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const int split = blockIdx.z, kvh = blockIdx.x, b = blockIdx.y;  // splits slowest
+    const int nsplit = gridDim.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = a.group;
     const int cached = a.seq_lens[b] < 0 ? 0 : a.seq_lens[b];
@@ -151,7 +152,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_split_kernel(const D
     const int L = cached + (has_new ? 1 : 0);
     int splits_b = (L + a.chunk - 1) / a.chunk;
     if (splits_b < 1) splits_b = 1;
-    if (splits_b > static_cast<int>(gridDim.x)) splits_b = gridDim.x;
+    if (splits_b > nsplit) splits_b = nsplit;
     if (split >= splits_b) return;
     const int t0 = split * a.chunk;
     const int t1 = (split == splits_b - 1) ? L : min(L, t0 + a.chunk);
@@ -419,7 +420,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_split_kernel(const D
 
     // ---- several splits: publish (O, m, l), last CTA of this (seq, kv head) merges
     const int64_t pbase =
-        ((static_cast<int64_t>(b) * a.kv_heads + kvh) * gridDim.x) * G;  // part row of split 0
+        ((static_cast<int64_t>(b) * a.kv_heads + kvh) * nsplit) * G;  // part row of split 0
     for (int idx = tid; idx < G * D; idx += kDecodeThreads) {
         const int g = idx / D, d = idx - g * D;
         float o = red[g * D + d] + red[(GP + g) * D + d] + red[(2 * GP + g) * D + d] +
@@ -442,8 +443,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_split_kernel(const D
 
     // merge weights w[s][g] = 2^(m_s - M_g), kept in the free ring
     float* wts = reinterpret_cast<float*>(smem);  // [splits_b][GP]
-    float* lsp = wts + static_cast<int64_t>(gridDim.x) * GP;  // [splits_b][GP]
-    float* Ms = lsp + static_cast<int64_t>(gridDim.x) * GP;
+    float* lsp = wts + static_cast<int64_t>(nsplit) * GP;  // [splits_b][GP]
+    float* Ms = lsp + static_cast<int64_t>(nsplit) * GP;
     float* den = Ms + GP;
     for (int i = tid; i < splits_b * G; i += kDecodeThreads) {
         const int s = i / G, g = i - s * G;
@@ -663,7 +664,8 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? 4 : 2) decode_mma_ke
     float* fin = reinterpret_cast<float*>(smem + Cfg::OFF_FIN);  // [16][D] exchange staging
     float* flse = fin + 16 * D;                                  // [16]
 
-    const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const int split = blockIdx.z, kvh = blockIdx.x, b = blockIdx.y;  // splits slowest
+    const int nsplit = gridDim.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = a.group;
     const int cached = a.seq_lens[b] < 0 ? 0 : a.seq_lens[b];
@@ -671,7 +673,7 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? 4 : 2) decode_mma_ke
     const int L = cached + (has_new ? 1 : 0);
     int splits_b = (L + a.chunk - 1) / a.chunk;
     if (splits_b < 1) splits_b = 1;
-    if (splits_b > static_cast<int>(gridDim.x)) splits_b = gridDim.x;
+    if (splits_b > nsplit) splits_b = nsplit;
     if (split >= splits_b) return;
     const int t0 = split * a.chunk;
     const int t1 = (split == splits_b - 1) ? L : min(L, t0 + a.chunk);
@@ -936,7 +938,7 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? 4 : 2) decode_mma_ke
     __syncthreads();
     // per row g: M = max_w m_w, weights 2^(m_w - M)
     const int64_t qh0 = static_cast<int64_t>(b) * a.q_heads + static_cast<int64_t>(kvh) * G;
-    const int64_t pbase = ((static_cast<int64_t>(b) * a.kv_heads + kvh) * gridDim.x) * G;
+    const int64_t pbase = ((static_cast<int64_t>(b) * a.kv_heads + kvh) * nsplit) * G;
     for (int idx = tid; idx < G * D; idx += kDecodeThreads) {
         const int g = idx / D, d = idx - g * D;
         float M = -INFINITY;
@@ -987,8 +989,8 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? 4 : 2) decode_mma_ke
     if (!*flag_s) return;
     __threadfence();
     float* wts = reinterpret_cast<float*>(smem);  // [splits_b][16] (red is consumed)
-    float* lsp = wts + static_cast<int64_t>(gridDim.x) * 16;  // [splits_b][16]
-    float* Ms = lsp + static_cast<int64_t>(gridDim.x) * 16;
+    float* lsp = wts + static_cast<int64_t>(nsplit) * 16;  // [splits_b][16]
+    float* Ms = lsp + static_cast<int64_t>(nsplit) * 16;
     float* dens = Ms + 16;
     // all (m, l) pairs of this (sequence, KV head) in one parallel round trip
     for (int i = tid; i < splits_b * G; i += kDecodeThreads) {
@@ -1017,7 +1019,7 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? 4 : 2) decode_mma_ke
     const int64_t stride4 = static_cast<int64_t>(G) * D / 4;
     const float4* src0 = reinterpret_cast<const float4*>(a.part_o + pbase * D);
     const size_t stage_bytes = static_cast<size_t>(splits_b) * stride4 * 16;
-    const size_t stage_off = static_cast<size_t>(2 * gridDim.x * 16 + 32) * 4;
+    const size_t stage_off = static_cast<size_t>(2 * nsplit * 16 + 32) * 4;
     const bool staged = stage_off + stage_bytes <= static_cast<size_t>(Cfg::OFF_FIN);
     float4* stage = reinterpret_cast<float4*>(smem + ((stage_off + 15) & ~static_cast<size_t>(15)));
     if (staged) {
@@ -1234,9 +1236,9 @@ int launch_tiled(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
     using Cfg = DecodeCfg<T, D, GP, TT, STAGES>;
     auto* fn = decode_split_kernel<T, D, GP, TT, STAGES>;
     const size_t bytes = static_cast<size_t>(Cfg::BYTES);
-    const size_t need_merge = (2 * static_cast<size_t>(grid.x) + 2) * GP * 4;
+    const size_t need_merge = (2 * static_cast<size_t>(grid.z) + 2) * GP * 4;
     if (need_merge > static_cast<size_t>(STAGES * 2 * Cfg::TILE))
-        return fail(TMLLM_INVALID_ARGUMENT, "too many splits (%u) for the merge scratch", grid.x);
+        return fail(TMLLM_INVALID_ARGUMENT, "too many splits (%u) for the merge scratch", grid.z);
     TMLLM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(bytes)));
     fn<<<grid, kDecodeThreads, bytes, s>>>(a);
@@ -1249,8 +1251,8 @@ int launch_mma(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
     using Cfg = MmaCfg<D, STAGES>;
     auto* fn = decode_mma_kernel<D, STAGES>;
     const size_t bytes = static_cast<size_t>(Cfg::BYTES);
-    if ((2 * static_cast<size_t>(grid.x) + 2) * 16 * 4 > static_cast<size_t>(Cfg::OFF_FIN))
-        return fail(TMLLM_INVALID_ARGUMENT, "too many splits (%u) for the merge scratch", grid.x);
+    if ((2 * static_cast<size_t>(grid.z) + 2) * 16 * 4 > static_cast<size_t>(Cfg::OFF_FIN))
+        return fail(TMLLM_INVALID_ARGUMENT, "too many splits (%u) for the merge scratch", grid.z);
     TMLLM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(bytes)));
     fn<<<grid, kDecodeThreads, bytes, s>>>(a);
@@ -1449,8 +1451,10 @@ int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
             a.part_ml = reinterpret_cast<float*>(base + w.part_ml);
             a.part_o = reinterpret_cast<float*>(base + w.part_o);
         }
-        dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(Hkv),
-                  static_cast<unsigned>(B));
+        // splits are the slowest grid dimension: every sequence's first chunk is scheduled
+        // before any second chunk, so the short remainders of long sequences run last
+        dim3 grid(static_cast<unsigned>(Hkv), static_cast<unsigned>(B),
+                  static_cast<unsigned>(splits));
         bool done = false;
         int st = launch_decode(kv->dtype, D, o.variant, a, grid, stream, &done);
         if (done) return st;
