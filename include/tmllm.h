@@ -163,6 +163,35 @@ int tmllm_add_rmsnorm(tmllm_dtype dtype, const void* x, const void* residual, co
 int tmllm_swiglu(tmllm_dtype dtype, const void* gate_up, void* out, size_t rows, size_t inter,
                  tmllm_stream stream);
 
+/* Replaces, for the few rows of a decode step, Linear::forward_encode (src/nn/linear.rs:105-170,
+ * out = x · W with W [in, out] row-major, F16 in and out, F32 accumulation) together with
+ * the element-wise kernels around it in TransformerBlock::forward_with_cache_encode
+ * (src/nn/transformer_block.rs:128-158), in one launch:
+ *   norm_weight != NULL: x is first RMS-normalised per row as kernels/rmsnorm.metal:71-126
+ *     does (half(x * rsqrt(mean(x^2) + eps) * norm_weight)), the mean over all k columns;
+ *     stats_in (may be NULL) holds the row statistics of x that the call which produced x
+ *     wrote to its stats_out, else the rows are read once more to compute them;
+ *   swiglu = 1: w is [k, 2n] holding the gate columns then the up columns, and
+ *     out = half(silu(half(x·Wg)) * half(x·Wu)) (kernels/silu.metal:38-46);
+ *   residual != NULL (swiglu = 0 only): out = half(residual + half(x · W))
+ *     (kernels/vector_add.metal:15-21); residual may alias out;
+ *   stats_out != NULL: receives the row statistics of out (tmllm_linear_stats_bytes(n)
+ *     bytes of device memory), for a later call that RMS-normalises out (its k = this n,
+ *     the same rows).
+ * rows <= 64; k and n multiples of 8; ldx / ldw / ldo / ldr are row strides in elements,
+ * multiples of 8, and x, w, out, residual and norm_weight are 16-byte aligned.
+ * flags: TMLLM_LINEAR_OVERLAP lets the launch overlap the tail of the work queued before it
+ * on `stream` (programmatic dependent launch): w is read before that work has finished, so
+ * the caller promises that it does not write w; x, residual, stats_in and norm_weight are
+ * read only after it has finished.  The result does not depend on `rows` beyond the row
+ * itself: a row computed alone equals the same row in any batch. */
+#define TMLLM_LINEAR_OVERLAP 1u
+size_t tmllm_linear_stats_bytes(int32_t n);
+int tmllm_linear(const void* x, int64_t ldx, const void* norm_weight, const float* stats_in,
+                 float eps, const void* w, int64_t ldw, void* out, int64_t ldo,
+                 const void* residual, int64_t ldr, float* stats_out, int32_t rows, int32_t k,
+                 int32_t n, int32_t swiglu, uint32_t flags, tmllm_stream stream);
+
 /* Replaces greedy sampling (src/generation/sampler.rs:79-88, on the CPU in the reference):
  * ids[r] = index of the largest of logits [rows, vocab] row r; the last of equal maxima. */
 int tmllm_argmax(tmllm_dtype dtype, const void* logits, int32_t* ids, size_t rows, size_t vocab,

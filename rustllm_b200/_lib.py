@@ -142,6 +142,9 @@ _PROTOS = {
     "tmllm_add_rmsnorm": (C.c_int, [C.c_int, vp, vp, vp, vp, vp, sz, sz, C.c_float, vp]),
     "tmllm_swiglu": (C.c_int, [C.c_int, vp, vp, sz, sz, vp]),
     "tmllm_argmax": (C.c_int, [C.c_int, vp, vp, sz, sz, vp]),
+    "tmllm_linear_stats_bytes": (sz, [i32]),
+    "tmllm_linear": (C.c_int, [vp, i64, vp, vp, C.c_float, vp, i64, vp, i64, vp, i64, vp, i32,
+                               i32, i32, i32, C.c_uint32, vp]),
     "tmllm_decode_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
     "tmllm_decode_workspace_init": (C.c_int, [vp, sz, vp]),
     "tmllm_decode_auto_splits": (i32, [i32, i32, i64]),

@@ -2,11 +2,17 @@
 // token embedding gather, residual add fused with RMSNorm, SwiGLU, and greedy argmax.
 // Each follows the reference kernel it replaces (kernels/embedding.metal,
 // kernels/vector_add.metal + kernels/rmsnorm.metal, kernels/silu.metal, and the CPU sampler
-// src/generation/sampler.rs) in its storage roundings; the plain GEMMs between them are
-// library calls.
+// src/generation/sampler.rs) in its storage roundings.  The projections of a decode step
+// (at most 64 rows) run in tmllm_linear, with the norm, SwiGLU and residual add fused into
+// it; the projections of a prompt (many rows) are library GEMMs.
+#include <atomic>
 #include <cmath>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace tmllm {
 namespace {
@@ -204,6 +210,405 @@ __global__ void __launch_bounds__(256) argmax_kernel(const T* __restrict__ logit
     if (threadIdx.x == 0) ids[blockIdx.x] = static_cast<int32_t>(bi[0] < 0 ? 0 : bi[0]);
 }
 
+// ---- Linear layers of a decode step (src/nn/linear.rs: y = x · W with W [in, out]) --------
+// With the few rows of a decode step (M <= 64) a projection streams its weight matrix once
+// and does little arithmetic, so it is written as a weight-streaming kernel with the
+// decoder's neighbouring element-wise work folded in:
+//  * RMSNorm of the input rows (kernels/rmsnorm.metal:71-126) as the A operand is staged:
+//    1/rms per row comes from row statistics the producing projection wrote (stats_in) or
+//    from a pass over the rows, and each staged tile is rewritten in shared memory as
+//    half(x * inv * w), the reference's rounding of the normed rows;
+//  * SwiGLU (kernels/silu.metal:38-46) on a fused [gate | up] weight: the CTA owns the same
+//    columns of both halves and writes half(silu(half(g)) * half(u));
+//  * a residual add (kernels/vector_add.metal:15-21): out = half(resid + half(x · W)),
+//    optionally with the per-row sums of squares of the stored output (stats_out) that the
+//    next norm-fused projection reads instead of re-reading the rows.
+// CTA tile: every row (<= 64) × 64 output columns over one K chunk.  The K chunks of a
+// column tile are the CTAs of one thread-block cluster (grid y = cluster y <= 8): each
+// leaves its F32 partial tile in its shared memory, and after a cluster barrier CTA r sums
+// rows r, r + splits, ... over the cluster's shared memory in split order, so the split-K
+// reduction never touches global memory.  Weight and x tiles move through a cp.async
+// ring; products run on the warp-level tensor cores (mma.sync m16n8k16, F16 in, F32
+// accumulate; weight tiles through ldmatrix.trans): with 1-64 rows the layer is bound by
+// the weight bytes and by latency, not by the MMA rate.
+// Launched with programmatic stream serialisation (opt-in, TMLLM_LINEAR_OVERLAP), a CTA
+// starts its weight prefetch while the previous kernel on the stream drains and waits for
+// that kernel's results (griddepcontrol.wait) only before it reads x, residual or stats.
+constexpr int kLinRows = 64;
+constexpr int kLinCols = 64;
+constexpr int kLinK = 64;
+constexpr int kLinThreads = 128;
+constexpr int kLinMaxSplits = 8;                 // portable cluster size
+constexpr int kLinSlab = kLinK * kLinCols * 2;  // one 64 x 64 F16 tile (weight or x)
+
+template <int NW> struct LinCfg {
+    static constexpr int STAGES = NW == 1 ? 4 : 3;  // 66 / 74 KB: three CTAs per SM
+    static constexpr int STAGE = (NW + 1) * kLinSlab + 128;
+    static constexpr int PSTRIDE = kLinCols * NW + 4;  // floats per partial row
+    static constexpr size_t SMEM = static_cast<size_t>(STAGES) * STAGE + kLinRows * 4;
+    static_assert(static_cast<size_t>(STAGES) * STAGE >= kLinRows * PSTRIDE * 4,
+                  "the partial tile reuses the ring");
+};
+
+struct LinearArgs {
+    const __half* x;         // [M, K], row stride ldx
+    const __half* norm_w;    // [K] RMSNorm weight, or null
+    const float* stats_in;   // [ceil(K/64)][64] row sums of squares of x, or null
+    const __half* w;         // [K, N] (or [K, 2N] with swiglu), row stride ldw
+    __half* out;             // [M, N], row stride ldo
+    const __half* resid;     // [M, N] added in the epilogue, or null (may alias out)
+    float* stats_out;        // [ceil(N/64)][64] row sums of squares of out, or null
+    int64_t ldx, ldw, ldo, ldr;
+    int M, K, N, kchunk;
+    float eps;
+};
+
+__device__ __forceinline__ void grid_dependency_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <int NW>
+__global__ void __launch_bounds__(kLinThreads) linear_kernel(const LinearArgs a) {
+    using Cfg = LinCfg<NW>;
+    constexpr int S = Cfg::STAGES, STAGE = Cfg::STAGE;
+    extern __shared__ __align__(128) unsigned char smem[];
+    float* inv_s = reinterpret_cast<float*>(smem + S * STAGE);  // [64]
+    cg::cluster_group cluster = cg::this_cluster();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tile = blockIdx.x, split = blockIdx.y, splits = gridDim.y;
+    const int n0 = tile * kLinCols;
+    const int k0 = split * a.kchunk;
+    const int k1 = min(a.K, k0 + a.kchunk);
+    const int nkt = k1 > k0 ? (k1 - k0 + kLinK - 1) / kLinK : 0;
+    const int MT = (a.M + 15) / 16;
+    const bool norm = a.norm_w != nullptr;
+    launch_dependents();  // the next projection may start prefetching its weights
+
+    // stage layout: NW weight slabs, the x tile, 64 norm weights; 16-byte chunks swizzled
+    // by row (chunk c of row r at r*128 + ((c ^ (r & 7)) << 4)); out-of-range chunks are
+    // zero-filled, so K tails add nothing and padding rows / columns are never stored
+    auto load_w = [&](int t, int slot) {
+        unsigned char* st = smem + slot * STAGE;
+        const int kb = k0 + t * kLinK, c = tid & 7;
+#pragma unroll
+        for (int sl = 0; sl < NW; ++sl) {
+            const int colb = sl * a.N + n0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int r = (tid >> 3) + 16 * i;
+                const int k = kb + r, col = n0 + c * 8;
+                const bool ok = k < k1 && col < a.N;
+                const __half* src = ok ? a.w + static_cast<int64_t>(k) * a.ldw + colb + c * 8 : a.w;
+                cp_async16(st + sl * kLinSlab + r * 128 + ((c ^ (r & 7)) << 4), src, ok ? 16 : 0);
+            }
+        }
+    };
+    auto load_x = [&](int t, int slot) {
+        unsigned char* st = smem + slot * STAGE;
+        const int kb = k0 + t * kLinK, c = tid & 7;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int r = (tid >> 3) + 16 * i;
+            if (r >= MT * 16) break;
+            const int k = kb + c * 8;
+            const bool ok = r < a.M && k < k1;
+            const __half* src = ok ? a.x + static_cast<int64_t>(r) * a.ldx + k : a.x;
+            cp_async16(st + NW * kLinSlab + r * 128 + ((c ^ (r & 7)) << 4), src, ok ? 16 : 0);
+        }
+        if (norm && tid < 8) {
+            const int k = kb + tid * 8;
+            const bool ok = k < k1;
+            cp_async16(st + (NW + 1) * kLinSlab + tid * 16, ok ? a.norm_w + k : a.norm_w,
+                       ok ? 16 : 0);
+        }
+    };
+    // weights first (constant through a decode step), then wait for the previous kernel
+    const int pro = min(S - 1, nkt);
+    for (int t = 0; t < pro; ++t) load_w(t, t);
+    grid_dependency_wait();
+    for (int t = 0; t < pro; ++t) load_x(t, t);
+    cp_async_commit();
+    // 1/rms of every row over the whole K while the prologue lands
+    if (norm) {
+        if (a.stats_in) {
+            if (tid < a.M) {
+                const int kt = (a.K + kLinCols - 1) / kLinCols;
+                float ss = 0.f;
+#pragma unroll 4
+                for (int t = 0; t < kt; ++t) ss += __ldg(a.stats_in + t * kLinRows + tid);
+                inv_s[tid] = rsqrtf(ss / static_cast<float>(a.K) + a.eps);
+            }
+        } else {
+            // four rows per warp at a time, four 16-byte loads per row in flight
+            const int nch = a.K / 8;
+            for (int m0 = warp * 4; m0 < a.M; m0 += 16) {
+                float ss[4] = {0.f, 0.f, 0.f, 0.f};
+                for (int c = lane; c < nch; c += 128) {
+                    uint4 v[4][4];
+#pragma unroll
+                    for (int r = 0; r < 4; ++r)
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int cc = c + 32 * u, m = m0 + r;
+                            v[r][u] = (m < a.M && cc < nch)
+                                          ? __ldg(reinterpret_cast<const uint4*>(
+                                                      a.x + static_cast<int64_t>(m) * a.ldx) + cc)
+                                          : make_uint4(0, 0, 0, 0);
+                        }
+#pragma unroll
+                    for (int r = 0; r < 4; ++r)
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            float f[8];
+                            Chunk<__half>::unpack(v[r][u], f);
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) ss[r] = fmaf(f[e], f[e], ss[r]);
+                        }
+                }
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const float t = warp_sum(ss[r]);
+                    if (lane == 0 && m0 + r < a.M)
+                        inv_s[m0 + r] = rsqrtf(t / static_cast<float>(a.K) + a.eps);
+                }
+            }
+        }
+    }
+    cp_async_wait<0>();
+
+    float acc[4][2 * NW][4];
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+        for (int j = 0; j < 2 * NW; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[mt][j][e] = 0.f;
+
+    const int mi = lane >> 3;
+    for (int t = 0; t < nkt; ++t) {
+        // stage t landed (the prologue completely, later stages S-2 groups back); every
+        // thread is done with stage t-1, whose slot receives stage t + S - 1
+        cp_async_wait<S - 2>();
+        __syncthreads();
+        {
+            const int tn = t + S - 1;
+            if (tn < nkt) {
+                load_w(tn, tn % S);
+                load_x(tn, tn % S);
+            }
+            cp_async_commit();
+        }
+        unsigned char* st = smem + (t % S) * STAGE;
+        unsigned char* xs = st + NW * kLinSlab;
+        if (norm) {  // rewrite this thread's x chunks as half(x * inv * w)
+            const int c = tid & 7;
+            float g[8];
+            Chunk<__half>::unpack(*reinterpret_cast<const uint4*>(st + (NW + 1) * kLinSlab + c * 16),
+                                  g);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int r = (tid >> 3) + 16 * i;
+                if (r >= a.M) break;
+                uint4* p = reinterpret_cast<uint4*>(xs + r * 128 + ((c ^ (r & 7)) << 4));
+                float v[8];
+                Chunk<__half>::unpack(*p, v);
+                const float inv = inv_s[r];
+                uint4 u;
+                __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    h[e] = __floats2half2_rn(v[2 * e] * inv * g[2 * e],
+                                             v[2 * e + 1] * inv * g[2 * e + 1]);
+                *p = u;
+            }
+            __syncthreads();
+        }
+#pragma unroll
+        for (int kk = 0; kk < kLinK / 16; ++kk) {
+            uint32_t b[NW][4];
+#pragma unroll
+            for (int sl = 0; sl < NW; ++sl) {
+                const int r = kk * 16 + (mi & 1) * 8 + (lane & 7);
+                const int c = warp * 2 + (mi >> 1);
+                ldsm_x4_t(static_cast<uint32_t>(__cvta_generic_to_shared(
+                              st + sl * kLinSlab + r * 128 + ((c ^ (r & 7)) << 4))),
+                          b[sl][0], b[sl][1], b[sl][2], b[sl][3]);
+            }
+#pragma unroll
+            for (int mt = 0; mt < 4; ++mt) {
+                if (mt >= MT) break;
+                const int r = mt * 16 + (mi & 1) * 8 + (lane & 7);
+                const int c = kk * 2 + (mi >> 1);
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4(static_cast<uint32_t>(__cvta_generic_to_shared(
+                            xs + r * 128 + ((c ^ (r & 7)) << 4))),
+                        a0, a1, a2, a3);
+#pragma unroll
+                for (int sl = 0; sl < NW; ++sl) {
+                    mma16816(acc[mt][2 * sl], a0, a1, a2, a3, b[sl][0], b[sl][1]);
+                    mma16816(acc[mt][2 * sl + 1], a0, a1, a2, a3, b[sl][2], b[sl][3]);
+                }
+            }
+        }
+    }
+    cp_async_wait<0>();
+    __syncthreads();  // the ring is free: it holds this CTA's partial tile from here on
+
+    // partial tile ps[m][cl] (cl < 64: gate / plain columns, cl >= 64: up columns); fragment
+    // (mt, j, e) is row mt*16 + g4 (+8 for e >= 2), column (j/2)*64 + warp*16 + (j%2)*8 +
+    // t4*2 + (e & 1)
+    float* ps = reinterpret_cast<float*>(smem);
+    const int g4 = lane >> 2, t4 = lane & 3;
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+        if (mt >= MT) break;
+#pragma unroll
+        for (int j = 0; j < 2 * NW; ++j)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int m = mt * 16 + g4 + 8 * h;
+                const int cl = (j >> 1) * kLinCols + warp * 16 + (j & 1) * 8 + t4 * 2;
+                *reinterpret_cast<float2*>(ps + m * Cfg::PSTRIDE + cl) =
+                    make_float2(acc[mt][j][2 * h], acc[mt][j][2 * h + 1]);
+            }
+    }
+    cluster.sync();  // every split's partial tile is complete and visible cluster-wide
+
+    // CTA `split` finishes rows split, split + splits, ...: 16-byte stores of 8 outputs
+    // per thread and chunk, the residual added on the way; the 8 chunks of a row sit in 8
+    // neighbouring lanes, which sum the row's squares
+    const int my_rows = a.M > split ? (a.M - split + splits - 1) / splits : 0;
+    const int items = ((my_rows * 8 + kLinThreads - 1) / kLinThreads) * kLinThreads;
+    for (int q = tid; q < items; q += kLinThreads) {
+        const int m = split + splits * (q >> 3), c = q & 7;
+        const int col = n0 + c * 8;
+        const bool ok = (q >> 3) < my_rows && col < a.N;
+        float sq = 0.f;
+        if (ok) {
+            // every split's partial loaded together, then summed in split order
+            float4 pg[kLinMaxSplits][2], pu[kLinMaxSplits][2];
+#pragma unroll
+            for (int r = 0; r < kLinMaxSplits; ++r) {
+                if (r < splits) {
+                    const float4* pr = reinterpret_cast<const float4*>(
+                        cluster.map_shared_rank(ps, r) + m * Cfg::PSTRIDE + c * 8);
+                    pg[r][0] = pr[0];
+                    pg[r][1] = pr[1];
+                    if (NW == 2) {
+                        pu[r][0] = pr[kLinCols / 4];
+                        pu[r][1] = pr[kLinCols / 4 + 1];
+                    }
+                }
+            }
+            float g[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            float u[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int r = 0; r < kLinMaxSplits; ++r) {
+                if (r < splits) {
+                    g[0] += pg[r][0].x; g[1] += pg[r][0].y; g[2] += pg[r][0].z; g[3] += pg[r][0].w;
+                    g[4] += pg[r][1].x; g[5] += pg[r][1].y; g[6] += pg[r][1].z; g[7] += pg[r][1].w;
+                    if (NW == 2) {
+                        u[0] += pu[r][0].x; u[1] += pu[r][0].y; u[2] += pu[r][0].z; u[3] += pu[r][0].w;
+                        u[4] += pu[r][1].x; u[5] += pu[r][1].y; u[6] += pu[r][1].z; u[7] += pu[r][1].w;
+                    }
+                }
+            }
+            float y[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float gh = __half2float(__float2half_rn(g[e]));
+                if (NW == 1) {
+                    y[e] = gh;
+                } else {
+                    const float uh = __half2float(__float2half_rn(u[e]));
+                    y[e] = (gh / (1.0f + expf(-gh))) * uh;
+                }
+            }
+            if (a.resid) {
+                float r[8];
+                Chunk<__half>::unpack(
+                    *reinterpret_cast<const uint4*>(a.resid + static_cast<int64_t>(m) * a.ldr + col), r);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) y[e] = __fadd_rn(y[e], r[e]);
+            }
+            uint4 o;
+            __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                oh[e] = __floats2half2_rn(y[2 * e], y[2 * e + 1]);
+                const float2 f = __half22float2(oh[e]);
+                sq = fmaf(f.x, f.x, sq);
+                sq = fmaf(f.y, f.y, sq);
+            }
+            *reinterpret_cast<uint4*>(a.out + static_cast<int64_t>(m) * a.ldo + col) = o;
+        }
+        if (a.stats_out) {
+            sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+            sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+            sq += __shfl_xor_sync(0xffffffffu, sq, 4);
+            if (c == 0 && (q >> 3) < my_rows) a.stats_out[tile * kLinRows + m] = sq;
+        }
+    }
+    cluster.sync();  // peers are done reading this CTA's partial tile
+}
+
+struct LinearPlan {
+    int tiles, splits, kchunk;
+};
+// K splits so that the grid fills the SMs once (three CTAs an SM, less an eighth for the
+// packing of clusters), in chunks of whole 64-deep tiles, at most one cluster (8) per
+// column tile.  The plan depends on the shape only, so a row's result is the same in
+// every batch.
+LinearPlan plan_linear(int64_t k, int64_t n) {
+    LinearPlan p{};
+    p.tiles = static_cast<int>((n + kLinCols - 1) / kLinCols);
+    const int64_t target = static_cast<int64_t>(device_sm_count()) * 3 * 7 / 8;
+    int64_t sp = target / p.tiles;
+    const int64_t kt = (k + kLinK - 1) / kLinK;
+    if (sp > kt) sp = kt;
+    if (sp > kLinMaxSplits) sp = kLinMaxSplits;
+    if (sp < 1) sp = 1;
+    int64_t chunk = (k + sp - 1) / sp;
+    chunk = ((chunk + kLinK - 1) / kLinK) * kLinK;
+    p.kchunk = static_cast<int>(chunk);
+    p.splits = static_cast<int>((k + chunk - 1) / chunk);
+    return p;
+}
+
+template <int NW>
+int launch_linear(const LinearArgs& a, const LinearPlan& p, bool overlap, cudaStream_t s) {
+    // the shared-memory opt-in once per device (bit d of the mask)
+    static std::atomic<uint64_t> opted{0};
+    int dev = 0;
+    TMLLM_CUDA_TRY(cudaGetDevice(&dev));
+    const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
+    if (!bit || !(opted.load(std::memory_order_relaxed) & bit)) {
+        TMLLM_CUDA_TRY(cudaFuncSetAttribute(linear_kernel<NW>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(LinCfg<NW>::SMEM)));
+        opted.fetch_or(bit, std::memory_order_relaxed);
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(p.tiles), static_cast<unsigned>(p.splits));
+    cfg.blockDim = dim3(kLinThreads);
+    cfg.dynamicSmemBytes = LinCfg<NW>::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = static_cast<unsigned>(p.splits);
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = overlap ? 2 : 1;
+    TMLLM_CUDA_TRY(cudaLaunchKernelEx(&cfg, linear_kernel<NW>, a));
+    return TMLLM_OK;
+}
+
 int check_dtype(int dtype) {
     if (!valid_dtype(dtype)) return fail(TMLLM_UNSUPPORTED_DTYPE, "unknown dtype %d", dtype);
     return TMLLM_OK;
@@ -296,6 +701,68 @@ int tmllm_swiglu(tmllm_dtype dtype, const void* gate_up, void* out, size_t rows,
     else
         swiglu_kernel<float><<<grid_rows(total, 256), 256, 0, s>>>(
             static_cast<const float*>(gate_up), static_cast<float*>(out), rows, inter);
+    TMLLM_LAUNCH_TRY();
+    return TMLLM_OK;
+}
+
+size_t tmllm_linear_stats_bytes(int32_t n) {
+    if (n <= 0) return 0;
+    return static_cast<size_t>((n + kLinCols - 1) / kLinCols) * kLinRows * sizeof(float);
+}
+
+int tmllm_linear(const void* x, int64_t ldx, const void* norm_weight, const float* stats_in,
+                 float eps, const void* w, int64_t ldw, void* out, int64_t ldo,
+                 const void* residual, int64_t ldr, float* stats_out, int32_t rows, int32_t k,
+                 int32_t n, int32_t swiglu, uint32_t flags, tmllm_stream stream) {
+    clear_error();
+    if (rows <= 0 || k <= 0 || n <= 0)
+        return fail(TMLLM_INVALID_SHAPE, "linear dimensions must be positive");
+    if (rows > kLinRows)
+        return fail(TMLLM_INVALID_SHAPE, "tmllm_linear takes at most %d rows, got %d", kLinRows,
+                    rows);
+    if (swiglu != 0 && swiglu != 1) return fail(TMLLM_INVALID_ARGUMENT, "swiglu must be 0 or 1");
+    if (flags & ~static_cast<uint32_t>(TMLLM_LINEAR_OVERLAP))
+        return fail(TMLLM_INVALID_ARGUMENT, "unknown linear flags 0x%x", flags);
+    if (swiglu && residual)
+        return fail(TMLLM_INVALID_ARGUMENT, "a residual add and SwiGLU cannot be combined");
+    if (stats_in && !norm_weight)
+        return fail(TMLLM_INVALID_ARGUMENT, "row statistics are an input of the RMSNorm only");
+    if (!x || !w || !out) return fail(TMLLM_INVALID_ARGUMENT, "null tensor pointer");
+    if (k % 8 || n % 8)
+        return fail(TMLLM_INVALID_SHAPE, "linear K and N must be multiples of 8 (got %d, %d)", k, n);
+    const int64_t wcols = static_cast<int64_t>(n) * (swiglu ? 2 : 1);
+    if (ldx < k || ldw < wcols || ldo < n || (residual && ldr < n))
+        return fail(TMLLM_INVALID_SHAPE, "row strides must cover a row");
+    if (!aligned16(x) || !aligned16(w) || !aligned16(out) || (residual && !aligned16(residual)) ||
+        (norm_weight && !aligned16(norm_weight)) || ldx % 8 || ldw % 8 || ldo % 8 ||
+        (residual && ldr % 8))
+        return fail(TMLLM_INVALID_ARGUMENT,
+                    "x, w, out, the residual and the norm weight need 16-byte aligned rows");
+    if (norm_weight && (!std::isfinite(eps) || eps <= 0.0f))
+        return fail(TMLLM_INVALID_SHAPE, "RMSNorm epsilon must be positive, got %g",
+                    static_cast<double>(eps));
+    const LinearPlan p = plan_linear(k, n);
+    LinearArgs a{};
+    a.x = static_cast<const __half*>(x);
+    a.norm_w = static_cast<const __half*>(norm_weight);
+    a.stats_in = stats_in;
+    a.w = static_cast<const __half*>(w);
+    a.out = static_cast<__half*>(out);
+    a.resid = static_cast<const __half*>(residual);
+    a.stats_out = stats_out;
+    a.ldx = ldx;
+    a.ldw = ldw;
+    a.ldo = ldo;
+    a.ldr = ldr;
+    a.M = rows;
+    a.K = k;
+    a.N = n;
+    a.kchunk = p.kchunk;
+    a.eps = eps;
+    auto s = reinterpret_cast<cudaStream_t>(stream);
+    const bool overlap = (flags & TMLLM_LINEAR_OVERLAP) != 0;
+    const int rc = swiglu ? launch_linear<2>(a, p, overlap, s) : launch_linear<1>(a, p, overlap, s);
+    if (rc != TMLLM_OK) return rc;
     TMLLM_LAUNCH_TRY();
     return TMLLM_OK;
 }

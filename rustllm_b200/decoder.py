@@ -8,12 +8,20 @@ batch of sequences, one decode token per sequence per step:
     fused RoPE + KV append + GQA attention -> O GEMM -> residual add + RMSNorm ->
     fused gate/up GEMM -> SwiGLU -> down GEMM -> ... -> final norm -> lm_head -> argmax
 
-The attention, the norms, SwiGLU, the embedding and the greedy argmax are this package's
-CUDA kernels; the dense projections are plain cuBLAS GEMMs (torch.matmul).  Weights keep
-the reference's [in, out] layout (src/nn/linear.rs:26-27); Q, K, V and gate/up are
-concatenated along `out` so each pair/triple is one GEMM, and the attention reads q, k, v
-in place from the fused output through per-sequence strides.  A whole step is captured
-into one CUDA graph (``GraphedDecoder``).
+Every piece is one of this package's CUDA kernels.  With at most 16 sequences (F16) a
+decode step's layer projections run in ``linear`` (tmllm_linear), which folds the RMSNorm
+into the projection that reads it, SwiGLU into the gate/up projection and each residual add
+into the projection that produces it, so a layer is five launches:
+
+    x -> [norm + QKV] -> attention -> [O + residual -> x] -> [norm + gate/up + SwiGLU]
+      -> [down + residual -> x]
+
+Prompts and larger batches use plain cuBLAS GEMMs (torch.matmul) between the norm, SwiGLU
+and attention kernels.  Weights keep the reference's [in, out] layout
+(src/nn/linear.rs:26-27); Q, K, V and gate/up are concatenated along `out` so each
+pair/triple is one projection, and the attention reads q, k, v in place from the fused
+output through per-sequence strides.  A whole step is captured into one CUDA graph
+(``GraphedDecoder``).
 """
 from __future__ import annotations
 
@@ -85,6 +93,58 @@ PRESETS = {
     "smollm2-360m": ModelConfig(49152, 960, 2560, 32, 15, 5, 2304, 1e-5, 100000.0),
     "tinystories-110m": ModelConfig(32000, 768, 2048, 12, 12, 12, 1024, 1e-5, 10000.0),
 }
+
+
+LINEAR_MAX_ROWS = 64
+# Batches up to this many sequences run the fused projections in a decode step; larger ones
+# (up to 64 rows the kernel still takes) measured faster as cuBLAS GEMMs with the separate
+# norm and SwiGLU kernels, whose tiles reuse each weight tile over more rows.
+FUSED_STEP_MAX_ROWS = 16
+LINEAR_OVERLAP = 1  # TMLLM_LINEAR_OVERLAP
+
+
+def linear_stats(n: int, *, device=None) -> torch.Tensor:
+    """Device buffer for the row statistics of an [rows, n] projection output."""
+    nbytes = _lib.load().tmllm_linear_stats_bytes(n)
+    return torch.empty(int(nbytes) // 4, dtype=torch.float32, device=device)
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, *, norm_weight: torch.Tensor | None = None,
+           eps: float = 1e-5, residual: torch.Tensor | None = None, swiglu: bool = False,
+           out: torch.Tensor | None = None, stats_in: torch.Tensor | None = None,
+           stats_out: torch.Tensor | None = None, overlap: bool = False) -> torch.Tensor:
+    """out = x · w for x [rows <= 64, k], w [k, n] (F16, src/nn/linear.rs:105-170), with
+    optional RMSNorm of x (norm_weight, kernels/rmsnorm.metal), SwiGLU over w = [gate | up]
+    [k, 2n] (kernels/silu.metal) or a residual add (kernels/vector_add.metal) fused in.
+    ``stats_out`` (``linear_stats(n)``) receives the row statistics of ``out``; a later call
+    that normalises ``out`` takes them as ``stats_in`` instead of re-reading the rows.
+    ``overlap`` lets the launch start while the previous work on the stream drains (the
+    caller promises that work does not write ``w``)."""
+    if x.dim() != 2 or w.dim() != 2:
+        raise _lib.ModelFormat(f"Linear expects rank-2 input, got {tuple(x.shape)}")
+    rows, k = x.shape
+    if w.shape[0] != k:
+        raise _lib.ModelFormat(f"Linear input feature mismatch: expected {w.shape[0]}, got {k}")
+    if x.dtype != torch.float16 or w.dtype != torch.float16:
+        raise _lib.UnsupportedDType(f"linear takes F16 input and weight, got {x.dtype}, {w.dtype}")
+    n = w.shape[1] // 2 if swiglu else w.shape[1]
+    if x.stride(1) != 1 or w.stride(1) != 1:
+        raise _lib.NonContiguousTensor("linear needs unit column stride")
+    if out is None:
+        out = torch.empty((rows, n), dtype=x.dtype, device=x.device)
+    for st, cols in ((stats_in, k), (stats_out, n)):
+        if st is not None and (st.dtype != torch.float32 or
+                               st.numel() * 4 < _lib.load().tmllm_linear_stats_bytes(cols)):
+            raise _lib.InvalidArgument("row statistics need a linear_stats buffer")
+    call("tmllm_linear", x.data_ptr(), x.stride(0),
+         norm_weight.data_ptr() if norm_weight is not None else None,
+         stats_in.data_ptr() if stats_in is not None else None, eps, w.data_ptr(),
+         w.stride(0), out.data_ptr(), out.stride(0),
+         residual.data_ptr() if residual is not None else None,
+         residual.stride(0) if residual is not None else 0,
+         stats_out.data_ptr() if stats_out is not None else None, rows, k, n, int(swiglu),
+         LINEAR_OVERLAP if overlap else 0, stream_ptr(x.device))
+    return out
 
 
 class DecoderWeights:
@@ -226,6 +286,13 @@ class Decoder:
         self.bad = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.dt = dtype_code(self.dtype)
         self.max_len_hint = 0
+        i = cfg.intermediate_size
+        shapes = [(h, (hq + 2 * hkv) * d), (hq * d, h), (h, i), (i, h)]
+        # the fused projections: F16, at most 64 rows, dimensions in whole 16-byte chunks
+        self.fused = (self.dtype == torch.float16 and B <= FUSED_STEP_MAX_ROWS and
+                      all(k % 8 == 0 and n % 8 == 0 for k, n in shapes))
+        if self.fused:
+            self.stats = linear_stats(h, device=self.device)  # row statistics of x
 
     # -- pieces ------------------------------------------------------------------------
     def _norm(self, x, residual, weight, out, sum_out):
@@ -247,6 +314,21 @@ class Decoder:
              base + (hq + hkv) * d * es, self.attn.data_ptr(), None, hq, C.byref(opts),
              stream_ptr(self.device))
 
+    def _linear(self, x, w, out, *, norm=None, stats_in=False, residual=None,
+                swiglu=False) -> None:
+        """A projection of the residual stream; norm-fused ones read the row statistics
+        the previous residual add wrote (stats_in), residual adds write them.  Weights are
+        never written during a step, so every projection may start its weight prefetch
+        while the kernel before it drains."""
+        st = self.stats.data_ptr()
+        call("tmllm_linear", x.data_ptr(), x.stride(0), norm.data_ptr() if norm is not None
+             else None, st if stats_in else None, self.cfg.rms_norm_eps, w.data_ptr(),
+             w.stride(0), out.data_ptr(), out.stride(0),
+             residual.data_ptr() if residual is not None else None,
+             residual.stride(0) if residual is not None else 0,
+             st if residual is not None else None, x.shape[0], x.shape[1], out.shape[1],
+             int(swiglu), LINEAR_OVERLAP, stream_ptr(self.device))
+
     def forward_step(self) -> None:
         """One decode step for every sequence: reads ``self.ids``, appends K/V at each
         sequence's length, writes ``self.next_ids``.  Lengths are not advanced."""
@@ -254,6 +336,23 @@ class Decoder:
         call("tmllm_embedding", self.dt, w.embedding.data_ptr(), self.ids.data_ptr(),
              self.x.data_ptr(), self.B, cfg.hidden_size, cfg.vocab_size, self.bad.data_ptr(),
              stream_ptr(self.device))
+        if self.fused:
+            # x carries the residual stream; each producing projection adds into it
+            # (transformer_block.rs:137-158 with the adds and norms folded into projections)
+            for li, L in enumerate(w.layers):
+                # layer 0 reads the embedded rows once more for their statistics
+                self._linear(self.x, L["wqkv"], self.qkv, norm=L["attn_norm"], stats_in=li > 0)
+                self._attention(li)
+                self._linear(self.attn.view(self.B, -1), L["wo"], self.x, residual=self.x)
+                self._linear(self.x, L["wgu"], self.act, norm=L["mlp_norm"], stats_in=True,
+                             swiglu=True)
+                self._linear(self.act, L["wd"], self.x, residual=self.x)
+            # the vocabulary-wide head streams best as a cuBLAS GEMM (wide tiles)
+            self._norm(self.x, None, w.final_norm, self.hn, None)
+            torch.matmul(self.hn, w.lm_head, out=self.logits)
+            call("tmllm_argmax", self.dt, self.logits.data_ptr(), self.next_ids.data_ptr(),
+                 self.B, cfg.vocab_size, stream_ptr(self.device))
+            return
         residual = None
         for li, L in enumerate(w.layers):
             # x <- x + residual; hn <- rmsnorm(x)  (transformer_block.rs:137-139,148)

@@ -191,3 +191,24 @@ def test_model_dir_round_trip_gives_identical_logits(cuda, tmp_path):
         bad["lm_head.weight"].data = bad["lm_head.weight"].data[:, :10].copy()
         bad["lm_head.weight"].shape = (TINY.hidden_size, 10)
         DecoderWeights.from_weights(TINY, bad, device=cuda)
+
+
+def test_fused_step_matches_library_step(cuda):
+    """The decode step with fused projections (tmllm_linear: norm, SwiGLU and residual adds
+    folded in) gives the logits of the step built from cuBLAS GEMMs and the separate norm
+    and SwiGLU kernels."""
+    w = DecoderWeights(TINY, device=cuda, seed=13, std=0.08)
+    prompts = torch.randint(0, TINY.vocab_size, (4, 20), generator=torch.Generator().manual_seed(14))
+    a = Decoder(TINY, w, 4, device=cuda)
+    b = Decoder(TINY, w, 4, device=cuda)
+    assert a.fused
+    b.fused = False
+    for dec in (a, b):
+        dec.prefill(prompts.to(cuda))
+    for _ in range(4):
+        ids = a.next_ids.clone()
+        for dec in (a, b):
+            dec.ids.copy_(ids)
+            dec.forward_step()
+            dec.cache.advance(1)
+        assert rel(a.logits, b.logits) < 2e-2
