@@ -187,6 +187,10 @@ int tmllm_swiglu(tmllm_dtype dtype, const void* gate_up, void* out, size_t rows,
  * itself: a row computed alone equals the same row in any batch. */
 #define TMLLM_LINEAR_OVERLAP 1u
 size_t tmllm_linear_stats_bytes(int32_t n);
+/* Reads and clears the status word of tmllm_linear's kernels: TMLLM_TIMEOUT when a bounded
+ * device-side wait (the receipt of another CTA's partial sums) expired since the last read
+ * (the outputs of that call are undefined), else TMLLM_OK.  Synchronises with the device. */
+int tmllm_linear_status(int32_t* status);
 int tmllm_linear(const void* x, int64_t ldx, const void* norm_weight, const float* stats_in,
                  float eps, const void* w, int64_t ldw, void* out, int64_t ldo,
                  const void* residual, int64_t ldr, float* stats_out, int32_t rows, int32_t k,

@@ -143,6 +143,7 @@ _PROTOS = {
     "tmllm_swiglu": (C.c_int, [C.c_int, vp, vp, sz, sz, vp]),
     "tmllm_argmax": (C.c_int, [C.c_int, vp, vp, sz, sz, vp]),
     "tmllm_linear_stats_bytes": (sz, [i32]),
+    "tmllm_linear_status": (C.c_int, [vp]),
     "tmllm_linear": (C.c_int, [vp, i64, vp, vp, C.c_float, vp, i64, vp, i64, vp, i64, vp, i32,
                                i32, i32, i32, C.c_uint32, vp]),
     "tmllm_decode_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),

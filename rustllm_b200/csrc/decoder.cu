@@ -8,11 +8,8 @@
 #include <atomic>
 #include <cmath>
 
-#include <cooperative_groups.h>
-
 #include "common.cuh"
 
-namespace cg = cooperative_groups;
 
 namespace tmllm {
 namespace {
@@ -224,10 +221,12 @@ __global__ void __launch_bounds__(256) argmax_kernel(const T* __restrict__ logit
 //    optionally with the per-row sums of squares of the stored output (stats_out) that the
 //    next norm-fused projection reads instead of re-reading the rows.
 // CTA tile: every row (<= 64) × 64 output columns over one K chunk.  The K chunks of a
-// column tile are the CTAs of one thread-block cluster (grid y = cluster y <= 8): each
-// leaves its F32 partial tile in its shared memory, and after a cluster barrier CTA r sums
-// rows r, r + splits, ... over the cluster's shared memory in split order, so the split-K
-// reduction never touches global memory.  Weight and x tiles move through a cp.async
+// column tile are the CTAs of one thread-block cluster (grid y = cluster y <= 8): CTA r
+// finishes the row band [r*rbr, (r+1)*rbr); every CTA pushes each band of its F32 partial
+// tile into the band owner's shared memory with one bulk copy (cp.async.bulk
+// shared::cta -> shared::cluster, completing on the owner's mbarrier), and the owner sums
+// the received slots in split order, so the split-K reduction never touches global memory
+// and needs no cluster barrier after the K loop.  Weight and x tiles move through a cp.async
 // ring; products run on the warp-level tensor cores (mma.sync m16n8k16, F16 in, F32
 // accumulate; weight tiles through ldmatrix.trans): with 1-64 rows the layer is bound by
 // the weight bytes and by latency, not by the MMA rate.
@@ -241,13 +240,22 @@ constexpr int kLinThreads = 128;
 constexpr int kLinMaxSplits = 8;                 // portable cluster size
 constexpr int kLinSlab = kLinK * kLinCols * 2;  // one 64 x 64 F16 tile (weight or x)
 
+constexpr unsigned long long kLinWaitNs = 1000000000ull;  // bounded waits: 1 s
+
+__device__ int g_linear_status;
+
 template <int NW> struct LinCfg {
     static constexpr int STAGES = NW == 1 ? 4 : 3;  // 66 / 74 KB: three CTAs per SM
     static constexpr int STAGE = (NW + 1) * kLinSlab + 128;
     static constexpr int PSTRIDE = kLinCols * NW + 4;  // floats per partial row
-    static constexpr size_t SMEM = static_cast<size_t>(STAGES) * STAGE + kLinRows * 4;
-    static_assert(static_cast<size_t>(STAGES) * STAGE >= kLinRows * PSTRIDE * 4,
-                  "the partial tile reuses the ring");
+    static constexpr int RING = STAGES * STAGE;
+    static constexpr int OFF_INV = RING;               // [64] floats
+    static constexpr int OFF_RECV = RING + 256;        // receive barrier of the partial rows
+    static constexpr int OFF_RB = RING + 384;          // [splits][rows a CTA finishes][PSTRIDE]
+    // the receive buffer holds at most rows + splits - 1 partial rows
+    static constexpr size_t SMEM_MAX =
+        OFF_RB + static_cast<size_t>(kLinRows + kLinMaxSplits - 1) * PSTRIDE * 4;
+    static_assert(RING >= kLinRows * PSTRIDE * 4, "the partial tile reuses the ring");
 };
 
 struct LinearArgs {
@@ -269,14 +277,47 @@ __device__ __forceinline__ void grid_dependency_wait() {
 __device__ __forceinline__ void launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
+__device__ __forceinline__ uint32_t lin_smem(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ bool lin_mbar_test(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait on an mbarrier phase: false after kLinWaitNs, recording TMLLM_TIMEOUT (a
+// correct run waits microseconds).
+__device__ __forceinline__ bool lin_wait(uint32_t bar, uint32_t parity) {
+    unsigned long long t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+        if (lin_mbar_test(bar, parity)) return true;
+        if ((it & 63u) == 63u) {
+            unsigned long long t;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+            if (t0 == 0) {
+                t0 = t;
+            } else if (t - t0 > kLinWaitNs) {
+                atomicExch(&g_linear_status, TMLLM_TIMEOUT);
+                return false;
+            }
+        }
+    }
+}
 
 template <int NW>
 __global__ void __launch_bounds__(kLinThreads) linear_kernel(const LinearArgs a) {
     using Cfg = LinCfg<NW>;
     constexpr int S = Cfg::STAGES, STAGE = Cfg::STAGE;
     extern __shared__ __align__(128) unsigned char smem[];
-    float* inv_s = reinterpret_cast<float*>(smem + S * STAGE);  // [64]
-    cg::cluster_group cluster = cg::this_cluster();
+    float* inv_s = reinterpret_cast<float*>(smem + Cfg::OFF_INV);  // [64]
+    const uint32_t recv = lin_smem(smem + Cfg::OFF_RECV);
+    float* rb = reinterpret_cast<float*>(smem + Cfg::OFF_RB);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tile = blockIdx.x, split = blockIdx.y, splits = gridDim.y;
     const int n0 = tile * kLinCols;
@@ -286,6 +327,12 @@ __global__ void __launch_bounds__(kLinThreads) linear_kernel(const LinearArgs a)
     const int MT = (a.M + 15) / 16;
     const bool norm = a.norm_w != nullptr;
     launch_dependents();  // the next projection may start prefetching its weights
+    if (tid == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(recv) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    // published to the cluster here, awaited only before the partial rows are pushed
+    asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
 
     // stage layout: NW weight slabs, the x tile, 64 norm weights; 16-byte chunks swizzled
     // by row (chunk c of row r at r*128 + ((c ^ (r & 7)) << 4)); out-of-range chunks are
@@ -475,26 +522,67 @@ __global__ void __launch_bounds__(kLinThreads) linear_kernel(const LinearArgs a)
                     make_float2(acc[mt][j][2 * h], acc[mt][j][2 * h + 1]);
             }
     }
-    cluster.sync();  // every split's partial tile is complete and visible cluster-wide
+    // rows are finished in bands: CTA `split` owns rows [split*rbr, split*rbr + rbr).  Each
+    // CTA pushes the band of its partial tile to the band's owner with one bulk copy into
+    // the owner's receive buffer (slot = the sender's split); the owner sums the slots in
+    // split order.  A single K chunk finishes straight from its own partial tile.
+    const int rbr = (a.M + splits - 1) / splits;
+    const int m0 = split * rbr;
+    const int mine = max(0, min(a.M, m0 + rbr) - m0);
+    const float* src = ps;
+    if (splits > 1) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // ps, for the copy engine
+        __syncthreads();
+        asm volatile("barrier.cluster.wait;" ::: "memory");  // every receive barrier is initialised
+        if (tid == 0) {
+            for (int r = 0; r < splits; ++r) {
+                const int b0 = r * rbr, b1 = min(a.M, b0 + rbr);
+                if (b1 <= b0) continue;
+                uint32_t dst, bar;
+                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                             : "=r"(dst)
+                             : "r"(lin_smem(rb + split * rbr * Cfg::PSTRIDE)), "r"(r));
+                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(bar) : "r"(recv), "r"(r));
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes"
+                    " [%0], [%1], %2, [%3];" ::"r"(dst),
+                    "r"(lin_smem(ps + b0 * Cfg::PSTRIDE)),
+                    "r"(static_cast<uint32_t>((b1 - b0) * Cfg::PSTRIDE * 4)), "r"(bar)
+                    : "memory");
+            }
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+        bool ok = true;
+        if (mine > 0) {
+            if (tid == 0)
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(recv),
+                             "r"(static_cast<uint32_t>(splits * mine * Cfg::PSTRIDE * 4))
+                             : "memory");
+            ok = lin_wait(recv, 0);
+        }
+        src = ok ? rb : nullptr;
+    } else {
+        asm volatile("barrier.cluster.wait;" ::: "memory");
+        __syncthreads();
+    }
 
-    // CTA `split` finishes rows split, split + splits, ...: 16-byte stores of 8 outputs
-    // per thread and chunk, the residual added on the way; the 8 chunks of a row sit in 8
-    // neighbouring lanes, which sum the row's squares
-    const int my_rows = a.M > split ? (a.M - split + splits - 1) / splits : 0;
-    const int items = ((my_rows * 8 + kLinThreads - 1) / kLinThreads) * kLinThreads;
+    // 16-byte stores of 8 outputs per thread and item, the residual added on the way; the
+    // 8 chunks of a row sit in 8 neighbouring lanes, which sum the row's squares
+    const int slot = splits > 1 ? rbr * Cfg::PSTRIDE : 0;  // floats between receive slots
+    const int items = ((mine * 8 + kLinThreads - 1) / kLinThreads) * kLinThreads;
     for (int q = tid; q < items; q += kLinThreads) {
-        const int m = split + splits * (q >> 3), c = q & 7;
+        const int m = m0 + (q >> 3), c = q & 7;
         const int col = n0 + c * 8;
-        const bool ok = (q >> 3) < my_rows && col < a.N;
+        const bool live = src != nullptr && (q >> 3) < mine && col < a.N;
         float sq = 0.f;
-        if (ok) {
+        if (live) {
             // every split's partial loaded together, then summed in split order
+            const float* base = src + (splits > 1 ? (m - m0) : m) * Cfg::PSTRIDE + c * 8;
             float4 pg[kLinMaxSplits][2], pu[kLinMaxSplits][2];
 #pragma unroll
             for (int r = 0; r < kLinMaxSplits; ++r) {
                 if (r < splits) {
-                    const float4* pr = reinterpret_cast<const float4*>(
-                        cluster.map_shared_rank(ps, r) + m * Cfg::PSTRIDE + c * 8);
+                    const float4* pr = reinterpret_cast<const float4*>(base + r * slot);
                     pg[r][0] = pr[0];
                     pg[r][1] = pr[1];
                     if (NW == 2) {
@@ -549,10 +637,11 @@ __global__ void __launch_bounds__(kLinThreads) linear_kernel(const LinearArgs a)
             sq += __shfl_xor_sync(0xffffffffu, sq, 1);
             sq += __shfl_xor_sync(0xffffffffu, sq, 2);
             sq += __shfl_xor_sync(0xffffffffu, sq, 4);
-            if (c == 0 && (q >> 3) < my_rows) a.stats_out[tile * kLinRows + m] = sq;
+            if (src != nullptr && c == 0 && (q >> 3) < mine) a.stats_out[tile * kLinRows + m] = sq;
         }
     }
-    cluster.sync();  // peers are done reading this CTA's partial tile
+    if (splits > 1 && tid == 0)  // the pushed rows have left this CTA's shared memory
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
 struct LinearPlan {
@@ -588,13 +677,16 @@ int launch_linear(const LinearArgs& a, const LinearPlan& p, bool overlap, cudaSt
     if (!bit || !(opted.load(std::memory_order_relaxed) & bit)) {
         TMLLM_CUDA_TRY(cudaFuncSetAttribute(linear_kernel<NW>,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            static_cast<int>(LinCfg<NW>::SMEM)));
+                                            static_cast<int>(LinCfg<NW>::SMEM_MAX)));
         opted.fetch_or(bit, std::memory_order_relaxed);
     }
+    const int rbr = (a.M + p.splits - 1) / p.splits;  // rows a CTA finishes
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(p.tiles), static_cast<unsigned>(p.splits));
     cfg.blockDim = dim3(kLinThreads);
-    cfg.dynamicSmemBytes = LinCfg<NW>::SMEM;
+    cfg.dynamicSmemBytes =
+        LinCfg<NW>::OFF_RB +
+        (p.splits > 1 ? static_cast<size_t>(p.splits) * rbr * LinCfg<NW>::PSTRIDE * 4 : 0);
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -702,6 +794,16 @@ int tmllm_swiglu(tmllm_dtype dtype, const void* gate_up, void* out, size_t rows,
         swiglu_kernel<float><<<grid_rows(total, 256), 256, 0, s>>>(
             static_cast<const float*>(gate_up), static_cast<float*>(out), rows, inter);
     TMLLM_LAUNCH_TRY();
+    return TMLLM_OK;
+}
+
+int tmllm_linear_status(int32_t* status) {
+    clear_error();
+    if (!status) return fail(TMLLM_INVALID_ARGUMENT, "null status pointer");
+    int v = 0, zero = 0;
+    TMLLM_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_linear_status, sizeof(int)));
+    TMLLM_CUDA_TRY(cudaMemcpyToSymbol(g_linear_status, &zero, sizeof(int)));
+    *status = v;
     return TMLLM_OK;
 }
 

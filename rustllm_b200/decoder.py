@@ -103,6 +103,14 @@ FUSED_STEP_MAX_ROWS = 16
 LINEAR_OVERLAP = 1  # TMLLM_LINEAR_OVERLAP
 
 
+def linear_status() -> int:
+    """Reads and clears the status word of the projection kernels (0, or TMLLM_TIMEOUT
+    after an expired device-side wait)."""
+    v = C.c_int32(0)
+    call("tmllm_linear_status", C.byref(v))
+    return int(v.value)
+
+
 def linear_stats(n: int, *, device=None) -> torch.Tensor:
     """Device buffer for the row statistics of an [rows, n] projection output."""
     nbytes = _lib.load().tmllm_linear_stats_bytes(n)

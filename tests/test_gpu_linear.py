@@ -9,7 +9,7 @@ import pytest
 import torch
 
 import rustllm_b200 as rb
-from rustllm_b200.decoder import linear, linear_stats
+from rustllm_b200.decoder import linear, linear_stats, linear_status
 
 pytestmark = pytest.mark.gpu
 
@@ -52,6 +52,7 @@ def test_plain_projection(cuda, rows, k, n):
     _, x, w = inputs(cuda, rows, k, n, rows * 7 + k)
     got = linear(x, w)
     assert rel(got, reference(x, w)) < 2e-3
+    assert linear_status() == 0
 
 
 @pytest.mark.parametrize("rows", [1, 5, 64])
