@@ -197,7 +197,9 @@ int tmllm_linear(const void* x, int64_t ldx, const void* norm_weight, const floa
                  int32_t n, int32_t swiglu, uint32_t flags, tmllm_stream stream);
 
 /* Replaces greedy sampling (src/generation/sampler.rs:79-88, on the CPU in the reference):
- * ids[r] = index of the largest of logits [rows, vocab] row r; the last of equal maxima. */
+ * ids[r] = index of the largest finite logit of logits [rows, vocab] row r under
+ * f32::total_cmp (-0 < +0; NaN and infinities are skipped), the last of equal maxima;
+ * -1 when row r has no finite logit (the reference returns TinyError::Sampling). */
 int tmllm_argmax(tmllm_dtype dtype, const void* logits, int32_t* ids, size_t rows, size_t vocab,
                  tmllm_stream stream);
 

@@ -171,40 +171,79 @@ __global__ void swiglu_vec_kernel(const __half* __restrict__ gu, __half* __restr
     }
 }
 
-// Greedy next token (src/generation/sampler.rs:79-88): the index of the largest logit;
-// among equal maxima the last one wins (Iterator::max_by keeps the last maximum).
+// Greedy next token (src/generation/sampler.rs:79-88, greedy_from_slice): the index of the
+// largest FINITE logit under f32::total_cmp (so -0 < +0), the last one among equal maxima
+// (Iterator::max_by keeps the last maximum); -1 when a row holds no finite logit (the
+// reference's TinyError::Sampling).  A candidate is the 64-bit key (total-order bits of the
+// value) << 32 | index, so one unsigned max picks the value and, among equal values, the
+// largest index.  One 1024-thread CTA per row; with 16-byte aligned rows every thread
+// issues its 16-byte loads (up to eight at a time) before it compares.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int64_t i) {
+    if (!isfinite(v)) return 0ull;
+    const uint32_t u = __float_as_uint(v);
+    const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // total_cmp order
+    return (static_cast<unsigned long long>(ord) << 32) | static_cast<uint32_t>(i);
+}
+
 template <typename T>
-__global__ void __launch_bounds__(256) argmax_kernel(const T* __restrict__ logits,
-                                                     int32_t* __restrict__ ids, int64_t vocab) {
-    __shared__ float bv[256];
-    __shared__ int64_t bi[256];
+__global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ logits,
+                                                      int32_t* __restrict__ ids, int64_t vocab,
+                                                      bool vec) {
+    __shared__ unsigned long long best_w[32];
     const T* row = logits + static_cast<int64_t>(blockIdx.x) * vocab;
-    float best = -INFINITY;
-    int64_t idx = -1;
-    for (int64_t i = threadIdx.x; i < vocab; i += 256) {
-        const float v = to_f32<T>(row[i]);
-        if (idx < 0 || v >= best) {  // later index wins ties within a thread
-            best = v;
-            idx = i;
-        }
-    }
-    bv[threadIdx.x] = best;
-    bi[threadIdx.x] = idx;
-    __syncthreads();
-    for (int s = 128; s > 0; s >>= 1) {
-        if (threadIdx.x < s) {
-            const float ov = bv[threadIdx.x + s];
-            const int64_t oi = bi[threadIdx.x + s];
-            const bool take = oi >= 0 && (bi[threadIdx.x] < 0 || ov > bv[threadIdx.x] ||
-                                          (ov == bv[threadIdx.x] && oi > bi[threadIdx.x]));
-            if (take) {
-                bv[threadIdx.x] = ov;
-                bi[threadIdx.x] = oi;
+    const int tid = threadIdx.x;
+    unsigned long long best = 0ull;  // below every finite key
+    if (vec) {
+        constexpr int E = 16 / sizeof(T);  // elements per 16-byte chunk
+        const int64_t nch = vocab / E;
+        const uint4* rv = reinterpret_cast<const uint4*>(row);
+        for (int64_t c0 = tid; c0 < nch; c0 += 8 * 1024) {
+            uint4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int64_t c = c0 + static_cast<int64_t>(u) * 1024;
+                v[u] = c < nch ? __ldg(rv + c) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int64_t c = c0 + static_cast<int64_t>(u) * 1024;
+                if (c >= nch) break;
+                float f[E];
+                Chunk<T>::unpack(v[u], f);
+#pragma unroll
+                for (int e = 0; e < E; ++e) {
+                    const unsigned long long k = argmax_key(f[e], c * E + e);
+                    best = k > best ? k : best;
+                }
             }
         }
-        __syncthreads();
+        for (int64_t i = nch * E + tid; i < vocab; i += 1024) {  // tail (vocab % E)
+            const unsigned long long k = argmax_key(to_f32<T>(row[i]), i);
+            best = k > best ? k : best;
+        }
+    } else {
+        for (int64_t i = tid; i < vocab; i += 1024) {
+            const unsigned long long k = argmax_key(to_f32<T>(row[i]), i);
+            best = k > best ? k : best;
+        }
     }
-    if (threadIdx.x == 0) ids[blockIdx.x] = static_cast<int32_t>(bi[0] < 0 ? 0 : bi[0]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+        best = k > best ? k : best;
+    }
+    if ((tid & 31) == 0) best_w[tid >> 5] = best;
+    __syncthreads();
+    if (tid < 32) {
+        best = best_w[tid];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+            best = k > best ? k : best;
+        }
+        if (tid == 0)
+            ids[blockIdx.x] = best ? static_cast<int32_t>(best & 0xffffffffull) : -1;
+    }
 }
 
 // ---- Linear layers of a decode step (src/nn/linear.rs: y = x · W with W [in, out]) --------
@@ -879,12 +918,14 @@ int tmllm_argmax(tmllm_dtype dtype, const void* logits, int32_t* ids, size_t row
     if (rows > 0x7fffffffull) return fail(TMLLM_INVALID_SHAPE, "too many rows");
     if (!logits || !ids) return fail(TMLLM_INVALID_ARGUMENT, "null tensor pointer");
     auto s = reinterpret_cast<cudaStream_t>(stream);
+    const size_t row_bytes = vocab * (dtype == TMLLM_F16 ? 2 : 4);
+    const bool vec = aligned16(logits) && row_bytes % 16 == 0;  // every row 16-byte aligned
     if (dtype == TMLLM_F16)
-        argmax_kernel<__half><<<static_cast<unsigned>(rows), 256, 0, s>>>(
-            static_cast<const __half*>(logits), ids, vocab);
+        argmax_kernel<__half><<<static_cast<unsigned>(rows), 1024, 0, s>>>(
+            static_cast<const __half*>(logits), ids, static_cast<int64_t>(vocab), vec);
     else
-        argmax_kernel<float><<<static_cast<unsigned>(rows), 256, 0, s>>>(
-            static_cast<const float*>(logits), ids, vocab);
+        argmax_kernel<float><<<static_cast<unsigned>(rows), 1024, 0, s>>>(
+            static_cast<const float*>(logits), ids, static_cast<int64_t>(vocab), vec);
     TMLLM_LAUNCH_TRY();
     return TMLLM_OK;
 }

@@ -86,6 +86,51 @@ def test_argmax_takes_last_of_equal_maxima(cuda):
     assert int(ids[1]) == 40000 and int(ids[2]) == 7
 
 
+def greedy_from_slice(row):
+    """sampler.rs:79-88 restated: finite logits only, f32::total_cmp, last maximum wins;
+    None when no logit is finite."""
+    import struct
+    best, best_i = None, None
+    for i, v in enumerate(row):
+        if v != v or v in (float("inf"), float("-inf")):
+            continue
+        u = struct.unpack("<I", struct.pack("<f", v))[0]
+        key = (~u & 0xFFFFFFFF) if u & 0x80000000 else (u | 0x80000000)
+        if best is None or key >= best:
+            best, best_i = key, i
+    return best_i
+
+
+@pytest.mark.parametrize("dtype,code", [(torch.float16, 1), (torch.float32, 0)])
+@pytest.mark.parametrize("vocab", [49152, 1003])
+def test_argmax_follows_greedy_from_slice(cuda, dtype, code, vocab):
+    """Non-finite logits are skipped (even +inf), -0 < +0 under total_cmp, ties go to the
+    last index, a row without a finite logit gives -1; 16-byte rows (vectorised loads) and
+    odd rows (scalar loads), F16 and F32."""
+    g = torch.Generator(device=cuda).manual_seed(vocab + code)
+    x = torch.randn((6, vocab), generator=g, device=cuda).to(dtype)
+    x[0, 5] = float("inf")              # skipped: the finite maximum wins
+    x[0, 9] = float("nan")
+    x[1].fill_(-1.0)
+    x[1, 3] = -0.0
+    x[1, 4] = 0.0                       # +0 above -0
+    x[1, 2] = -0.0
+    x[2].fill_(float("nan"))
+    x[2, 0] = float("-inf")             # nothing finite: -1
+    x[3].fill_(2.5)                     # all equal: the last index
+    x[4, vocab - 1] = 50.0              # the tail of an odd row
+    x[5, 0] = 50.0
+    x[5, vocab // 2] = 50.0
+    ids = torch.empty(6, dtype=torch.int32, device=cuda)
+    _lib.call("tmllm_argmax", code, x.data_ptr(), ids.data_ptr(), 6, vocab, stream(cuda))
+    host = x.float().cpu().tolist()
+    for r in range(6):
+        want = greedy_from_slice(host[r])
+        assert int(ids[r]) == (-1 if want is None else want), r
+    assert int(ids[1]) == 4 and int(ids[2]) == -1 and int(ids[3]) == vocab - 1
+    assert int(ids[5]) == vocab // 2
+
+
 def test_decoder_logits_match_float32_model(cuda):
     w = DecoderWeights(TINY, device=cuda, seed=1, std=0.08)
     dec = Decoder(TINY, w, 1, device=cuda)
