@@ -241,11 +241,18 @@ typedef struct tmllm_decode_opts {
                             /* 0 = the capacity.  Affects speed only, never results.   */
     int32_t variant;        /* 0 = automatic; 1 = CUDA-core FMA kernel; 2 = tensor-core */
                             /* (mma.sync) kernel, F16 with head_dim 64 or 128 only     */
-    int32_t reserved;
+    int32_t flags;          /* TMLLM_DECODE_OVERLAP or 0                                */
     int64_t q_seq_stride;   /* elements between sequences in q (0 = q_heads*head_dim),  */
     int64_t kv_seq_stride;  /* and in k_new/v_new (0 = num_kv_heads*head_dim): lets the */
                             /* outputs of one fused QKV projection be read in place.    */
 } tmllm_decode_opts;
+
+/* tmllm_decode_opts.flags: the tensor-core decode launch may overlap the tail of the work
+ * queued before it on the stream (programmatic dependent launch).  The lengths, block table
+ * and cached K/V are read before that work has finished, so the caller promises it does not
+ * write them; q, k_new and v_new are read, and anything is written, only after it has
+ * finished.  Ignored by the other kernels and with the cross-GPU exchange. */
+#define TMLLM_DECODE_OVERLAP 1
 
 /* Bytes of scratch tmllm_gqa_decode needs for `num_splits` splits (0 = enough for any
  * automatic choice for this shape on this device).  Zero it once (tmllm_decode_workspace_init)

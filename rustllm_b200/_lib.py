@@ -111,7 +111,7 @@ class DecodeOpts(C.Structure):
     _fields_ = [("scale", C.c_float), ("num_splits", i32), ("out_f32", i32),
                 ("rope_cos", vp), ("rope_sin", vp), ("rope_len", i32),
                 ("rope_pos_offset", i32), ("max_len_hint", i64), ("variant", i32),
-                ("reserved", i32), ("q_seq_stride", i64), ("kv_seq_stride", i64)]
+                ("flags", i32), ("q_seq_stride", i64), ("kv_seq_stride", i64)]
 
 
 class CacheConfig(C.Structure):

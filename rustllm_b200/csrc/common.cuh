@@ -156,6 +156,17 @@ __device__ __forceinline__ float warp_max(float v) {
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
+// Programmatic dependent launch: a kernel launched with programmatic stream serialisation
+// may start before the kernel ahead of it on the stream has finished; griddepcontrol.wait
+// blocks until that kernel has completed and its writes are visible (immediately when
+// there is no such dependency), launch_dependents lets the next such kernel start early.
+__device__ __forceinline__ void grid_dependency_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

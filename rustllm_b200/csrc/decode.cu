@@ -53,6 +53,7 @@ struct DecodeArgs {
     uint32_t epoch;          // exchange step number (1, 2, ...)
     int64_t q_stride;        // elements between sequences in q
     int64_t kv_stride;       // elements between sequences in k_new / v_new
+    int32_t overlap;         // launched with programmatic stream serialisation
 };
 
 // Physical slot of 16-byte chunk `c` of tile row `r` (XOR swizzle inside groups of 8).
@@ -147,6 +148,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_split_kernel(const D
     const int nsplit = gridDim.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = a.group;
+    launch_dependents();
+    // With an overlapped launch (TMLLM_DECODE_OVERLAP) everything up to the K/V ring's
+    // prologue reads only the cache (lengths, block table, cached K/V), which the kernel
+    // ahead of this one does not write; q, k_new and v_new are read after its completion.
     const int cached = a.seq_lens[b] < 0 ? 0 : a.seq_lens[b];
     const bool has_new = a.k_new != nullptr;
     const int L = cached + (has_new ? 1 : 0);
@@ -749,6 +754,7 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? 4 : 2) decode_mma_ke
         if (s < nmine) load_sub(s, s, sub_block(s));
         cp_async_commit();
     }
+    if (a.overlap) grid_dependency_wait();  // q, k_new, v_new come from the kernel ahead
 
     // ---- (while the first K/V tiles are in flight) q rows, rotated and rounded to F16,
     // into q_s; rows >= G are zero
@@ -1242,7 +1248,21 @@ int launch_tiled(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
         return fail(TMLLM_INVALID_ARGUMENT, "too many splits (%u) for the merge scratch", grid.z);
     TMLLM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(bytes)));
-    fn<<<grid, kDecodeThreads, bytes, s>>>(a);
+    if (a.overlap) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(kDecodeThreads);
+        cfg.dynamicSmemBytes = bytes;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        TMLLM_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, a));
+    } else {
+        fn<<<grid, kDecodeThreads, bytes, s>>>(a);
+    }
     TMLLM_LAUNCH_TRY();
     return TMLLM_OK;
 }
@@ -1353,6 +1373,8 @@ int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
     const int G = q_heads / Hkv;
     if (opts && (opts->variant < 0 || opts->variant > 2))
         return fail(TMLLM_INVALID_ARGUMENT, "unknown decode variant %d", opts->variant);
+    if (opts && (opts->flags & ~TMLLM_DECODE_OVERLAP))
+        return fail(TMLLM_INVALID_ARGUMENT, "unknown decode flags 0x%x", opts->flags);
     const bool mma_shape = kv->dtype == TMLLM_F16 && (D == 64 || D == 128) &&
                            !(opts && opts->variant == 1);
     if (opts && opts->variant == 2 && !mma_shape)
@@ -1424,6 +1446,8 @@ int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
         return fail(TMLLM_INVALID_SHAPE, "sequence strides of q / k_new must cover a sequence");
     a.q_stride = o.q_seq_stride > 0 ? o.q_seq_stride : static_cast<int64_t>(q_heads) * D;
     a.kv_stride = o.kv_seq_stride > 0 ? o.kv_seq_stride : static_cast<int64_t>(Hkv) * D;
+    // the overlapped launch is for the single-GPU tensor-core kernel (not the exchange)
+    a.overlap = (o.flags & TMLLM_DECODE_OVERLAP) && !ex ? 1 : 0;
     if (ex && !(mma_shape && o.variant != 1))
         return fail(TMLLM_INVALID_ARGUMENT,
                     "the cross-GPU exchange needs the tensor-core decode (F16, head_dim 64/128)");

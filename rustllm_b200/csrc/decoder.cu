@@ -310,12 +310,6 @@ struct LinearArgs {
     float eps;
 };
 
-__device__ __forceinline__ void grid_dependency_wait() {
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-__device__ __forceinline__ void launch_dependents() {
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
 __device__ __forceinline__ uint32_t lin_smem(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

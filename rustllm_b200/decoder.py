@@ -101,6 +101,7 @@ LINEAR_MAX_ROWS = 64
 # norm and SwiGLU kernels, whose tiles reuse each weight tile over more rows.
 FUSED_STEP_MAX_ROWS = 16
 LINEAR_OVERLAP = 1  # TMLLM_LINEAR_OVERLAP
+DECODE_OVERLAP = 1  # TMLLM_DECODE_OVERLAP
 
 
 def linear_status() -> int:
@@ -315,7 +316,10 @@ class Decoder:
         w = self.qkv.shape[1]
         base = self.qkv.data_ptr()
         es = self.qkv.element_size()
-        opts = DecodeOpts(q_seq_stride=w, kv_seq_stride=w, max_len_hint=self.max_len_hint)
+        # the QKV projection ahead does not touch the cache: the attention may start its
+        # K/V prefetch while that projection drains
+        opts = DecodeOpts(q_seq_stride=w, kv_seq_stride=w, max_len_hint=self.max_len_hint,
+                          flags=DECODE_OVERLAP)
         cos, sin = self.rope
         opts.rope_cos, opts.rope_sin, opts.rope_len = cos.data_ptr(), sin.data_ptr(), cos.shape[0]
         call("tmllm_cache_decode", self.cache.handle, layer, base, base + hq * d * es,

@@ -257,3 +257,39 @@ def test_fused_step_matches_library_step(cuda):
             dec.forward_step()
             dec.cache.advance(1)
         assert rel(a.logits, b.logits) < 2e-2
+
+
+def test_overlapped_decode_launch_matches_plain(cuda):
+    """TMLLM_DECODE_OVERLAP (the attention's K/V prefetch overlapping the kernel ahead) gives
+    bit-identical outputs and appended rows to the plain launch, also right after a kernel
+    that writes q and k_new."""
+    B, hq, hkv, d, n = 3, 8, 2, 64, 300
+    outs = []
+    for flags in (0, 1):
+        cache = rb.PagedKvCache(1, B, n + 2, hkv, d, dtype=torch.float16, block_size=16,
+                                shuffle_seed=2, device=cuda)
+        g = torch.Generator(device=cuda).manual_seed(3)
+        for s in range(B):
+            x = torch.randn((hkv, n - 40 * s, d), generator=g, device=cuda).half()
+            cache.append(0, s, x, x)
+            cache.advance(n - 40 * s, s)
+            cache.reserve(s, 1)
+        qkv = torch.empty((B, (hq + 2 * hkv) * d), dtype=torch.float16, device=cuda)
+        src = torch.randn((B, (hq + 2 * hkv) * d), generator=g, device=cuda).half()
+        out = torch.empty((B, hq, d), dtype=torch.float16, device=cuda)
+        w = qkv.shape[1]
+        opts = _lib.DecodeOpts(q_seq_stride=w, kv_seq_stride=w, flags=flags)
+        base, es = qkv.data_ptr(), qkv.element_size()
+        qkv.copy_(src * 1.5)  # the kernel right ahead writes q, k_new and v_new
+        _lib.call("tmllm_cache_decode", cache.handle, 0, base, base + hq * d * es,
+                  base + (hq + hkv) * d * es, out.data_ptr(), None, hq, C.byref(opts),
+                  stream(cuda))
+        torch.cuda.synchronize()
+        k, v = cache.gather(0, 0)
+        outs.append((out.clone(), k.clone(), v.clone()))
+    assert all(torch.equal(a, b) for a, b in zip(outs[0], outs[1]))
+    with pytest.raises(rb.InvalidArgument):
+        opts = _lib.DecodeOpts(flags=2)
+        _lib.call("tmllm_cache_decode", cache.handle, 0, base, base + hq * d * es,
+                  base + (hq + hkv) * d * es, out.data_ptr(), None, hq, C.byref(opts),
+                  stream(cuda))
