@@ -102,3 +102,47 @@ def test_workspace_size_arithmetic():
         return (x + 255) // 256 * 256
     assert got == up(b * hkv * 4) + up(b * hq * s * 2 * 4) + up(b * hq * s * d * 4)
     assert lib.tmllm_decode_workspace_bytes(0, hq, hkv, d, s) == 0
+
+
+def test_linear_host_validation():
+    """tmllm_linear rejects bad shapes, strides, alignment and option mixes on the host,
+    before any device work; its statistics buffer size is [ceil(n/64)][64] floats."""
+    lib = _lib.load()
+    p = C.c_void_p(256)  # 16-byte aligned, never dereferenced
+
+    def lin(x=p, ldx=64, norm=None, stats_in=None, eps=1e-5, w=p, ldw=64, out=p, ldo=64,
+            res=None, ldr=0, stats_out=None, rows=4, k=64, n=64, swiglu=0, flags=0):
+        return lib.tmllm_linear(x, ldx, norm, stats_in, eps, w, ldw, out, ldo, res, ldr,
+                                stats_out, rows, k, n, swiglu, flags, None)
+    assert lin(rows=0) == 2 and lin(rows=65) == 2      # 1..64 rows
+    assert lin(k=60, ldx=64) == 2 and lin(n=60) == 2   # whole 16-byte chunks
+    assert lin(swiglu=2) == 1
+    assert lin(flags=2) == 1                           # only TMLLM_LINEAR_OVERLAP
+    assert lin(swiglu=1, ldw=128, res=p, ldr=64) == 1  # SwiGLU and a residual together
+    assert lin(stats_in=p) == 1                        # statistics without a norm
+    assert lin(x=None) == 1 and lin(out=None) == 1
+    assert lin(ldx=32) == 2                            # stride shorter than a row
+    assert lin(swiglu=1, ldw=64) == 2                  # [gate | up] needs 2n columns
+    assert lin(x=C.c_void_p(258)) == 1                 # 16-byte alignment
+    assert lin(ldx=68) == 1                            # row stride in whole chunks
+    assert lin(norm=p, eps=0.0) == 2 and lin(norm=p, eps=float("nan")) == 2
+    assert b"epsilon" in lib.tmllm_last_error()
+    assert lib.tmllm_linear_stats_bytes(960) == 15 * 64 * 4
+    assert lib.tmllm_linear_stats_bytes(1000) == 16 * 64 * 4
+    assert lib.tmllm_linear_stats_bytes(0) == 0
+
+
+def test_argmax_and_decode_flag_validation():
+    lib = _lib.load()
+    p = C.c_void_p(256)
+    assert lib.tmllm_argmax(1, p, p, 2, 0, None) == 2          # empty vocabulary
+    assert lib.tmllm_argmax(1, None, p, 2, 8, None) == 1
+    assert lib.tmllm_argmax(9, p, p, 2, 8, None) == 5          # unknown dtype
+    assert lib.tmllm_argmax(1, p, p, 0, 8, None) == 0          # no rows: nothing to do
+    kv = _lib.PagedKV(k_cache=256, v_cache=256, block_table=256, seq_lens=256, num_blocks=4,
+                      num_seqs=1, num_kv_heads=2, head_dim=64, block_size=16,
+                      max_blocks_per_seq=4, dtype=1)
+    opts = _lib.DecodeOpts(flags=4)  # only TMLLM_DECODE_OVERLAP is defined
+    assert lib.tmllm_gqa_decode(C.byref(kv), p, None, None, p, None, 4, C.byref(opts), None,
+                                0, None) == 1
+    assert b"flags" in lib.tmllm_last_error()
