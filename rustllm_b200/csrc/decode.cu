@@ -629,9 +629,15 @@ struct MmaCfg {
     static_assert(OFF_FIN >= 4 * 16 * D * 4, "warp-merge scratch and staging fit in the rings");
 };
 
-template <int D, int STAGES>
+// PT (positions-major, D = 64 and G <= 8): S^T[16 positions x 8 heads] = K Q^T with K as
+// the A operand and the query heads as N, O^T[D x 8] += V^T P^T with V (ldmatrix.trans) as
+// A and P^T as B, moved from S^T's accumulator layout by movmatrix.trans.  Half the MMAs,
+// exponentials and rescales of the head-major form (whose M = 16 rows carry G real query
+// heads), which is what bounds the loop at short contexts (instruction issue, not memory).
+template <int D, int STAGES, bool PT>
 __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? 4 : 2) decode_mma_kernel(const DecodeArgs a) {
     using Cfg = MmaCfg<D, STAGES>;
+    static_assert(!PT || D == 64, "the positions-major form is instantiated for D = 64");
     constexpr int C = Cfg::C, ROW = Cfg::ROW, SUBB = Cfg::SUBB, QROW = Cfg::QROW;
     constexpr int KS = D / 16;  // k-steps of QK
     constexpr int NT = D / 8;   // n-tiles of PV
@@ -800,9 +806,18 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? 4 : 2) decode_mma_ke
         }
     }
 
-    // ---- Q fragments (A operand, 16 rows x D) into registers
-    uint32_t qa[KS][4];
-    {
+    const int g4 = lane >> 2, t4 = lane & 3;
+    // ---- Q fragments into registers: head-major, A operand (16 rows x D); positions-major,
+    // B operand (Q^T: k = dims, n = the 8 heads): thread holds q[g4][16ks + 2t4 (+8) ..+1]
+    constexpr int QA = PT ? 2 : 4;
+    uint32_t qa[KS][QA];
+    if constexpr (PT) {
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            qa[ks][0] = *reinterpret_cast<const uint32_t*>(q_s + g4 * QROW + ks * 16 + 2 * t4);
+            qa[ks][1] = *reinterpret_cast<const uint32_t*>(q_s + g4 * QROW + ks * 16 + 8 + 2 * t4);
+        }
+    } else {
         const int mi = lane >> 3, r = (mi & 1) * 8 + (lane & 7);
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
@@ -811,11 +826,14 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? 4 : 2) decode_mma_ke
         }
     }
 
-    float o[NT][4];
+    // head-major: o[j] = O[rows g4, g4+8][dims 8j + 2t4 ..]; m_r / l_r of rows g4, g4 + 8.
+    // positions-major: o[mt] = O^T[dims 16mt + g4 (+8)][heads 2t4, 2t4+1]; m_r / l_r of
+    // heads 2t4, 2t4 + 1.
+    constexpr int NO = PT ? D / 16 : NT;
+    float o[NO][4];
 #pragma unroll
-    for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    for (int j = 0; j < NO; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
     float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
-    const int g4 = lane >> 2, t4 = lane & 3;
 
     for (int it = 0; it < nmine; ++it) {
         cp_async_wait<STAGES - 2>();
@@ -838,109 +856,201 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? 4 : 2) decode_mma_ke
             }
             __syncwarp();
         }
-        // S = Q K^T: two n-tiles of 8 positions, even/odd k-steps in separate accumulators
-        float sc[2][4], sx[2][4];
+        if constexpr (PT) {
+            // S^T = K Q^T: A = K rows (positions) by ldmatrix, B = Q^T from registers; even
+            // and odd k-steps in separate accumulators.  st[e]: positions g4 (e < 2) and
+            // g4 + 8, heads 2t4 + (e & 1).
+            float st[4] = {0.f, 0.f, 0.f, 0.f}, sx[4] = {0.f, 0.f, 0.f, 0.f};
+            {
+                const int mi = lane >> 3, r = (mi & 1) * 8 + (lane & 7);
+                const uint32_t rbase = smem_u32(ks + r * ROW);
 #pragma unroll
-        for (int n = 0; n < 2; ++n)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) sc[n][e] = sx[n][e] = 0.f;
-        {
-            const int mi = lane >> 3, r = (mi >> 1) * 8 + (lane & 7);
-            const uint32_t rbase = smem_u32(ks + r * ROW);
-#pragma unroll
-            for (int kstep = 0; kstep < KS; ++kstep) {
-                const int c = kstep * 2 + (mi & 1);
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4(rbase + swz<C>(r, c) * 16, b0, b1, b2, b3);
-                float* c0 = (kstep & 1) ? sx[0] : sc[0];
-                float* c1 = (kstep & 1) ? sx[1] : sc[1];
-                mma16816(c0, qa[kstep][0], qa[kstep][1], qa[kstep][2], qa[kstep][3], b0, b1);
-                mma16816(c1, qa[kstep][0], qa[kstep][1], qa[kstep][2], qa[kstep][3], b2, b3);
+                for (int kstep = 0; kstep < KS; ++kstep) {
+                    const int c = kstep * 2 + (mi >> 1);
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4(rbase + swz<C>(r, c) * 16, a0, a1, a2, a3);
+                    mma16816((kstep & 1) ? sx : st, a0, a1, a2, a3, qa[kstep][0], qa[kstep][1]);
+                }
             }
-        }
-        const bool full = base + 16 <= t1;
-#pragma unroll
-        for (int n = 0; n < 2; ++n)
+            const bool full = base + 16 <= t1;
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                float v = (sc[n][e] + sx[n][e]) * a.scale_log2;
-                if (!full && base + n * 8 + t4 * 2 + (e & 1) >= t1) v = -INFINITY;
-                sc[n][e] = v;
+                float v = (st[e] + sx[e]) * a.scale_log2;
+                if (!full && base + g4 + (e >= 2 ? 8 : 0) >= t1) v = -INFINITY;
+                st[e] = v;
             }
-        // online softmax over the 16 positions, rows g4 and g4 + 8
-        float alpha[2];
+            // online softmax per head over the 16 positions (8 lanes of equal t4 x 2 rows)
+            float alpha[2];
 #pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-            float mx = fmaxf(fmaxf(sc[0][rr * 2], sc[0][rr * 2 + 1]),
-                             fmaxf(sc[1][rr * 2], sc[1][rr * 2 + 1]));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-            const float m_new = fmaxf(m_r[rr], mx);
-            // rows that have seen no position yet keep m = -inf: use 0 as the reference
-            const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-            alpha[rr] = fast_exp2(m_r[rr] - m_use);
-            float sum = 0.f;
+            for (int h = 0; h < 2; ++h) {
+                float mx = fmaxf(st[h], st[2 + h]);
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                const float m_new = fmaxf(m_r[h], mx);
+                const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+                alpha[h] = fast_exp2(m_r[h] - m_use);
+                const float p0 = fast_exp2(st[h] - m_use), p1 = fast_exp2(st[2 + h] - m_use);
+                st[h] = p0;
+                st[2 + h] = p1;
+                l_r[h] = l_r[h] * alpha[h] + (p0 + p1);
+                m_r[h] = m_new;
+            }
+            if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
 #pragma unroll
-            for (int n = 0; n < 2; ++n)
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const float p = fast_exp2(sc[n][rr * 2 + e] - m_use);
-                    sc[n][rr * 2 + e] = p;
-                    sum += p;
+                for (int mt = 0; mt < NO; ++mt) {
+                    o[mt][0] *= alpha[0];
+                    o[mt][1] *= alpha[1];
+                    o[mt][2] *= alpha[0];
+                    o[mt][3] *= alpha[1];
                 }
-            l_r[rr] = l_r[rr] * alpha[rr] + sum;
-            m_r[rr] = m_new;
-        }
-        if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
-#pragma unroll
-            for (int j = 0; j < NT; ++j) {
-                o[j][0] *= alpha[0];
-                o[j][1] *= alpha[0];
-                o[j][2] *= alpha[1];
-                o[j][3] *= alpha[1];
             }
-        }
-        // O += P V: P's A fragment is S's accumulator layout
-        const uint32_t pa0 = pack_half2(sc[0][0], sc[0][1]);
-        const uint32_t pa1 = pack_half2(sc[0][2], sc[0][3]);
-        const uint32_t pa2 = pack_half2(sc[1][0], sc[1][1]);
-        const uint32_t pa3 = pack_half2(sc[1][2], sc[1][3]);
-        {
-            const int mi = lane >> 3, r = (mi & 1) * 8 + (lane & 7);
-            const uint32_t rbase = smem_u32(vs + r * ROW);
+            // P^T as the B operand: the 8 x 8 blocks (positions 0-7 | 8-15) x heads of the
+            // accumulator layout, transposed across the warp
+            uint32_t pb0, pb1;
+            const uint32_t pk0 = pack_half2(st[0], st[1]), pk1 = pack_half2(st[2], st[3]);
+            asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(pb0) : "r"(pk0));
+            asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(pb1) : "r"(pk1));
+            // O^T += V^T P^T: A = V^T (dims x positions) by ldmatrix.trans of the V rows
+            {
+                const int mi = lane >> 3, r = (mi >> 1) * 8 + (lane & 7);
+                const uint32_t rbase = smem_u32(vs + r * ROW);
 #pragma unroll
-            for (int jj = 0; jj < NT / 2; ++jj) {
-                const int c = jj * 2 + (mi >> 1);
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4_t(rbase + swz<C>(r, c) * 16, b0, b1, b2, b3);
-                mma16816(o[2 * jj], pa0, pa1, pa2, pa3, b0, b1);
-                mma16816(o[2 * jj + 1], pa0, pa1, pa2, pa3, b2, b3);
+                for (int mt = 0; mt < NO; ++mt) {
+                    const int c = mt * 2 + (mi & 1);
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4_t(rbase + swz<C>(r, c) * 16, a0, a1, a2, a3);
+                    mma16816(o[mt], a0, a1, a2, a3, pb0, pb1);
+                }
+            }
+        } else {
+            // S = Q K^T: two n-tiles of 8 positions, even/odd k-steps in separate accumulators
+            float sc[2][4], sx[2][4];
+    #pragma unroll
+            for (int n = 0; n < 2; ++n)
+    #pragma unroll
+                for (int e = 0; e < 4; ++e) sc[n][e] = sx[n][e] = 0.f;
+            {
+                const int mi = lane >> 3, r = (mi >> 1) * 8 + (lane & 7);
+                const uint32_t rbase = smem_u32(ks + r * ROW);
+    #pragma unroll
+                for (int kstep = 0; kstep < KS; ++kstep) {
+                    const int c = kstep * 2 + (mi & 1);
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4(rbase + swz<C>(r, c) * 16, b0, b1, b2, b3);
+                    float* c0 = (kstep & 1) ? sx[0] : sc[0];
+                    float* c1 = (kstep & 1) ? sx[1] : sc[1];
+                    mma16816(c0, qa[kstep][0], qa[kstep][1], qa[kstep][2], qa[kstep][3], b0, b1);
+                    mma16816(c1, qa[kstep][0], qa[kstep][1], qa[kstep][2], qa[kstep][3], b2, b3);
+                }
+            }
+            const bool full = base + 16 <= t1;
+    #pragma unroll
+            for (int n = 0; n < 2; ++n)
+    #pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    float v = (sc[n][e] + sx[n][e]) * a.scale_log2;
+                    if (!full && base + n * 8 + t4 * 2 + (e & 1) >= t1) v = -INFINITY;
+                    sc[n][e] = v;
+                }
+            // online softmax over the 16 positions, rows g4 and g4 + 8
+            float alpha[2];
+    #pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+                float mx = fmaxf(fmaxf(sc[0][rr * 2], sc[0][rr * 2 + 1]),
+                                 fmaxf(sc[1][rr * 2], sc[1][rr * 2 + 1]));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                const float m_new = fmaxf(m_r[rr], mx);
+                // rows that have seen no position yet keep m = -inf: use 0 as the reference
+                const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+                alpha[rr] = fast_exp2(m_r[rr] - m_use);
+                float sum = 0.f;
+    #pragma unroll
+                for (int n = 0; n < 2; ++n)
+    #pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const float p = fast_exp2(sc[n][rr * 2 + e] - m_use);
+                        sc[n][rr * 2 + e] = p;
+                        sum += p;
+                    }
+                l_r[rr] = l_r[rr] * alpha[rr] + sum;
+                m_r[rr] = m_new;
+            }
+            if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
+    #pragma unroll
+                for (int j = 0; j < NT; ++j) {
+                    o[j][0] *= alpha[0];
+                    o[j][1] *= alpha[0];
+                    o[j][2] *= alpha[1];
+                    o[j][3] *= alpha[1];
+                }
+            }
+            // O += P V: P's A fragment is S's accumulator layout
+            const uint32_t pa0 = pack_half2(sc[0][0], sc[0][1]);
+            const uint32_t pa1 = pack_half2(sc[0][2], sc[0][3]);
+            const uint32_t pa2 = pack_half2(sc[1][0], sc[1][1]);
+            const uint32_t pa3 = pack_half2(sc[1][2], sc[1][3]);
+            {
+                const int mi = lane >> 3, r = (mi & 1) * 8 + (lane & 7);
+                const uint32_t rbase = smem_u32(vs + r * ROW);
+    #pragma unroll
+                for (int jj = 0; jj < NT / 2; ++jj) {
+                    const int c = jj * 2 + (mi >> 1);
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4_t(rbase + swz<C>(r, c) * 16, b0, b1, b2, b3);
+                    mma16816(o[2 * jj], pa0, pa1, pa2, pa3, b0, b1);
+                    mma16816(o[2 * jj + 1], pa0, pa1, pa2, pa3, b2, b3);
+                }
             }
         }
     }
     cp_async_wait<0>();
 #pragma unroll
     for (int rr = 0; rr < 2; ++rr) {
-        l_r[rr] += __shfl_xor_sync(0xffffffffu, l_r[rr], 1);
-        l_r[rr] += __shfl_xor_sync(0xffffffffu, l_r[rr], 2);
+        if constexpr (PT) {  // a head's positions sit in the 8 lanes of equal t4
+            l_r[rr] += __shfl_xor_sync(0xffffffffu, l_r[rr], 4);
+            l_r[rr] += __shfl_xor_sync(0xffffffffu, l_r[rr], 8);
+            l_r[rr] += __shfl_xor_sync(0xffffffffu, l_r[rr], 16);
+        } else {
+            l_r[rr] += __shfl_xor_sync(0xffffffffu, l_r[rr], 1);
+            l_r[rr] += __shfl_xor_sync(0xffffffffu, l_r[rr], 2);
+        }
     }
     __syncthreads();
 
     // ---- combine the four warps: red[w][16][D] (rings are free now)
     float* red = reinterpret_cast<float*>(smem);
+    if constexpr (PT) {  // rows = heads 2t4, 2t4 + 1 (< 8), dims 16mt + g4 (+8)
 #pragma unroll
-    for (int j = 0; j < NT; ++j) {
-        const int d = j * 8 + t4 * 2;
-        red[(warp * 16 + g4) * D + d] = o[j][0];
-        red[(warp * 16 + g4) * D + d + 1] = o[j][1];
-        red[(warp * 16 + g4 + 8) * D + d] = o[j][2];
-        red[(warp * 16 + g4 + 8) * D + d + 1] = o[j][3];
-    }
-    if (t4 == 0) {
-        wm[warp * 16 + g4] = m_r[0];
-        wm[warp * 16 + g4 + 8] = m_r[1];
-        wl[warp * 16 + g4] = l_r[0];
-        wl[warp * 16 + g4 + 8] = l_r[1];
+        for (int mt = 0; mt < NO; ++mt) {
+            const int d = mt * 16 + g4;
+            red[(warp * 16 + 2 * t4) * D + d] = o[mt][0];
+            red[(warp * 16 + 2 * t4 + 1) * D + d] = o[mt][1];
+            red[(warp * 16 + 2 * t4) * D + d + 8] = o[mt][2];
+            red[(warp * 16 + 2 * t4 + 1) * D + d + 8] = o[mt][3];
+        }
+        if (g4 == 0) {
+            wm[warp * 16 + 2 * t4] = m_r[0];
+            wm[warp * 16 + 2 * t4 + 1] = m_r[1];
+            wl[warp * 16 + 2 * t4] = l_r[0];
+            wl[warp * 16 + 2 * t4 + 1] = l_r[1];
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+            const int d = j * 8 + t4 * 2;
+            red[(warp * 16 + g4) * D + d] = o[j][0];
+            red[(warp * 16 + g4) * D + d + 1] = o[j][1];
+            red[(warp * 16 + g4 + 8) * D + d] = o[j][2];
+            red[(warp * 16 + g4 + 8) * D + d + 1] = o[j][3];
+        }
+        if (t4 == 0) {
+            wm[warp * 16 + g4] = m_r[0];
+            wm[warp * 16 + g4 + 8] = m_r[1];
+            wl[warp * 16 + g4] = l_r[0];
+            wl[warp * 16 + g4 + 8] = l_r[1];
+        }
     }
     __syncthreads();
     // per row g: M = max_w m_w, weights 2^(m_w - M)
@@ -1267,10 +1377,10 @@ int launch_tiled(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
     return TMLLM_OK;
 }
 
-template <int D, int STAGES>
+template <int D, int STAGES, bool PT = false>
 int launch_mma(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
     using Cfg = MmaCfg<D, STAGES>;
-    auto* fn = decode_mma_kernel<D, STAGES>;
+    auto* fn = decode_mma_kernel<D, STAGES, PT>;
     const size_t bytes = static_cast<size_t>(Cfg::BYTES);
     if ((2 * static_cast<size_t>(grid.z) + 2) * 16 * 4 > static_cast<size_t>(Cfg::OFF_FIN))
         return fail(TMLLM_INVALID_ARGUMENT, "too many splits (%u) for the merge scratch", grid.z);
@@ -1293,6 +1403,7 @@ int launch_decode(int dtype, int D, int variant, const DecodeArgs& a, dim3 grid,
                   bool* done) {
     *done = true;
     if (dtype == TMLLM_F16 && a.group <= 16 && variant != 1) {
+        if (D == 64 && a.group <= 8 && a.ex == nullptr) return launch_mma<64, 3, true>(a, grid, s);
         if (D == 64) return launch_mma<64, 3>(a, grid, s);
         if (D == 128) return launch_mma<128, 3>(a, grid, s);
     }

@@ -154,6 +154,8 @@ CASES = [
     (np.float16, 6, 2, 96, [200], 16, None),
     (np.float32, 4, 4, 2, [9], 4, None),
     (np.float16, 32, 8, 128, [0, 15, 16, 31], 16, None),
+    (np.float16, 24, 3, 64, [777, 5, 64, 0], 24, 10000.0),  # D = 64, G = 8, ragged pages
+    (np.float16, 7, 7, 64, [4099, 31], 48, None),
 ]
 
 
