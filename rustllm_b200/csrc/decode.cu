@@ -631,9 +631,10 @@ struct MmaCfg {
 
 // PT (positions-major, D = 64 and G <= 8): S^T[16 positions x 8 heads] = K Q^T with K as
 // the A operand and the query heads as N, O^T[D x 8] += V^T P^T with V (ldmatrix.trans) as
-// A and P^T as B, moved from S^T's accumulator layout by movmatrix.trans.  Half the MMAs,
-// exponentials and rescales of the head-major form (whose M = 16 rows carry G real query
-// heads), which is what bounds the loop at short contexts (instruction issue, not memory).
+// A and P^T as B, moved from S^T's accumulator layout by movmatrix.trans.  Half the MMAs
+// and rescales and 6 instead of 10 exponentials a thread per sub-tile compared with the
+// head-major form (whose M = 16 rows carry only G real query heads): at short contexts the
+// loop is bound by a warp's per-sub-tile chain, not by memory bandwidth.
 template <int D, int STAGES, bool PT>
 __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? 4 : 2) decode_mma_kernel(const DecodeArgs a) {
     using Cfg = MmaCfg<D, STAGES>;
