@@ -131,6 +131,9 @@ def linear(x: torch.Tensor, w: torch.Tensor, *, norm_weight: torch.Tensor | None
     caller promises that work does not write ``w``)."""
     if x.dim() != 2 or w.dim() != 2:
         raise _lib.ModelFormat(f"Linear expects rank-2 input, got {tuple(x.shape)}")
+    given = [t for t in (x, w, norm_weight, residual, out, stats_in, stats_out) if t is not None]
+    if any(not t.is_cuda or t.device != x.device for t in given):
+        raise _lib.InvalidArgument("linear tensors must live on one CUDA device")
     rows, k = x.shape
     if w.shape[0] != k:
         raise _lib.ModelFormat(f"Linear input feature mismatch: expected {w.shape[0]}, got {k}")

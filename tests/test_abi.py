@@ -146,3 +146,13 @@ def test_argmax_and_decode_flag_validation():
     assert lib.tmllm_gqa_decode(C.byref(kv), p, None, None, p, None, 4, C.byref(opts), None,
                                 0, None) == 1
     assert b"flags" in lib.tmllm_last_error()
+
+
+def test_linear_wrapper_refuses_host_tensors():
+    """The Python wrapper checks placement before any pointer reaches the library."""
+    import torch
+    from rustllm_b200.decoder import linear
+    x = torch.zeros((2, 64), dtype=torch.float16)
+    w = torch.zeros((64, 64), dtype=torch.float16)
+    with pytest.raises(_lib.InvalidArgument):
+        linear(x, w)
