@@ -13,7 +13,7 @@ import torch
 
 from . import _lib
 from ._lib import DecodeOpts, PagedKV, call
-from .tensor_ops import dtype_code, stream_ptr
+from .tensor_ops import dtype_code, on_device, stream_ptr
 
 
 class DecodeWorkspace:
@@ -48,6 +48,7 @@ def gqa_decode(kv: PagedKV, q: torch.Tensor, k_new: torch.Tensor | None,
 
     q [num_seqs, Hq, D]; k_new, v_new [num_seqs, Hkv, D] or both None; out
     [num_seqs, Hq, D] in ``out_dtype`` (default: q's dtype); lse [num_seqs, Hq] F32."""
+    on_device(q.device, q, k_new, v_new, out, lse, rope)
     if out is None:
         out = torch.empty(q.shape, dtype=out_dtype or q.dtype, device=q.device)
     if out.dtype not in (q.dtype, torch.float32) or out.shape != q.shape:
@@ -69,6 +70,7 @@ def gqa_decode(kv: PagedKV, q: torch.Tensor, k_new: torch.Tensor | None,
 def merge_lse(parts_o: torch.Tensor, parts_lse: torch.Tensor, *, out: torch.Tensor | None = None,
               out_dtype: torch.dtype = torch.float32, out_lse: torch.Tensor | None = None):
     """Log-sum-exp merge: parts_o [n, rows, D] F32 (normalised), parts_lse [n, rows] F32."""
+    on_device(parts_o.device, parts_o, parts_lse, out, out_lse)
     n, rows, d = parts_o.shape
     if out is None:
         out = torch.empty((rows, d), dtype=out_dtype, device=parts_o.device)
@@ -114,6 +116,7 @@ def gqa_prefill(kv: PagedKV, q: torch.Tensor, k_new: torch.Tensor | None,
     ``rows_per_seq`` rows per sequence.  Row i of sequence s is appended at seq_lens[s] + i
     and attends keys [0, seq_lens[s] + i]; with k_new = v_new = None nothing is appended
     (those positions already hold the rows).  Returns out [rows, Hq, D]."""
+    on_device(q.device, q, k_new, v_new, out, q_start, rope)
     rows, hq, d = q.shape
     hkv = kv.num_kv_heads
     qs = _row_stride(q, hq, d, "q")

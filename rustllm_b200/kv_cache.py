@@ -15,7 +15,7 @@ import torch
 
 from . import _lib
 from ._lib import CacheConfig, DecodeOpts, PagedKV, call
-from .tensor_ops import dtype_code, stream_ptr
+from .tensor_ops import dtype_code, on_device, stream_ptr
 
 _TORCH = {_lib.F32: torch.float32, _lib.F16: torch.float16}
 
@@ -101,6 +101,7 @@ class PagedKvCache:
 
     def append(self, layer: int, seq: int, key: torch.Tensor, value: torch.Tensor) -> None:
         """Writes key/value [Hkv, n, D] (or [1, Hkv, n, D]) at the sequence's length."""
+        on_device(self.device, key, value)
         if key.dtype != value.dtype or key.dtype != self.dtype:
             raise _lib.UnsupportedDType(
                 f"KV cache dtype mismatch: cache={self.dtype}, input={key.dtype}/{value.dtype}")
@@ -160,6 +161,7 @@ class PagedKvCache:
         Returns out [num_seqs, Hq, D] (and lse [num_seqs, Hq] F32 when ``want_lse`` or
         ``lse`` is given).  Lengths are not advanced; call ``advance()`` once per step
         after the last layer."""
+        on_device(self.device, q, k_new, v_new, out, lse, rope)
         if q.dtype != self.dtype:
             raise _lib.UnsupportedDType(
                 f"SelfAttention/cache dtype mismatch: attention={q.dtype}, cache={self.dtype}")
@@ -205,6 +207,7 @@ class PagedKvCache:
         its length + i and attends positions [0, length + i].  Returns out
         [num_seqs * n, Hq, D].  Lengths are not advanced; call ``advance(n)`` after the last
         layer."""
+        on_device(self.device, q, k_new, v_new, out, rope)
         if q.dtype != self.dtype:
             raise _lib.UnsupportedDType(
                 f"SelfAttention/cache dtype mismatch: attention={q.dtype}, cache={self.dtype}")

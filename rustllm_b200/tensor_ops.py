@@ -37,6 +37,19 @@ def _on_cuda(*ts: torch.Tensor) -> None:
             raise _lib.InvalidArgument("tensors must live on a CUDA device")
 
 
+def on_device(device: torch.device, *ts) -> None:
+    """Every given tensor (None entries and (cos, sin) pairs allowed) lives on ``device``:
+    a host or foreign-device pointer must never reach a kernel."""
+    for t in ts:
+        if t is None:
+            continue
+        if isinstance(t, (tuple, list)):
+            on_device(device, *t)
+            continue
+        if not t.is_cuda or t.device != device:
+            raise _lib.InvalidArgument(f"tensors must live on {device}, got one on {t.device}")
+
+
 def _same_dtype(op: str, a: torch.Tensor, b: torch.Tensor) -> None:
     if a.dtype != b.dtype:
         raise _lib.UnsupportedDType(f"{op} dtype mismatch: {a.dtype} vs {b.dtype}")

@@ -156,3 +156,18 @@ def test_linear_wrapper_refuses_host_tensors():
     w = torch.zeros((64, 64), dtype=torch.float16)
     with pytest.raises(_lib.InvalidArgument):
         linear(x, w)
+
+
+def test_attention_wrappers_refuse_host_tensors():
+    """gqa_decode / gqa_prefill / merge_lse check tensor placement before any pointer
+    reaches the library (a host pointer in a kernel would fault the device)."""
+    import torch
+    import rustllm_b200 as rb
+    q = torch.zeros((1, 4, 64), dtype=torch.float16)
+    kv = _lib.PagedKV(num_seqs=1, num_kv_heads=2, head_dim=64, block_size=16, dtype=1)
+    with pytest.raises(_lib.InvalidArgument):
+        rb.gqa_decode(kv, q, None, None, None)
+    with pytest.raises(_lib.InvalidArgument):
+        rb.gqa_prefill(kv, q, None, None, rows_per_seq=1)
+    with pytest.raises(_lib.InvalidArgument):
+        rb.merge_lse(torch.zeros((2, 4, 64)), torch.zeros((2, 4)))
