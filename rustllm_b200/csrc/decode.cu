@@ -1641,7 +1641,12 @@ int32_t decode_auto_splits_lens(const int64_t* lens, int64_t B, int64_t Hkv, int
         }
         return n * Hkv;
     };
-    int64_t hi = (hint + 255) / 256;  // never chunks under 256 positions
+    // Never chunks under 256 positions; and when one CTA per (sequence, KV head) already
+    // covers every SM, a split only adds a merge, so chunks keep >= 1024 positions there
+    // (measured: 577 positions x 192 heads ran 12.7 us unsplit vs 13.9 us in 3 chunks; 64
+    // sequences of 256-2048 positions x 5 heads stay best at 2 chunks of <= 1152).
+    int64_t hi = (hint + 255) / 256;
+    if (B * Hkv >= static_cast<int64_t>(device_sm_count())) hi = hint / 1024;
     if (hi > 1024) hi = 1024;
     if (hi < 1) hi = 1;
     int64_t lo = 1;
