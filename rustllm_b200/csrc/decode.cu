@@ -148,10 +148,6 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_split_kernel(const D
     const int nsplit = gridDim.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = a.group;
-    launch_dependents();
-    // With an overlapped launch (TMLLM_DECODE_OVERLAP) everything up to the K/V ring's
-    // prologue reads only the cache (lengths, block table, cached K/V), which the kernel
-    // ahead of this one does not write; q, k_new and v_new are read after its completion.
     const int cached = a.seq_lens[b] < 0 ? 0 : a.seq_lens[b];
     const bool has_new = a.k_new != nullptr;
     const int L = cached + (has_new ? 1 : 0);
@@ -656,6 +652,29 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? 4 : 2) decode_mma_ke
     const int nsplit = gridDim.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = a.group;
+    launch_dependents();
+    // With an overlapped launch (TMLLM_DECODE_OVERLAP) everything up to the K/V ring's
+    // prologue reads only the cache (lengths, block table, cached K/V), which the kernel
+    // ahead of this one does not write; q, k_new and v_new are read after its completion.
+    const bool whole_blocks = (a.block_size % 16) == 0;
+    const int t0 = split * a.chunk;
+    // Block-table entry of this warp's sub-tile j (with whole blocks a sub-tile lies in one
+    // block; out-of-table positions give -1).  At D = 64 (short sub-tiles, where a table
+    // read per sub-tile left the ring waiting at short contexts) the entries sit 32 at a
+    // time in the lanes: lane l holds the entry of sub-tile jb + l (`cur`) and of
+    // jb + 32 + l (`nxt`, read a batch ahead), so issuing a sub-tile's copies never waits
+    // on a table read; the first two batches depend on the chunk only and are read
+    // together with the length.  At D = 128 the entry is read at issue (measured 1.5 %
+    // faster there: fewer registers on the critical loop).
+    auto entry = [&](int j) -> int64_t {
+        return whole_blocks ? block_of(a, b, t0 + (warp + 4 * j) * 16) : -1;
+    };
+    constexpr bool kLaneTable = D == 64;
+    int64_t cur = -1, nxt = -1;
+    if (kLaneTable) {
+        cur = entry(lane);
+        nxt = entry(32 + lane);
+    }
     const int cached = a.seq_lens[b] < 0 ? 0 : a.seq_lens[b];
     const bool has_new = a.k_new != nullptr;
     const int L = cached + (has_new ? 1 : 0);
@@ -663,7 +682,6 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? 4 : 2) decode_mma_ke
     if (splits_b < 1) splits_b = 1;
     if (splits_b > nsplit) splits_b = nsplit;
     if (split >= splits_b) return;
-    const int t0 = split * a.chunk;
     const int t1 = (split == splits_b - 1) ? L : min(L, t0 + a.chunk);
     const int nsub = t1 > t0 ? (t1 - t0 + 15) / 16 : 0;
     const bool owns_new = has_new && cached >= t0 && cached < t1;
@@ -676,32 +694,17 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? 4 : 2) decode_mma_ke
     const unsigned char* kbase = static_cast<const unsigned char*>(a.k_cache);
     const unsigned char* vbase = static_cast<const unsigned char*>(a.v_cache);
     const int lc = lane % C, lr0 = lane / C;
-    const bool whole_blocks = (a.block_size % 16) == 0;
     int dst_off[Cfg::LOADS];
 #pragma unroll
     for (int k = 0; k < Cfg::LOADS; ++k) {
         const int r = lr0 + k * Cfg::RSTEP;
         dst_off[k] = r * ROW + swz<C>(r, lc) * 16;
     }
-    // Block-table entry of sub-tile j (with whole blocks a sub-tile lies in one block).  At
-    // D = 64 (short sub-tiles, where a table read per sub-tile left the ring waiting at
-    // short contexts) the entries sit 32 at a time in the lanes: lane l holds the entry of
-    // sub-tile jb + l (`cur`) and of jb + 32 + l (`nxt`, read a batch ahead), so issuing a
-    // sub-tile's copies never waits on a table read.  At D = 128 the entry is read at
-    // issue (measured 1.5 % faster there: fewer registers on the critical loop).  Called
-    // with warp-uniform j = 0, 1, 2, ...
-    auto entry = [&](int j) -> int64_t {
-        return whole_blocks && j < nmine ? block_of(a, b, t0 + (warp + 4 * j) * 16) : -1;
-    };
-    constexpr bool kLaneTable = D == 64;
+    // called with warp-uniform j = 0, 1, 2, ... < nmine
     int jb = 0;
-    int64_t cur = -1, nxt = -1;
-    if (kLaneTable) {
-        cur = entry(lane);
-        nxt = entry(32 + lane);
-    }
     auto sub_block = [&](int j) -> int64_t {
-        if (!kLaneTable) return entry(j);
+        if (!kLaneTable)
+            return whole_blocks && j < nmine ? block_of(a, b, t0 + (warp + 4 * j) * 16) : -1;
         if (j >= jb + 32) {
             jb += 32;
             cur = nxt;
