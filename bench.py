@@ -9,8 +9,14 @@ steps, so every step appends at the same position and does identical work.  The 
 K/V read per step is larger than the 126 MB L2, so no flush is needed between steps.
 
 At N > 1 GPUs the sequence is split along its positions (strong scaling: total work
-fixed); each rank attends its share and the partial (O, lse) are merged after one NCCL
-all-gather.
+fixed); each rank attends its share and the partial (O, lse) are exchanged and merged
+inside the decode kernel itself over NVLink (``--exchange p2p``, the default: every rank's
+final CTAs store their rows into the other ranks' buffers and merge what arrives), or
+after one NCCL all-gather plus a merge kernel (``--exchange nccl``).
+
+On one GPU consecutive steps are launched with programmatic dependent launch: a step's
+block-table reads and first K/V copies may start while the previous step drains; it reads
+q / k_new / v_new and writes anything only after the previous step has finished.
 
 Other workloads are parity-test cases, not bench lines.
 
@@ -36,10 +42,28 @@ sys.path.insert(0, ROOT)
 METRIC = ("decode tok/s; fused KV-append+GQA attn HBM GB/s vs B200 peak at 1/2/4/8 GPU")
 HQ, HKV, D, CACHED, BS = 32, 8, 128, 131072, 16
 ESIZE = 2
-# DRAM bytes (read + write) of one full-size launch of decode_mma_kernel<128,3>, from the
-# ncu capture summarised in profiles/decode_mma_kernel_cfg4_32k.md (32768-position case,
-# reads scaled by the cached length, writes constant).
-NCU_TRAFFIC_PER_LAUNCH = 541.2e6
+# The workload both arms report (the driver compares the two `config` dicts).
+CFG4_CONFIG = {"workload": "cfg4 long-context decode attention op (Llama-3-8B attention "
+                           "shape), 131072 cached + 1 appended, batch 1",
+               "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "cached": CACHED,
+               "block_size": BS,
+               "l2": "inputs larger than L2 (537 MB K/V per step vs 126 MB L2)"}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one full-size launch of the
+# tensor-core decode kernel, from one ncu capture of a 32768-position launch (reads scaled
+# by the cached length, writes constant).  The figure belongs to the kernel source it was
+# captured on: `roofline.traffic` is reported only while rustllm_b200/csrc/decode.cu still
+# has that SHA-256.
+NCU_TRAFFIC = {"bytes_per_launch": 541.2e6,
+               "decode_cu_sha256": "unset"}
+# Untimed steps run between the warm-up and the timed region so the GPU's clocks have left
+# their idle state (the clock sampler's start-up pause idles the GPU for 0.4 s).
+SETTLE_STEPS = 2000
+
+
+def decode_cu_sha256() -> str:
+    import hashlib
+    with open(os.path.join(ROOT, "rustllm_b200", "csrc", "decode.cu"), "rb") as f:
+        return hashlib.sha256(f.read()).hexdigest()
 
 
 def algorithmic_bytes(cached: int = CACHED, hq: int = HQ, hkv: int = HKV, d: int = D,
@@ -194,10 +218,8 @@ def run_reference(args) -> None:
         "n_gpus": world, "steps": steps, "warmup": min(args.warmup, 1),
         "ms_per_step": 1000.0 * secs / steps, "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f16",
-        "data": "synthetic (seeded N(0,1) K/V, q)",
-        "config": {"workload": "cfg4 long-context decode attention op (Llama-3-8B attention "
-                               "shape), 131072 cached + 1 appended, batch 1",
-                   "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "cached": CACHED},
+        "data": "synthetic (seeded N(0,1) K/V, q; random block permutation)",
+        "config": dict(CFG4_CONFIG),
         "hbm_gbs_equiv": algorithmic_bytes() * tok_s / 1e9,
         "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port",
                          "sample": f"{steps} full config-4 steps (all 32 query heads x 131073 "
@@ -233,9 +255,11 @@ def run_ours(args) -> None:
 
     torch.manual_seed(1234 + rank)
     cached = args.cached
+    overlap = world == 1 and not args.no_overlap
     sp = SequenceSplitAttention(cached, HQ, HKV, D, dtype=torch.float16, block_size=BS,
                                 shuffle_seed=77 + rank, device=dev, variant=args.variant,
-                                num_splits=args.splits, exchange=args.exchange)
+                                num_splits=args.splits, exchange=args.exchange,
+                                overlap=overlap)
     n_local = sp.hi - sp.lo
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     # fill in slabs to bound the temporary footprint
@@ -257,16 +281,15 @@ def run_ours(args) -> None:
     def step():
         sp.step(q, kn, vn, out)
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-
     stream = torch.cuda.current_stream(dev)
     sampler = ClockSampler(local) if rank == 0 else None
     if sampler:
-        sampler.start()
+        sampler.start()  # idles the GPU for 0.4 s: the warm-up and settle steps follow it
+    for _ in range(args.warmup):
+        step()
+    # the same fixed count on every rank (the exchange pairs the ranks' calls step by step)
+    for _ in range(args.settle):
+        step()
     # (1) the timed steps: one fused launch each (plus the all-gather and merge with
     # --exchange nccl), no other host work inside the loop
     t_start = torch.cuda.Event(enable_timing=True)
@@ -359,27 +382,32 @@ def run_ours(args) -> None:
         if world > 1 and not sp.owner:
             launch_bytes = 2 * HKV * n_local * D * ESIZE + 2 * HQ * D * ESIZE
         achieved = launch_bytes / (k_ms * 1e-3) / 1e9
+        traffic, traffic_note = None, "no ncu capture of this kernel source"
+        if args.traffic is not None:
+            traffic, traffic_note = args.traffic, "given on the command line"
+        elif (world == 1 and cached == CACHED and args.variant != 1
+              and NCU_TRAFFIC["decode_cu_sha256"] == decode_cu_sha256()):
+            traffic = NCU_TRAFFIC["bytes_per_launch"]
+            traffic_note = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of a "
+                            "32768-position launch, reads scaled to 131073 positions; "
+                            "captured on this decode.cu (sha256 "
+                            f"{NCU_TRAFFIC['decode_cu_sha256'][:12]})")
         line = {
             "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (seeded N(0,1) K/V, q; random block permutation)",
-            "config": {"workload": "cfg4 long-context decode attention op (Llama-3-8B "
-                                   "attention shape), 131072 cached + 1 appended, batch 1",
-                       "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "cached": CACHED,
-                       "block_size": BS,
-                       "parallelism": (f"seqsplit{world}-{args.exchange}" if world > 1
-                                       else "1gpu"),
-                       "l2": "inputs larger than L2 (537 MB K/V per step vs 126 MB L2)"},
+            "config": dict(CFG4_CONFIG),
+            "parallelism": (f"seqsplit{world}-{args.exchange}" if world > 1 else "1gpu"),
+            "settle_steps": args.settle,
+            "overlapped_launches": overlap,
             "hbm_gbs": algorithmic_bytes(cached=cached) / (ms_step * 1e-3) / 1e9,
             "gpu_launches": args.steps * (2 if world > 1 and args.exchange == "nccl" else 1),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
-                         "peak_source": peaks["source"],
-                         "traffic": (args.traffic if args.traffic is not None else
-                                     (NCU_TRAFFIC_PER_LAUNCH if world == 1 and cached == CACHED
-                                      and args.variant != 1 else None)),
+                         "peak_source": peaks["source"], "traffic": traffic,
+                         "traffic_source": traffic_note,
                          "kernel": ("decode_split_kernel<__half,128,4,64,3>" if args.variant == 1
                                     else "decode_mma_kernel<128,3>"),
                          "kernel_ms": k_ms, "kernel_ms_single_launch_events": k_ms_events,
@@ -402,12 +430,16 @@ def run_ours(args) -> None:
             kc[0, :, cached] = kn[0].cpu().numpy()
             vc[0, :, cached] = vn[0].cpu().numpy()
             threads = os.cpu_count() or 1
-            steps, secs = cpu_time(args.cpu_budget, 1000, threads,
-                                   (q[:, :, None].cpu().numpy(), kc, vc))
+            data = (q[:, :, None].cpu().numpy(), kc, vc)
+            steps, secs = cpu_time(args.cpu_budget, 1000, threads, data)
+            # the strict single-thread transcription: one full step
+            s1, secs1 = cpu_time(0.0, 1, 1, data)
             line["cpu_baseline"] = {
                 "value": steps / secs, "unit": "tok/s", "cores": threads, "kind": "port",
                 "sample": f"{steps} full config-4 steps on the host (faithful F16 chain of "
-                          f"the reference's kernels), time-boxed to {args.cpu_budget:.0f} s"}
+                          f"the reference's kernels), time-boxed to {args.cpu_budget:.0f} s",
+                "single_thread": {"value": s1 / secs1, "unit": "tok/s", "cores": 1,
+                                  "sample": "1 full config-4 step, one thread"}}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -467,7 +499,9 @@ def run_decoder(args) -> None:
             for layer in range(cfg.num_layers):
                 k = torch.randn((cfg.num_kv_heads, ctx[s], cfg.head_dim), generator=g,
                                 device=dev).half()
-                dec.cache.append(layer, i, k, k)
+                v = torch.randn((cfg.num_kv_heads, ctx[s], cfg.head_dim), generator=g,
+                                device=dev).half()
+                dec.cache.append(layer, i, k, v)
             dec.cache.advance(ctx[s], i)
         first = torch.randint(0, cfg.vocab_size, (B,), generator=gen).to(dev, torch.int32)
     else:
@@ -937,7 +971,12 @@ def main() -> None:
     ap.add_argument("--cached", type=int, default=CACHED,
                     help="cached positions (smaller values only for profiling captures)")
     ap.add_argument("--traffic", type=float, default=None,
-                    help="ncu DRAM bytes per launch of the decode kernel (from profiles/)")
+                    help="ncu DRAM bytes per launch of the decode kernel, if measured anew")
+    ap.add_argument("--settle", type=int, default=SETTLE_STEPS,
+                    help="untimed steps after the warm-up, before the timed region")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="config 4 on one GPU: launch consecutive steps without "
+                         "programmatic dependent launch")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

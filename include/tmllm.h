@@ -4,13 +4,15 @@
  * This is the drop-in boundary for Lee-Dongwook/RustLLM's per-layer KV-cache decode
  * path: the KV-cache append, concat_sequence, repeat_kv and the GQA attention chain
  * (QK^T -> scale/mask -> softmax -> PV).  A Rust `build.rs` links `libtmllm_b200.so`
- * and binds these functions with `extern "C"`; INTEGRATION.md shows the binding.
+ * and binds these functions with `extern "C"` (plain pointers, sizes and C structs; no
+ * C++ or CUDA types cross the boundary).
  *
  * Conventions
  *  - Every function returns an `int` status (tmllm_status).  0 is success.  Non-zero
  *    codes map one-to-one onto the reference's `TinyError` variants (src/error.rs:3-43)
  *    plus three codes the new runtime needs.  tmllm_last_error() returns a
- *    human-readable message for the calling thread's last failure.
+ *    human-readable message for the calling thread's last failure, and
+ *    tmllm_last_error_fields() the fields of the structured variants.
  *  - Arguments are validated on the host BEFORE anything is enqueued or mutated; a
  *    rejected call leaves every buffer and every cache length unchanged (the reference's
  *    rule, src/model/kv_cache.rs:18-53 and its test at :295-306).
@@ -65,6 +67,29 @@ int tmllm_version(void);
 const char* tmllm_status_name(int status);
 /* Message of the calling thread's most recent failure ("" if none). */
 const char* tmllm_last_error(void);
+
+/* Fields of the calling thread's most recent failure, for the reference's two structured
+ * error variants (src/error.rs:6-9, 19-23), so a binding rebuilds them exactly:
+ *   TMLLM_POSITION_OUT_OF_RANGE -> TinyError::PositionOutOfRange { start_pos, seq_len,
+ *     max_seq_len } (raised as in src/model/kv_cache.rs:46-50, src/ops/kv_cache_write.rs:106,
+ *     src/nn/rope.rs:122 for the RoPE table);
+ *   TMLLM_SHAPE_MISMATCH -> TinyError::ShapeMismatch { left, right } (the first left_rank /
+ *     right_rank entries of left / right).
+ * `status` is that failure's status (TMLLM_OK after a successful call: every entry point
+ * clears the record on entry); the other fields are zero unless the status uses them. */
+#define TMLLM_MAX_RANK 8
+typedef struct tmllm_error_fields {
+    int32_t status;
+    int32_t left_rank;
+    int32_t right_rank;
+    int32_t reserved;
+    int64_t start_pos;
+    int64_t seq_len;
+    int64_t max_seq_len;
+    int64_t left[TMLLM_MAX_RANK];
+    int64_t right[TMLLM_MAX_RANK];
+} tmllm_error_fields;
+int tmllm_last_error_fields(tmllm_error_fields* out);
 /* Blocks until all work on `stream` is done (MetalExecution::finish's wait,
  * src/metal/execution.rs:30-36). */
 int tmllm_sync(tmllm_stream stream);
@@ -251,7 +276,9 @@ typedef struct tmllm_decode_opts {
  * queued before it on the stream (programmatic dependent launch).  The lengths, block table
  * and cached K/V are read before that work has finished, so the caller promises it does not
  * write them; q, k_new and v_new are read, and anything is written, only after it has
- * finished.  Ignored by the other kernels and with the cross-GPU exchange. */
+ * finished.  Ignored by the CUDA-core kernels (always launched plainly), with the cross-GPU
+ * exchange, and by tmllm_cache_decode on a call that assigns a new block (the table update
+ * it queues must finish first). */
 #define TMLLM_DECODE_OVERLAP 1
 
 /* Bytes of scratch tmllm_gqa_decode needs for `num_splits` splits (0 = enough for any

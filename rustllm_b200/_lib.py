@@ -14,6 +14,8 @@ LIB_PATH = os.path.join(_HERE, "libtmllm_b200.so")
 
 F32 = 0
 F16 = 1
+DECODE_OVERLAP = 1  # TMLLM_DECODE_OVERLAP
+LINEAR_OVERLAP = 1  # TMLLM_LINEAR_OVERLAP
 
 vp = C.c_void_p
 i32 = C.c_int32
@@ -41,7 +43,14 @@ class InvalidShape(TinyError):
 
 
 class ShapeMismatch(TinyError):
+    """TinyError::ShapeMismatch { left, right } (src/error.rs:6-9): the two shapes."""
+
     status = 3
+
+    def __init__(self, message: str, status: int | None = None, *, left=None, right=None):
+        super().__init__(message, status)
+        self.left = [int(d) for d in left] if left is not None else []
+        self.right = [int(d) for d in right] if right is not None else []
 
 
 class InvalidDimension(TinyError):
@@ -57,7 +66,18 @@ class NonContiguousTensor(TinyError):
 
 
 class PositionOutOfRange(TinyError):
+    """TinyError::PositionOutOfRange { start_pos, seq_len, max_seq_len } (src/error.rs:19-23)."""
+
     status = 7
+
+    def __init__(self, message: str | None = None, status: int | None = None, *,
+                 start_pos: int = 0, seq_len: int = 0, max_seq_len: int = 0):
+        if message is None:  # the reference's Display text (src/error.rs:86-95)
+            message = (f"position range [{start_pos}, {start_pos + seq_len}) exceeds max "
+                       f"sequence length {max_seq_len}")
+        super().__init__(message, status)
+        self.start_pos, self.seq_len, self.max_seq_len = int(start_pos), int(seq_len), \
+            int(max_seq_len)
 
 
 class ModelFormat(TinyError):
@@ -123,10 +143,22 @@ class CacheConfig(C.Structure):
                 ("shuffle_seed", C.c_uint64)]
 
 
+MAX_RANK = 8
+
+
+class ErrorFields(C.Structure):
+    """``tmllm_error_fields``: the fields of the last failure's structured variant."""
+
+    _fields_ = [("status", i32), ("left_rank", i32), ("right_rank", i32), ("reserved", i32),
+                ("start_pos", i64), ("seq_len", i64), ("max_seq_len", i64),
+                ("left", i64 * MAX_RANK), ("right", i64 * MAX_RANK)]
+
+
 _PROTOS = {
     "tmllm_version": (C.c_int, []),
     "tmllm_status_name": (C.c_char_p, [C.c_int]),
     "tmllm_last_error": (C.c_char_p, []),
+    "tmllm_last_error_fields": (C.c_int, [C.POINTER(ErrorFields)]),
     "tmllm_sync": (C.c_int, [vp]),
     "tmllm_kv_cache_write": (C.c_int, [C.c_int, vp, vp, sz, sz, sz, sz, sz, vp]),
     "tmllm_concat_sequence": (C.c_int, [C.c_int, vp, vp, vp, sz, sz, sz, sz, sz, vp]),
@@ -208,15 +240,31 @@ def load():
     return _lib
 
 
+def last_error_fields() -> ErrorFields:
+    """The calling thread's ``tmllm_error_fields`` record."""
+    f = ErrorFields()
+    load().tmllm_last_error_fields(C.byref(f))
+    return f
+
+
 def check(rc: int) -> None:
-    """Raises the TinyError subclass for a non-zero status."""
+    """Raises the TinyError subclass for a non-zero status, with the fields of the
+    structured variants (PositionOutOfRange, ShapeMismatch) taken from the library."""
     if rc == 0:
         return
     lib = load()
     msg = lib.tmllm_last_error().decode(errors="replace")
     name = lib.tmllm_status_name(rc).decode()
     cls = _BY_STATUS.get(rc, TinyError)
-    raise cls(f"{name}: {msg}", rc)
+    text = f"{name}: {msg}"
+    f = last_error_fields()
+    if cls is PositionOutOfRange and f.status == rc:
+        raise PositionOutOfRange(text, rc, start_pos=f.start_pos, seq_len=f.seq_len,
+                                 max_seq_len=f.max_seq_len)
+    if cls is ShapeMismatch and f.status == rc:
+        raise ShapeMismatch(text, rc, left=list(f.left[: f.left_rank]),
+                            right=list(f.right[: f.right_rank]))
+    raise cls(text, rc)
 
 
 def call(name: str, *args) -> None:

@@ -127,7 +127,8 @@ def gqa_prefill(kv: PagedKV, q: torch.Tensor, k_new: torch.Tensor | None,
         ks = _row_stride(k_new, hkv, d, "k_new")
         if (_row_stride(v_new, hkv, d, "v_new") != ks or k_new.shape[0] != rows
                 or v_new.shape[0] != rows):
-            raise _lib.ShapeMismatch("k_new and v_new must have q's rows and the same row stride")
+            raise _lib.ShapeMismatch("k_new and v_new must have q's rows and the same row stride",
+                                     left=k_new.shape, right=v_new.shape)
     if out is None:
         out = torch.empty((rows, hq, d), dtype=out_dtype or q.dtype, device=q.device)
     if (out.dtype not in (q.dtype, torch.float32) or tuple(out.shape) != (rows, hq, d)
@@ -148,7 +149,8 @@ def gqa_prefill(kv: PagedKV, q: torch.Tensor, k_new: torch.Tensor | None,
         qp = q_start.data_ptr()
     else:
         if rows_per_seq * kv.num_seqs != rows:
-            raise _lib.ShapeMismatch(f"{rows} rows are not {kv.num_seqs} x {rows_per_seq}")
+            raise _lib.ShapeMismatch(f"{rows} rows are not {kv.num_seqs} x {rows_per_seq}",
+                                     left=[rows], right=[kv.num_seqs * rows_per_seq])
         qp = None
     call("tmllm_gqa_prefill", C.byref(kv), q.data_ptr(),
          k_new.data_ptr() if k_new is not None else None,

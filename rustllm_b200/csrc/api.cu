@@ -10,18 +10,58 @@ namespace tmllm {
 
 namespace {
 thread_local std::string g_last_error;
+thread_local tmllm_error_fields g_fields{};
+
+void set_message(const char* fmt, va_list ap) {
+    char buf[1024];
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    g_last_error = buf;
+}
+}  // namespace
+
+void clear_error() {
+    g_last_error.clear();
+    g_fields = tmllm_error_fields{};
 }
 
-void clear_error() { g_last_error.clear(); }
-
 int fail(int status, const char* fmt, ...) {
-    char buf[1024];
     va_list ap;
     va_start(ap, fmt);
-    vsnprintf(buf, sizeof(buf), fmt, ap);
+    set_message(fmt, ap);
     va_end(ap);
-    g_last_error = buf;
+    g_fields = tmllm_error_fields{};
+    g_fields.status = status;
     return status;
+}
+
+int fail_position(int64_t start_pos, int64_t seq_len, int64_t max_seq_len) {
+    g_fields = tmllm_error_fields{};
+    g_fields.status = TMLLM_POSITION_OUT_OF_RANGE;
+    g_fields.start_pos = start_pos;
+    g_fields.seq_len = seq_len;
+    g_fields.max_seq_len = max_seq_len;
+    // the reference's Display text (src/error.rs:86-95)
+    char buf[160];
+    snprintf(buf, sizeof(buf), "position range [%lld, %lld) exceeds max sequence length %lld",
+             static_cast<long long>(start_pos), static_cast<long long>(start_pos + seq_len),
+             static_cast<long long>(max_seq_len));
+    g_last_error = buf;
+    return TMLLM_POSITION_OUT_OF_RANGE;
+}
+
+int fail_shapes(std::initializer_list<int64_t> left, std::initializer_list<int64_t> right,
+                const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    set_message(fmt, ap);
+    va_end(ap);
+    g_fields = tmllm_error_fields{};
+    g_fields.status = TMLLM_SHAPE_MISMATCH;
+    for (int64_t d : left)
+        if (g_fields.left_rank < TMLLM_MAX_RANK) g_fields.left[g_fields.left_rank++] = d;
+    for (int64_t d : right)
+        if (g_fields.right_rank < TMLLM_MAX_RANK) g_fields.right[g_fields.right_rank++] = d;
+    return TMLLM_SHAPE_MISMATCH;
 }
 
 int cuda_fail(cudaError_t err, const char* what) {
@@ -82,7 +122,14 @@ const char* tmllm_status_name(int status) {
 
 const char* tmllm_last_error(void) { return tmllm::g_last_error.c_str(); }
 
+int tmllm_last_error_fields(tmllm_error_fields* out) {
+    if (!out) return TMLLM_INVALID_ARGUMENT;  // leaves the recorded failure untouched
+    *out = tmllm::g_fields;
+    return TMLLM_OK;
+}
+
 int tmllm_sync(tmllm_stream stream) {
+    tmllm::clear_error();
     TMLLM_CUDA_TRY(cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)));
     return TMLLM_OK;
 }

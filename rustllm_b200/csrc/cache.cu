@@ -193,10 +193,7 @@ int validate_extend(const tmllm_cache* c, int32_t seq, int64_t n) {
                            static_cast<long long>(n));
     const int64_t len = c->h_lens[seq];
     if (n > c->cfg.max_seq_len - len)  // kv_cache.rs:40-51
-        return fail(TMLLM_POSITION_OUT_OF_RANGE,
-                    "position range [%lld, %lld) exceeds max sequence length %d",
-                    static_cast<long long>(len), static_cast<long long>(len + n),
-                    c->cfg.max_seq_len);
+        return fail_position(len, n, c->cfg.max_seq_len);
     if (blocks_needed(c, seq, len + n) > static_cast<int64_t>(c->free_ids.size()))
         return fail(TMLLM_OUT_OF_BLOCKS, "KV block pool exhausted (%zu free, %lld needed)",
                     c->free_ids.size(), static_cast<long long>(blocks_needed(c, seq, len + n)));
@@ -403,10 +400,7 @@ int tmllm_cache_advance(tmllm_cache* cache, int32_t seq, int64_t n, tmllm_stream
     const int first = seq < 0 ? 0 : seq, last = seq < 0 ? cache->cfg.num_seqs : seq + 1;
     for (int i = first; i < last; ++i) {
         if (n < 0 || n > cache->cfg.max_seq_len - cache->h_lens[i])
-            return fail(TMLLM_POSITION_OUT_OF_RANGE,
-                        "position range [%lld, %lld) exceeds max sequence length %d",
-                        static_cast<long long>(cache->h_lens[i]),
-                        static_cast<long long>(cache->h_lens[i] + n), cache->cfg.max_seq_len);
+            return fail_position(cache->h_lens[i], n, cache->cfg.max_seq_len);
         if (blocks_needed(cache, i, cache->h_lens[i] + n) > 0)
             return fail(TMLLM_NOT_RESERVED, "sequence %d has no block for position %lld", i,
                         static_cast<long long>(cache->h_lens[i] + n - 1));
@@ -481,10 +475,7 @@ int tmllm_cache_decode(tmllm_cache* cache, int32_t layer, const void* q, const v
     for (int i = 0; i < cache->cfg.num_seqs; ++i) {
         const int64_t len = cache->h_lens[i];
         if (append && len >= cache->cfg.max_seq_len)
-            return fail(TMLLM_POSITION_OUT_OF_RANGE,
-                        "position range [%lld, %lld) exceeds max sequence length %d",
-                        static_cast<long long>(len), static_cast<long long>(len + 1),
-                        cache->cfg.max_seq_len);
+            return fail_position(len, 1, cache->cfg.max_seq_len);
         if (append) need_total += blocks_needed(cache, i, len + 1);
         max_len = std::max<int64_t>(max_len, len + (append ? 1 : 0));
     }
@@ -500,9 +491,7 @@ int tmllm_cache_decode(tmllm_cache* cache, int32_t layer, const void* q, const v
         for (int i = 0; i < cache->cfg.num_seqs; ++i) {
             const int64_t pos = cache->h_lens[i] + o.rope_pos_offset;
             if (pos < 0 || pos >= o.rope_len)
-                return fail(TMLLM_POSITION_OUT_OF_RANGE,
-                            "RoPE position %lld outside the %d-entry table",
-                            static_cast<long long>(pos), o.rope_len);
+                return fail_position(pos, 1, o.rope_len);  // rope.rs:121-127
         }
     }
     int32_t splits = o.num_splits;
@@ -537,6 +526,10 @@ int tmllm_cache_decode(tmllm_cache* cache, int32_t layer, const void* q, const v
     if (append)
         for (int i = 0; i < cache->cfg.num_seqs; ++i)
             if (int st = assign_blocks(cache, i, cache->h_lens[i] + 1, s)) return st;
+    // A block assigned just now reaches the device table through a kernel queued right
+    // ahead of the decode, which an overlapped launch would read before that kernel ends:
+    // such a call launches plainly.
+    if (need_total > 0) o.flags &= ~TMLLM_DECODE_OVERLAP;
     // a caller that knows lengths will grow (a captured graph replayed for several steps)
     // may ask for splits sized for the longest length it will see
     const int64_t hint = std::max<int64_t>(max_len, o.max_len_hint);
@@ -563,10 +556,7 @@ int tmllm_cache_prefill(tmllm_cache* cache, int32_t layer, const void* q, const 
     for (int i = 0; i < cache->cfg.num_seqs; ++i) {
         const int64_t len = cache->h_lens[i];
         if (n > cache->cfg.max_seq_len - len)  // kv_cache.rs:40-51
-            return fail(TMLLM_POSITION_OUT_OF_RANGE,
-                        "position range [%lld, %lld) exceeds max sequence length %d",
-                        static_cast<long long>(len), static_cast<long long>(len + n),
-                        cache->cfg.max_seq_len);
+            return fail_position(len, n, cache->cfg.max_seq_len);
         need_total += blocks_needed(cache, i, len + n);
     }
     if (need_total > static_cast<int64_t>(cache->free_ids.size()))
@@ -577,9 +567,7 @@ int tmllm_cache_prefill(tmllm_cache* cache, int32_t layer, const void* q, const 
         for (int i = 0; i < cache->cfg.num_seqs; ++i) {
             const int64_t lo = cache->h_lens[i] + o.rope_pos_offset, hi = lo + n - 1;
             if (lo < 0 || hi >= o.rope_len)
-                return fail(TMLLM_POSITION_OUT_OF_RANGE,
-                            "RoPE positions [%lld, %lld] outside the %d-entry table",
-                            static_cast<long long>(lo), static_cast<long long>(hi), o.rope_len);
+                return fail_position(lo, n, o.rope_len);  // rope.rs:121-127
         }
     }
     DeviceGuard guard(cache->cfg.device);

@@ -8,6 +8,7 @@
 #include <cstdarg>
 #include <cstddef>
 #include <cstdint>
+#include <initializer_list>
 
 #include "tmllm.h"
 
@@ -17,8 +18,15 @@ namespace tmllm {
 int fail(int status, const char* fmt, ...);
 // Records a CUDA runtime error and returns TMLLM_DEVICE_ERROR.
 int cuda_fail(cudaError_t err, const char* what);
-// Clears the calling thread's last error.
+// Clears the calling thread's last error (message and fields).
 void clear_error();
+// TinyError::PositionOutOfRange {start_pos, seq_len, max_seq_len}: records the fields and
+// the reference's message, returns TMLLM_POSITION_OUT_OF_RANGE.
+int fail_position(int64_t start_pos, int64_t seq_len, int64_t max_seq_len);
+// TinyError::ShapeMismatch {left, right}: records both shapes (up to TMLLM_MAX_RANK dims
+// each) and a message, returns TMLLM_SHAPE_MISMATCH.
+int fail_shapes(std::initializer_list<int64_t> left, std::initializer_list<int64_t> right,
+                const char* fmt, ...);
 
 inline bool valid_dtype(int dt) { return dt == TMLLM_F32 || dt == TMLLM_F16; }
 inline size_t dtype_size(int dt) { return dt == TMLLM_F16 ? 2u : 4u; }

@@ -54,6 +54,7 @@ struct DecodeArgs {
     int64_t q_stride;        // elements between sequences in q
     int64_t kv_stride;       // elements between sequences in k_new / v_new
     int32_t overlap;         // launched with programmatic stream serialisation
+    int32_t clear_tickets;   // host side: zero the split tickets on the stream before launch
 };
 
 // Physical slot of 16-byte chunk `c` of tile row `r` (XOR swizzle inside groups of 8).
@@ -63,8 +64,11 @@ __device__ __forceinline__ int swz(int r, int c) {
     return c ^ (r & M);
 }
 
-__device__ __forceinline__ int64_t block_of(const DecodeArgs& a, int b, int pos) {
-    int idx = a.bs_shift >= 0 ? (pos >> a.bs_shift) : (pos / a.block_size);
+// Arena block of position `pos` of sequence b, or -1 when the position is outside the
+// table (negative, or past max_blocks entries) or its entry names no block.
+__device__ __forceinline__ int64_t block_of(const DecodeArgs& a, int b, int64_t pos) {
+    if (pos < 0) return -1;
+    const int64_t idx = a.bs_shift >= 0 ? (pos >> a.bs_shift) : (pos / a.block_size);
     if (idx >= a.max_blocks) return -1;
     int64_t blk = __ldg(&a.block_table[static_cast<int64_t>(b) * a.max_blocks + idx]);
     return (blk >= 0 && blk < a.num_blocks) ? blk : -1;
@@ -666,8 +670,9 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? 4 : 2) decode_mma_ke
     // on a table read; the first two batches depend on the chunk only and are read
     // together with the length.  At D = 128 the entry is read at issue (measured 1.5 %
     // faster there: fewer registers on the critical loop).
-    auto entry = [&](int j) -> int64_t {
-        return whole_blocks ? block_of(a, b, t0 + (warp + 4 * j) * 16) : -1;
+    auto entry = [&](int j) -> int64_t {  // j may run past the chunk: 64-bit position
+        return whole_blocks ? block_of(a, b, static_cast<int64_t>(t0) + (warp + 4 * j) * 16)
+                            : -1;
     };
     constexpr bool kLaneTable = D == 64;
     int64_t cur = -1, nxt = -1;
@@ -1335,6 +1340,16 @@ __global__ void merge_lse_kernel(const float* __restrict__ po, const float* __re
 
 // ---- launch plumbing -------------------------------------------------------------------
 
+// When asked (the allocation-free entry point, whose scratch keeps the previous call's
+// contents), zero the split tickets on the stream right before the launch -- after every
+// argument check, so a refused call enqueues nothing.  Tickets exist only with splits.
+int clear_split_tickets(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
+    if (a.clear_tickets && grid.z > 1 && a.counters)
+        TMLLM_CUDA_TRY(cudaMemsetAsync(a.counters, 0,
+                                       static_cast<size_t>(grid.x) * grid.y * sizeof(int32_t), s));
+    return TMLLM_OK;
+}
+
 struct WorkspaceLayout {
     size_t counters, part_ml, part_o, total;
 };
@@ -1362,7 +1377,27 @@ int launch_tiled(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
         return fail(TMLLM_INVALID_ARGUMENT, "too many splits (%u) for the merge scratch", grid.z);
     TMLLM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(bytes)));
+    if (int st = clear_split_tickets(a, grid, s)) return st;
+    // Always a plain launch: this kernel reads q / k_new / v_new without a grid-dependency
+    // wait, so it must not start before the kernel ahead of it has finished.
+    fn<<<grid, kDecodeThreads, bytes, s>>>(a);
+    TMLLM_LAUNCH_TRY();
+    return TMLLM_OK;
+}
+
+template <int D, int STAGES, bool PT = false>
+int launch_mma(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
+    using Cfg = MmaCfg<D, STAGES>;
+    auto* fn = decode_mma_kernel<D, STAGES, PT>;
+    const size_t bytes = static_cast<size_t>(Cfg::BYTES);
+    if ((2 * static_cast<size_t>(grid.z) + 2) * 16 * 4 > static_cast<size_t>(Cfg::OFF_FIN))
+        return fail(TMLLM_INVALID_ARGUMENT, "too many splits (%u) for the merge scratch", grid.z);
+    TMLLM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(bytes)));
+    if (int st = clear_split_tickets(a, grid, s)) return st;
     if (a.overlap) {
+        // programmatic stream serialisation: the kernel may start while the one ahead of it
+        // is still running; it reads q / k_new / v_new only after griddepcontrol.wait
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = grid;
         cfg.blockDim = dim3(kDecodeThreads);
@@ -1377,20 +1412,6 @@ int launch_tiled(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
     } else {
         fn<<<grid, kDecodeThreads, bytes, s>>>(a);
     }
-    TMLLM_LAUNCH_TRY();
-    return TMLLM_OK;
-}
-
-template <int D, int STAGES, bool PT = false>
-int launch_mma(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
-    using Cfg = MmaCfg<D, STAGES>;
-    auto* fn = decode_mma_kernel<D, STAGES, PT>;
-    const size_t bytes = static_cast<size_t>(Cfg::BYTES);
-    if ((2 * static_cast<size_t>(grid.z) + 2) * 16 * 4 > static_cast<size_t>(Cfg::OFF_FIN))
-        return fail(TMLLM_INVALID_ARGUMENT, "too many splits (%u) for the merge scratch", grid.z);
-    TMLLM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(bytes)));
-    fn<<<grid, kDecodeThreads, bytes, s>>>(a);
     TMLLM_LAUNCH_TRY();
     return TMLLM_OK;
 }
@@ -1457,23 +1478,25 @@ int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
                    const void* v_new, void* out, float* lse, int32_t q_heads,
                    const tmllm_decode_opts* opts, void* workspace, size_t workspace_bytes,
                    int64_t max_len_hint, const ExchangeArgs* ex, uint32_t epoch,
-                   cudaStream_t stream);
+                   bool clear_tickets, cudaStream_t stream);
 
 int decode_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, const void* v_new,
                 void* out, float* lse, int32_t q_heads, const tmllm_decode_opts* opts,
                 void* workspace, size_t workspace_bytes, int64_t max_len_hint,
                 cudaStream_t stream) {
     return decode_impl_ex(kv, q, k_new, v_new, out, lse, q_heads, opts, workspace,
-                          workspace_bytes, max_len_hint, nullptr, 0, stream);
+                          workspace_bytes, max_len_hint, nullptr, 0, false, stream);
 }
 
 // `ex` (device-resident) makes the launch finish a sequence split across GPUs: the final
-// rows are exchanged with every rank and merged (tensor-core kernel only).
+// rows are exchanged with every rank and merged (tensor-core kernel only).  With
+// `clear_tickets` the split tickets in the workspace are zeroed on `stream` right before
+// the launch (only when the call passed every check and uses splits).
 int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
                    const void* v_new, void* out, float* lse, int32_t q_heads,
                    const tmllm_decode_opts* opts, void* workspace, size_t workspace_bytes,
                    int64_t max_len_hint, const ExchangeArgs* ex, uint32_t epoch,
-                   cudaStream_t stream) {
+                   bool clear_tickets, cudaStream_t stream) {
     if (!kv) return fail(TMLLM_INVALID_ARGUMENT, "null paged KV descriptor");
     if (!valid_dtype(kv->dtype)) return fail(TMLLM_UNSUPPORTED_DTYPE, "unknown cache dtype");
     const int D = kv->head_dim, Hkv = kv->num_kv_heads, B = kv->num_seqs;
@@ -1482,6 +1505,8 @@ int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
         return fail(TMLLM_INVALID_SHAPE, "paged KV dimensions must be positive");
     if (D % 2 != 0 || D > 512)
         return fail(TMLLM_INVALID_SHAPE, "head_dim must be even and <= 512, got %d", D);
+    if (B > 65535)  // the sequences are the grid's y dimension
+        return fail(TMLLM_INVALID_SHAPE, "at most 65535 sequences per decode call, got %d", B);
     if (q_heads <= 0 || q_heads % Hkv != 0)
         return fail(TMLLM_MODEL_FORMAT, "Q heads %d must be divisible by non-zero KV heads %d",
                     q_heads, Hkv);
@@ -1563,6 +1588,7 @@ int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
     a.kv_stride = o.kv_seq_stride > 0 ? o.kv_seq_stride : static_cast<int64_t>(Hkv) * D;
     // the overlapped launch is for the single-GPU tensor-core kernel (not the exchange)
     a.overlap = (o.flags & TMLLM_DECODE_OVERLAP) && !ex ? 1 : 0;
+    a.clear_tickets = clear_tickets ? 1 : 0;
     if (ex && !(mma_shape && o.variant != 1))
         return fail(TMLLM_INVALID_ARGUMENT,
                     "the cross-GPU exchange needs the tensor-core decode (F16, head_dim 64/128)");

@@ -13,7 +13,7 @@ int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
                    const void* v_new, void* out, float* lse, int32_t q_heads,
                    const tmllm_decode_opts* opts, void* workspace, size_t workspace_bytes,
                    int64_t max_len_hint, const ExchangeArgs* ex, uint32_t epoch,
-                   cudaStream_t stream);
+                   bool clear_tickets, cudaStream_t stream);
 }
 
 using namespace tmllm;
@@ -201,15 +201,18 @@ int tmllm_gqa_decode_exchange(const tmllm_paged_kv* kv, const void* q, const voi
     if (static_cast<int64_t>(kv->num_seqs) * q_heads != ex->rows ||
         static_cast<int64_t>(kv->num_seqs) * kv->num_kv_heads != ex->groups ||
         kv->head_dim != ex->head_dim)
-        return fail(TMLLM_SHAPE_MISMATCH,
-                    "exchange sized for %d rows / %d groups / head_dim %d, call has %d x %d / %d x %d"
-                    " / %d",
-                    ex->rows, ex->groups, ex->head_dim, kv->num_seqs, q_heads, kv->num_seqs,
-                    kv->num_kv_heads, kv->head_dim);
+        return fail_shapes({ex->rows, ex->groups, ex->head_dim},
+                           {static_cast<int64_t>(kv->num_seqs) * q_heads,
+                            static_cast<int64_t>(kv->num_seqs) * kv->num_kv_heads,
+                            kv->head_dim},
+                           "exchange sized for %d rows / %d groups / head_dim %d, call has "
+                           "%d x %d / %d x %d / %d",
+                           ex->rows, ex->groups, ex->head_dim, kv->num_seqs, q_heads,
+                           kv->num_seqs, kv->num_kv_heads, kv->head_dim);
     const uint32_t epoch = ex->epoch + 1;
     int st = decode_impl_ex(kv, q, k_new, v_new, out, lse, q_heads, opts, workspace,
                             workspace_bytes, opts ? opts->max_len_hint : 0, ex->dev_args, epoch,
-                            reinterpret_cast<cudaStream_t>(stream));
+                            false, reinterpret_cast<cudaStream_t>(stream));
     if (st == TMLLM_OK) ex->epoch = epoch;
     return st;
 }

@@ -15,8 +15,9 @@
 //    address with cudaGetSymbolAddress and remembers it; make that first call before any
 //    stream capture.
 //  * Every call uses the same array and it keeps whatever the previous call left there.
-//    The ticket counters the kernel needs at zero are cleared (cudaMemsetAsync, no
-//    allocation) on the caller's stream before each launch.  Two calls whose work overlaps
+//    When the call uses split-K, the ticket counters the kernel needs at zero are cleared
+//    (cudaMemsetAsync, no allocation) on the caller's stream right before the launch, after
+//    every argument check: a rejected call enqueues nothing.  Two calls whose work overlaps
 //    on the GPU (different streams, or different host threads on the same device) race on
 //    the array and produce wrong results; serialise them.
 //  * A call whose split-K partials would not fit in the array is rejected before anything
@@ -26,10 +27,11 @@
 #include "common.cuh"
 
 namespace tmllm {
-int decode_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, const void* v_new,
-                void* out, float* lse, int32_t q_heads, const tmllm_decode_opts* opts,
-                void* workspace, size_t workspace_bytes, int64_t max_len_hint,
-                cudaStream_t stream);
+int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
+                   const void* v_new, void* out, float* lse, int32_t q_heads,
+                   const tmllm_decode_opts* opts, void* workspace, size_t workspace_bytes,
+                   int64_t max_len_hint, const ExchangeArgs* ex, uint32_t epoch,
+                   bool clear_tickets, cudaStream_t stream);
 size_t decode_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t splits);
 int32_t decode_auto_splits(int64_t B, int64_t Hkv, int64_t max_len);
 }  // namespace tmllm
@@ -90,10 +92,10 @@ extern "C" int tmllm_gqa_decode_noalloc(const tmllm_paged_kv* kv, const void* q,
                     TMLLM_NOALLOC_SCRATCH_BYTES);
     void* scratch = nullptr;
     if (int st = scratch_address(&scratch)) return st;
-    auto s = reinterpret_cast<cudaStream_t>(stream);
-    // The ticket counters sit at the start of the scratch and must be zero at launch.
-    const size_t counter_bytes = static_cast<size_t>(kv->num_seqs) * kv->num_kv_heads * 4;
-    TMLLM_CUDA_TRY(cudaMemsetAsync(scratch, 0, counter_bytes, s));
-    return decode_impl(kv, q, k_new, v_new, out, lse, q_heads, &o, scratch,
-                       static_cast<size_t>(TMLLM_NOALLOC_SCRATCH_BYTES), o.max_len_hint, s);
+    // The ticket counters sit at the start of the scratch and must be zero at launch: the
+    // decode clears them itself once every argument has been checked (never with a single
+    // split, where no ticket is taken and `need` covers no counters).
+    return decode_impl_ex(kv, q, k_new, v_new, out, lse, q_heads, &o, scratch,
+                          static_cast<size_t>(TMLLM_NOALLOC_SCRATCH_BYTES), o.max_len_hint,
+                          nullptr, 0, true, reinterpret_cast<cudaStream_t>(stream));
 }

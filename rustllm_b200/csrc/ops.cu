@@ -262,9 +262,8 @@ int tmllm_kv_cache_write(tmllm_dtype dtype, void* cache, const void* source, siz
     if (num_heads == 0 || max_seq == 0 || head_dim == 0)
         return fail(TMLLM_INVALID_SHAPE, "invalid KV cache write shape");
     if (start > max_seq || source_seq > max_seq - start)
-        return fail(TMLLM_POSITION_OUT_OF_RANGE,
-                    "position range [%zu, %zu) exceeds max sequence length %zu", start,
-                    start + source_seq, max_seq);
+        return fail_position(static_cast<int64_t>(start), static_cast<int64_t>(source_seq),
+                             static_cast<int64_t>(max_seq));
     int64_t numel;
     if (!checked_numel({num_heads, max_seq, head_dim, dtype_size(dtype)}, &numel) ||
         numel / static_cast<int64_t>(dtype_size(dtype)) > UINT32_MAX)

@@ -401,7 +401,8 @@ class Decoder:
         self.check_ids(prompts)
         B, S = prompts.shape
         if B != self.B:
-            raise _lib.ShapeMismatch(f"prefill expects {self.B} prompts, got {B}")
+            raise _lib.ShapeMismatch(f"prefill expects {self.B} prompts, got {B}",
+                                     left=[self.B, S], right=list(prompts.shape))
         cfg, w = self.cfg, self.w
         T = B * S
         h, d = cfg.hidden_size, cfg.head_dim
@@ -491,45 +492,11 @@ class GraphedDecoder:
 
     def step(self) -> None:
         if self.steps_left <= 0:
-            raise _lib.PositionOutOfRange("graph was captured for fewer steps")
+            pos = self.dec.cache.lens()[0]
+            raise _lib.PositionOutOfRange(
+                f"graph was captured for fewer steps: position range [{pos}, {pos + 1}) "
+                f"is past the captured steps", start_pos=pos, seq_len=1, max_seq_len=pos)
         self.graph.replay()
         self.dec.cache.advance(1)
         self.steps_left -= 1
 
-
-def reference_forward(cfg: ModelConfig, w: DecoderWeights, tokens: torch.Tensor) -> torch.Tensor:
-    """Float32 restatement of the whole model on one sequence (tokens [S]) with full causal
-    attention, used as the test reference: logits [S, vocab]."""
-    f = torch.float32
-    x = w.embedding[tokens.long()].to(f)
-    S = x.shape[0]
-    hq, hkv, d = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
-    pos = torch.arange(S, device=x.device, dtype=f)
-    inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, d, 2, device=x.device, dtype=f) / d))
-    ang = pos[:, None] * inv[None, :]
-    cos, sin = torch.cos(ang), torch.sin(ang)
-
-    def rope(t):  # t [S, H, d], half-split pairs (kernels/rope.metal:57-63)
-        a, b = t[..., : d // 2], t[..., d // 2:]
-        return torch.cat([a * cos[:, None] - b * sin[:, None], b * cos[:, None] + a * sin[:, None]], -1)
-
-    def norm(t, wt):
-        return t * torch.rsqrt((t * t).mean(-1, keepdim=True) + cfg.rms_norm_eps) * wt.to(f)
-
-    mask = torch.full((S, S), float("-inf"), device=x.device).triu(1)
-    for L in w.layers:
-        hn = norm(x, L["attn_norm"])
-        qkv = hn @ L["wqkv"].to(f)
-        q = rope(qkv[:, : hq * d].view(S, hq, d))
-        k = rope(qkv[:, hq * d:(hq + hkv) * d].view(S, hkv, d))
-        v = qkv[:, (hq + hkv) * d:].view(S, hkv, d)
-        k = k.repeat_interleave(hq // hkv, dim=1)
-        v = v.repeat_interleave(hq // hkv, dim=1)
-        att = torch.einsum("shd,thd->hst", q, k) / math.sqrt(d) + mask
-        o = torch.einsum("hst,thd->shd", att.softmax(-1), v).reshape(S, hq * d)
-        x = x + o @ L["wo"].to(f)
-        hn = norm(x, L["mlp_norm"])
-        gu = hn @ L["wgu"].to(f)
-        g_, u_ = gu[:, : cfg.intermediate_size], gu[:, cfg.intermediate_size:]
-        x = x + (g_ * torch.sigmoid(g_) * u_) @ L["wd"].to(f)
-    return norm(x, w.final_norm) @ w.lm_head.to(f)

@@ -3,8 +3,8 @@
 * ``SequenceSplitAttention`` — one long sequence split along its positions (BASELINE
   config 4).  Rank r holds positions [r*L/N, (r+1)*L/N) in its own paged cache; the last
   rank holds the tail and appends.  Every rank attends its range for all query heads and
-  publishes (O_r F32, lse_r) packed in one buffer; one all-gather exchanges them and each
-  rank merges by log-sum-exp (``tmllm_merge_lse``).
+  the partial (O_r, lse_r) are merged by log-sum-exp on every rank (see below for the two
+  exchanges).
 * ``shard_sequences`` — batch sharding (config 3): sequence s goes to rank s mod N; the
   ranks never exchange data.
 
@@ -115,7 +115,7 @@ class SequenceSplitAttention:
     def __init__(self, total_cached: int, q_heads: int, kv_heads: int, head_dim: int, *,
                  dtype=torch.float16, block_size: int = 16, max_new: int = 256,
                  shuffle_seed: int = 0, device=None, group=None, variant: int = 0,
-                 num_splits: int = 0, exchange: str = "p2p"):
+                 num_splits: int = 0, exchange: str = "p2p", overlap: bool = False):
         self.group = group
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -132,6 +132,9 @@ class SequenceSplitAttention:
         self.recv = torch.zeros((self.world, width), dtype=torch.float32, device=self.device)
         self.global_len = total_cached
         self.kw = {"variant": variant, "num_splits": num_splits}
+        # one GPU: consecutive steps may overlap (TMLLM_DECODE_OVERLAP); the caller promises
+        # that nothing between two steps writes this rank's cache
+        self.overlap = overlap
         if exchange not in ("p2p", "nccl"):
             raise ValueError(f"unknown exchange {exchange!r}")
         self.exchange = exchange if self.world > 1 else "none"
@@ -217,7 +220,7 @@ class SequenceSplitAttention:
         if self.world == 1:
             off = self.global_len - self.cache.len(0)
             self.cache.decode(0, q, k_new, v_new, out=out, rope=rope, rope_pos_offset=off,
-                              **self.kw)
+                              overlap=self.overlap, **self.kw)
             return out
         self.attend_local(q, k_new, v_new, rope)
         return self.exchange_and_merge(out)

@@ -154,13 +154,15 @@ class PagedKvCache:
                v_new: torch.Tensor | None, *, out: torch.Tensor | None = None,
                out_dtype: torch.dtype | None = None, lse: torch.Tensor | None = None,
                want_lse: bool = False, scale: float = 0.0, num_splits: int = 0, rope=None,
-               rope_pos_offset: int = 0, variant: int = 0):
+               rope_pos_offset: int = 0, variant: int = 0, overlap: bool = False):
         """Fused append + GQA decode attention for every sequence (one query token each).
 
         q [num_seqs, Hq, D]; k_new, v_new [num_seqs, Hkv, D] or None (attend only).
         Returns out [num_seqs, Hq, D] (and lse [num_seqs, Hq] F32 when ``want_lse`` or
         ``lse`` is given).  Lengths are not advanced; call ``advance()`` once per step
-        after the last layer."""
+        after the last layer.  ``overlap`` (TMLLM_DECODE_OVERLAP) lets the tensor-core
+        kernel start while the kernel ahead of it drains: the caller promises that kernel
+        writes neither the lengths, the block table nor the cached K/V."""
         on_device(self.device, q, k_new, v_new, out, lse, rope)
         if q.dtype != self.dtype:
             raise _lib.UnsupportedDType(
@@ -185,7 +187,8 @@ class PagedKvCache:
         if lse is None and want_lse:
             lse = torch.empty((self.num_seqs, hq), dtype=torch.float32, device=self.device)
         opts = DecodeOpts(scale=scale, num_splits=num_splits, out_f32=int(out.dtype == torch.float32),
-                          rope_pos_offset=rope_pos_offset, variant=variant)
+                          rope_pos_offset=rope_pos_offset, variant=variant,
+                          flags=_lib.DECODE_OVERLAP if overlap else 0)
         if rope is not None:
             cos, sin = rope
             opts.rope_cos, opts.rope_sin, opts.rope_len = cos.data_ptr(), sin.data_ptr(), cos.shape[0]
@@ -305,9 +308,8 @@ class LayerKvCache:
                 f"{self.num_kv_heads} KV heads, input has {key.shape[1] if key.dim() > 1 else '?'} heads")
         seq = key.shape[2]
         if self.len() + seq > self.max_seq_len:
-            raise _lib.PositionOutOfRange(
-                f"position range [{self.len()}, {self.len() + seq}) exceeds max sequence "
-                f"length {self.max_seq_len}")
+            raise _lib.PositionOutOfRange(start_pos=self.len(), seq_len=seq,
+                                          max_seq_len=self.max_seq_len)
         self._store.append(0, 0, key, value)
         self._store.advance(seq, 0)
 

@@ -115,14 +115,15 @@ def _kv_view(k: torch.Tensor, kv_len: int | None):
 def gqa_qk_matmul(q: torch.Tensor, k: torch.Tensor, kv_len: int | None = None) -> torch.Tensor:
     """Tensor::gqa_qk_matmul (src/tensor/gqa_matmul.rs:16-62): Q [B,Hq,S,D] x K^T, K read
     as [B,Hkv,cap,D] for its first kv_len rows (a cache's narrow view)."""
-    _on_cuda(q, k)
     _same_dtype("GQA QK", q, k)
     if q.dim() != 4 or k.dim() != 4:
         raise _lib.ModelFormat(f"GQA QK expects Q [B,QH,Q,D] and K [B,KVH,K,D], got "
                                f"{list(q.shape)} and {list(k.shape)}")
     b, hq, s, d = q.shape
-    if k.shape[0] != b or k.shape[3] != d:
-        raise _lib.ShapeMismatch(f"{list(q.shape)} vs {list(k.shape)}")
+    if k.shape[0] != b or k.shape[3] != d:  # gqa_matmul.rs:111-116
+        raise _lib.ShapeMismatch(f"shape mismatch: left={list(q.shape)}, right={list(k.shape)}",
+                                 left=q.shape, right=k.shape)
+    _on_cuda(q, k)
     cap, kv_len = _kv_view(k, kv_len)
     q, k = q.contiguous(), k.contiguous()
     out = torch.empty((b, hq, s, kv_len), dtype=q.dtype, device=q.device)
@@ -134,14 +135,16 @@ def gqa_qk_matmul(q: torch.Tensor, k: torch.Tensor, kv_len: int | None = None) -
 def gqa_pv_matmul(probs: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
     """Tensor::gqa_pv_matmul (src/tensor/gqa_matmul.rs:65-105): P [B,Hq,S,L] x V, V read
     as [B,Hkv,cap,D] for its first L rows."""
-    _on_cuda(probs, v)
     _same_dtype("GQA PV", probs, v)
     if probs.dim() != 4 or v.dim() != 4:
         raise _lib.ModelFormat(f"GQA PV expects P [B,QH,Q,K] and V [B,KVH,K,D], got "
                                f"{list(probs.shape)} and {list(v.shape)}")
     b, hq, s, kv_len = probs.shape
-    if v.shape[0] != b or v.shape[2] < kv_len:
-        raise _lib.ShapeMismatch(f"{list(probs.shape)} vs {list(v.shape)}")
+    if v.shape[0] != b or v.shape[2] < kv_len:  # gqa_matmul.rs:130-135
+        raise _lib.ShapeMismatch(
+            f"shape mismatch: left={list(probs.shape)}, right={list(v.shape)}",
+            left=probs.shape, right=v.shape)
+    _on_cuda(probs, v)
     probs, v = probs.contiguous(), v.contiguous()
     d = v.shape[3]
     out = torch.empty((b, hq, s, d), dtype=probs.dtype, device=probs.device)
@@ -178,15 +181,16 @@ def softmax_last_dim(x: torch.Tensor) -> torch.Tensor:
 
 def batched_matmul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     """Tensor::batched_matmul (src/tensor/tensor.rs:497-602)."""
-    _on_cuda(a, b)
     _same_dtype("batched matmul", a, b)
     if a.dim() < 3:
         raise _lib.InvalidDimension(f"batched matmul requires rank >= 3, left rank is {a.dim()}")
     if b.dim() != a.dim():
         raise _lib.InvalidDimension(
             f"batched matmul requires tensors with equal rank, got {a.dim()} and {b.dim()}")
-    if a.shape[:-2] != b.shape[:-2] or a.shape[-1] != b.shape[-2]:
-        raise _lib.ShapeMismatch(f"{list(a.shape)} vs {list(b.shape)}")
+    if a.shape[:-2] != b.shape[:-2] or a.shape[-1] != b.shape[-2]:  # tensor.rs:541-563
+        raise _lib.ShapeMismatch(f"shape mismatch: left={list(a.shape)}, right={list(b.shape)}",
+                                 left=a.shape, right=b.shape)
+    _on_cuda(a, b)
     a, b = a.contiguous(), b.contiguous()
     m, k, n = a.shape[-2], a.shape[-1], b.shape[-1]
     batch = math.prod(a.shape[:-2])

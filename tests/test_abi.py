@@ -83,6 +83,47 @@ def test_error_mapping_raises_reference_kinds():
         _lib.call("tmllm_repeat_kv", 0, C.c_void_p(16), C.c_void_p(16), 1, 2, 2, 2, 0, None)
 
 
+def test_structured_error_fields():
+    """PositionOutOfRange {start_pos, seq_len, max_seq_len} and ShapeMismatch {left, right}
+    cross the ABI with their fields (src/error.rs:6-9,19-23; raised as in
+    src/ops/kv_cache_write.rs:100-110 and src/tensor/gqa_matmul.rs:111-116)."""
+    lib = _lib.load()
+    dummy = C.c_void_p(16)
+    # a cache write of positions [7, 9) into an 8-position cache
+    assert rc("tmllm_kv_cache_write", 1, dummy, dummy, 2, 8, 4, 7, 2, None) == 7
+    f = _lib.last_error_fields()
+    assert (f.status, f.start_pos, f.seq_len, f.max_seq_len) == (7, 7, 2, 8)
+    assert (f.left_rank, f.right_rank) == (0, 0)
+    assert lib.tmllm_last_error() == b"position range [7, 9) exceeds max sequence length 8"
+    with pytest.raises(_lib.PositionOutOfRange) as e:
+        _lib.call("tmllm_kv_cache_write", 0, dummy, dummy, 3, 100, 4, 99, 5, None)
+    assert (e.value.start_pos, e.value.seq_len, e.value.max_seq_len) == (99, 5, 100)
+    # any other failure, and any success, replaces the record
+    assert rc("tmllm_repeat_kv", 0, dummy, dummy, 1, 2, 2, 2, 0, None) == 8
+    f = _lib.last_error_fields()
+    assert (f.status, f.start_pos, f.seq_len, f.max_seq_len) == (8, 0, 0, 0)
+    cos = np.empty((4, 2), np.float32)
+    sin = np.empty((4, 2), np.float32)
+    assert rc("tmllm_rope_tables", cos.ctypes.data, sin.ctypes.data, 4, 4, 10000.0) == 0
+    assert _lib.last_error_fields().status == 0
+    assert lib.tmllm_last_error_fields(None) == _lib.InvalidArgument.status
+    # the Python mirror of the reference's Tensor API validates shapes on the host first
+    import torch
+    from rustllm_b200 import tensor_ops
+    q = torch.zeros((1, 4, 1, 64), dtype=torch.float16)
+    k = torch.zeros((2, 2, 8, 64), dtype=torch.float16)
+    with pytest.raises(_lib.ShapeMismatch) as e:
+        tensor_ops.gqa_qk_matmul(q, k)
+    assert (e.value.left, e.value.right) == ([1, 4, 1, 64], [2, 2, 8, 64])
+    a = torch.zeros((3, 2, 5), dtype=torch.float32)
+    b = torch.zeros((3, 4, 6), dtype=torch.float32)
+    with pytest.raises(_lib.ShapeMismatch) as e:
+        tensor_ops.batched_matmul(a, b)
+    assert (e.value.left, e.value.right) == ([3, 2, 5], [3, 4, 6])
+    assert str(_lib.PositionOutOfRange(start_pos=3, seq_len=2, max_seq_len=4)) == \
+        "position range [3, 5) exceeds max sequence length 4"
+
+
 def test_rope_tables_bit_exact_with_oracle(orc):
     """tmllm_rope_tables (host-side, as the reference builds them) equals the oracle."""
     for d, n, theta in [(64, 300, 100000.0), (4, 8, 10000.0), (128, 64, 500000.0)]:

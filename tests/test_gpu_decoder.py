@@ -11,8 +11,9 @@ import torch
 
 import rustllm_b200 as rb
 from rustllm_b200 import _lib
-from rustllm_b200.decoder import (Decoder, DecoderWeights, GraphedDecoder, ModelConfig,
-                                  reference_forward)
+from rustllm_b200.decoder import Decoder, DecoderWeights, GraphedDecoder, ModelConfig
+
+from model_reference import reference_forward
 
 pytestmark = pytest.mark.gpu
 
@@ -257,6 +258,46 @@ def test_fused_step_matches_library_step(cuda):
             dec.forward_step()
             dec.cache.advance(1)
         assert rel(a.logits, b.logits) < 2e-2
+
+
+@pytest.mark.parametrize("variant,d", [(0, 64), (2, 128), (1, 64), (1, 128)])
+def test_overlapped_decode_after_projection(cuda, variant, d):
+    """TMLLM_DECODE_OVERLAP right behind a projection that writes q, k_new and v_new
+    (tmllm_linear lets its dependents start as soon as it runs, so the decode really can
+    start early): the tensor-core kernel reads them only after its grid-dependency wait, and
+    the CUDA-core kernel (variant 1), which has no such wait, is launched plainly whatever
+    the flag says.  Either way the result is bit-identical to the plain launch."""
+    from rustllm_b200.decoder import linear
+    B, hq, hkv, n, hidden = 3, 8, 2, 300, 256
+    W = (hq + 2 * hkv) * d
+    g = torch.Generator(device=cuda).manual_seed(17)
+    wq = (torch.randn((hidden, W), generator=g, device=cuda) / 16).half()
+    x = torch.randn((B, hidden), generator=g, device=cuda).half()
+    kv_rows = [torch.randn((hkv, n - 40 * s, d), generator=g, device=cuda).half()
+               for s in range(B)]
+    outs = []
+    for flags in (0, 1):
+        cache = rb.PagedKvCache(1, B, n + 2, hkv, d, dtype=torch.float16, block_size=16,
+                                shuffle_seed=2, device=cuda)
+        for s in range(B):
+            cache.append(0, s, kv_rows[s], kv_rows[s])
+            cache.advance(n - 40 * s, s)
+            cache.reserve(s, 1)
+        qkv = torch.full((B, W), 3.0, dtype=torch.float16, device=cuda)  # stale values
+        out = torch.empty((B, hq, d), dtype=torch.float16, device=cuda)
+        torch.cuda.synchronize()
+        opts = _lib.DecodeOpts(q_seq_stride=W, kv_seq_stride=W, flags=flags, variant=variant)
+        base, es = qkv.data_ptr(), qkv.element_size()
+        linear(x, wq, out=qkv, overlap=True)  # the kernel right ahead writes q, k_new, v_new
+        _lib.call("tmllm_cache_decode", cache.handle, 0, base, base + hq * d * es,
+                  base + (hq + hkv) * d * es, out.data_ptr(), None, hq, C.byref(opts),
+                  stream(cuda))
+        torch.cuda.synchronize()
+        cache.advance(1)  # the appended rows are compared too
+        k, v = cache.gather(0, 0)
+        outs.append((out.clone(), k.clone(), v.clone()))
+    assert all(torch.equal(a, b) for a, b in zip(outs[0], outs[1]))
+    assert not torch.equal(outs[0][1][:, -1], torch.full_like(outs[0][1][:, -1], 3.0))
 
 
 def test_overlapped_decode_launch_matches_plain(cuda):

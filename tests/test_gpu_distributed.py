@@ -139,3 +139,29 @@ def test_exchange_wait_expires_with_status(cuda):
     finally:
         for r in range(2):
             _lib.load().tmllm_exchange_destroy(h[r])
+
+
+def test_exchange_shape_mismatch_carries_both_shapes(cuda):
+    """A call whose shape differs from the exchange's is refused on the host with
+    ShapeMismatch {left = the exchange's [rows, groups, head_dim], right = the call's}."""
+    import ctypes as C
+
+    import rustllm_b200 as rb
+    from rustllm_b200 import _lib
+
+    hq, hkv, d = 8, 2, 128
+    h = C.c_void_p()
+    _lib.call("tmllm_exchange_create", 1, 0, hq, hkv, d, C.byref(h), None)
+    arr = (C.c_void_p * 1)(h)
+    _lib.call("tmllm_exchange_connect_local", h, arr)
+    try:
+        cache = rb.PagedKvCache(1, 2, 64, hkv, d, dtype=torch.float16, device=cuda)
+        kv = cache.view(0)  # two sequences: 16 rows, 4 groups
+        opts = _lib.DecodeOpts()
+        p = torch.zeros((2, hq, d), dtype=torch.float16, device=cuda)
+        with pytest.raises(_lib.ShapeMismatch) as e:
+            _lib.call("tmllm_gqa_decode_exchange", C.byref(kv), p.data_ptr(), None, None,
+                      p.data_ptr(), None, hq, C.byref(opts), None, 0, h, None)
+        assert (e.value.left, e.value.right) == ([hq, hkv, d], [2 * hq, 2 * hkv, d])
+    finally:
+        _lib.load().tmllm_exchange_destroy(h)

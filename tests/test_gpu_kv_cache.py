@@ -63,8 +63,9 @@ def test_layer_cache_rejects_overflow_and_bad_shape(cuda):
     cache = rb.LayerKvCache(2, 4, 4, torch.float16, cuda)
     x = torch.ones((1, 2, 3, 4), dtype=torch.float16, device=cuda)
     cache.append(x, x)
-    with pytest.raises(rb.PositionOutOfRange):
+    with pytest.raises(rb.PositionOutOfRange) as e:  # kv_cache.rs:40-51
         cache.append(x, x)
+    assert (e.value.start_pos, e.value.seq_len, e.value.max_seq_len) == (3, 3, 4)
     assert cache.len() == 3
     with pytest.raises(rb.ModelFormat):
         cache.append(torch.ones((1, 3, 1, 4), dtype=torch.float16, device=cuda),
@@ -154,5 +155,7 @@ def test_paged_pool_exhaustion_and_reset(cuda):
     cache.append(0, 1, x, x)
     cache.advance(48, 1)
     assert len(cache.block_table(1)) == 3
-    with pytest.raises(rb.PositionOutOfRange):
+    with pytest.raises(rb.PositionOutOfRange) as e:  # through the C ABI's error fields
         cache.reserve(1, 17)
+    assert (e.value.start_pos, e.value.seq_len, e.value.max_seq_len) == (48, 17, 64)
+    assert "position range [48, 65) exceeds max sequence length 64" in str(e.value)

@@ -70,3 +70,33 @@ def test_noalloc_refuses_oversized_scratch(cuda):
                                               C.c_void_p(256), None, 16, C.byref(opts), None)
     assert rc == _lib.InvalidShape.status
     assert b"built-in scratch" in _lib.load().tmllm_last_error()
+
+
+def test_noalloc_single_split_with_more_groups_than_counters(cuda):
+    """With one split no ticket is taken, so nothing is cleared: 65535 sequences x 16 KV
+    heads (about a million (sequence, KV head) groups, whose tickets would need 4 MiB, twice
+    the built-in scratch) run with num_splits = 1 and match the workspace decode."""
+    B, hq, hkv, d, n = 65535, 16, 16, 64, 5
+    g = torch.Generator(device=cuda).manual_seed(7)
+    k_ar = torch.randn((1, hkv, 16, d), generator=g, device=cuda).half()
+    v_ar = torch.randn((1, hkv, 16, d), generator=g, device=cuda).half()
+    table = torch.zeros((B, 1), dtype=torch.int32, device=cuda)  # every sequence: block 0
+    lens = torch.full((B,), n, dtype=torch.int32, device=cuda)
+    kv = rb.paged_kv_from_tensors(k_ar, v_ar, table, lens)
+    q = torch.randn((B, hq, d), generator=g, device=cuda).half()
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    opts = _lib.DecodeOpts(num_splits=1, max_len_hint=n)
+    ref = torch.empty_like(q)
+    _lib.call("tmllm_gqa_decode", C.byref(kv), q.data_ptr(), None, None, ref.data_ptr(), None,
+              hq, C.byref(opts), None, 0, stream)
+    for _ in range(2):
+        out = torch.full_like(q, float("nan"))
+        _lib.call("tmllm_gqa_decode_noalloc", C.byref(kv), q.data_ptr(), None, None,
+                  out.data_ptr(), None, hq, C.byref(opts), stream)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+    # one more sequence than the grid allows is refused on the host
+    kv.num_seqs = B + 1
+    rc = _lib.load().tmllm_gqa_decode_noalloc(C.byref(kv), q.data_ptr(), None, None,
+                                              out.data_ptr(), None, hq, C.byref(opts), stream)
+    assert rc == _lib.InvalidShape.status
