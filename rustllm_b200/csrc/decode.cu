@@ -19,6 +19,7 @@
 //   v_new into their paged slot and uses them from shared memory (no read-after-write
 //   through memory).  With several splits, each CTA writes (O, m, l) partials and the
 //   last CTA of a (seq, kv head) -- found with an atomic ticket -- merges them.
+#include <atomic>
 #include <cmath>
 
 #include "common.cuh"
@@ -1340,6 +1341,21 @@ __global__ void merge_lse_kernel(const float* __restrict__ po, const float* __re
 
 // ---- launch plumbing -------------------------------------------------------------------
 
+// Opts `fn` into `bytes` of dynamic shared memory on the current device, once per device
+// (bit d of `mask`, one mask per kernel instantiation): the attribute call costs more host
+// time than the launch itself on short decode steps.
+template <typename F>
+int opt_in_smem(F* fn, size_t bytes, std::atomic<uint64_t>& mask) {
+    int dev = 0;
+    TMLLM_CUDA_TRY(cudaGetDevice(&dev));
+    const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
+    if (bit && (mask.load(std::memory_order_relaxed) & bit)) return TMLLM_OK;
+    TMLLM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(bytes)));
+    mask.fetch_or(bit, std::memory_order_relaxed);
+    return TMLLM_OK;
+}
+
 // When asked (the allocation-free entry point, whose scratch keeps the previous call's
 // contents), zero the split tickets on the stream right before the launch -- after every
 // argument check, so a refused call enqueues nothing.  Tickets exist only with splits.
@@ -1375,8 +1391,8 @@ int launch_tiled(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
     const size_t need_merge = (2 * static_cast<size_t>(grid.z) + 2) * GP * 4;
     if (need_merge > static_cast<size_t>(STAGES * 2 * Cfg::TILE))
         return fail(TMLLM_INVALID_ARGUMENT, "too many splits (%u) for the merge scratch", grid.z);
-    TMLLM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(bytes)));
+    static std::atomic<uint64_t> opted{0};
+    if (int st = opt_in_smem(fn, bytes, opted)) return st;
     if (int st = clear_split_tickets(a, grid, s)) return st;
     // Always a plain launch: this kernel reads q / k_new / v_new without a grid-dependency
     // wait, so it must not start before the kernel ahead of it has finished.
@@ -1392,8 +1408,8 @@ int launch_mma(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
     const size_t bytes = static_cast<size_t>(Cfg::BYTES);
     if ((2 * static_cast<size_t>(grid.z) + 2) * 16 * 4 > static_cast<size_t>(Cfg::OFF_FIN))
         return fail(TMLLM_INVALID_ARGUMENT, "too many splits (%u) for the merge scratch", grid.z);
-    TMLLM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(bytes)));
+    static std::atomic<uint64_t> opted{0};
+    if (int st = opt_in_smem(fn, bytes, opted)) return st;
     if (int st = clear_split_tickets(a, grid, s)) return st;
     if (a.overlap) {
         // programmatic stream serialisation: the kernel may start while the one ahead of it

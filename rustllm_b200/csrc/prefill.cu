@@ -18,6 +18,7 @@
 // accumulation of those kernels and one F16 rounding of P before the second product.
 // F32 caches, other head sizes and small pages run a CUDA-core kernel with the same
 // semantics (prefill_generic_kernel).
+#include <atomic>
 #include <cuda.h>  // CUtensorMap and its enums; the encoder is fetched from the driver at run time
 
 #include <cmath>
@@ -906,15 +907,17 @@ int launch_tc(const PrefillArgs& a, int64_t arena_rows, int max_rows, cudaStream
         if (int st = make_map(&cmap, a.rope_cos, D / 2, a.rope_len, D * 2, kTile, true)) return st;
         if (int st = make_map(&smap, a.rope_sin, D / 2, a.rope_len, D * 2, kTile, true)) return st;
     }
-    static std::once_flag once[64];
+    // the shared-memory opt-in once per device (bit d of the mask; retried after a failure)
+    static std::atomic<uint64_t> opted{0};
     int dev = 0;
     TMLLM_CUDA_TRY(cudaGetDevice(&dev));
-    cudaError_t attr = cudaSuccess;
-    std::call_once(once[dev & 63], [&] {
-        attr = cudaFuncSetAttribute(prefill_tc_kernel<D>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
-    });
-    if (attr != cudaSuccess) return cuda_fail(attr, "prefill shared-memory attribute");
+    const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
+    if (!bit || !(opted.load(std::memory_order_relaxed) & bit)) {
+        TMLLM_CUDA_TRY(cudaFuncSetAttribute(prefill_tc_kernel<D>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            Cfg::SMEM));
+        opted.fetch_or(bit, std::memory_order_relaxed);
+    }
     const int row_tiles = (max_rows + kTile - 1) / kTile;
     const int64_t units = static_cast<int64_t>(row_tiles) * a.q_heads * a.num_seqs;
     if (units > INT32_MAX) return fail(TMLLM_INVALID_SHAPE, "too many prefill tiles");

@@ -1,9 +1,14 @@
 """Fused KV-append + GQA decode attention (the hot path) against the CPU oracle.
 
 Tolerances (from the north star): attention outputs within 1e-5 relative for F32 and 2e-3
-for F16, measured as max|gpu - ref| / max|ref| over the output tensor, against both the
-oracle's faithful chain (the reference's storage roundings) and its float64 chain.  The
-appended K/V rows and block tables are bit-exact."""
+for F16.  Against the oracle's float64 chain (the exact result of the same inputs) this is
+checked two ways: norm-relative, max|gpu - ref| / max|ref| over a sequence's output, and
+element by element, |gpu - ref| <= tol * (|ref| + rms(ref)) (a per-element relative bound
+whose floor, tol * rms, keeps outputs near zero from demanding more than the storage
+precision).  The faithful chain (the reference's own F16 store points for scores,
+probabilities and outputs) itself sits up to ~1.7e-3 from the exact result at config 3's
+lengths, so against it the bound is the triangle inequality's: norm-relative within
+tol + rel(faithful, float64).  The appended K/V rows and block tables are bit-exact."""
 from __future__ import annotations
 
 import math
@@ -23,6 +28,21 @@ def rel(a, b) -> float:
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), 1e-30))
+
+
+def elem_excess(a, b, tol) -> float:
+    """max over elements of |a - b| / (tol * (|b| + rms(b))): <= 1 passes the element-wise
+    bound."""
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    rms = float(np.sqrt(np.mean(b * b)))
+    return float(np.max(np.abs(a - b) / (tol * (np.abs(b) + rms) + 1e-300)))
+
+
+def assert_close(got, want, tol, what="", elementwise=True):
+    r = rel(got, want)
+    e = elem_excess(got, want, tol) if elementwise else 0.0
+    assert r < tol and e <= 1.0, (what, r, e)
 
 
 def bits(x: np.ndarray) -> np.ndarray:
@@ -98,8 +118,9 @@ def check(case: Case, orc, got, lse, append=True, tol=None):
     tol = tol or TOL[case.npd]
     for s in range(case.B):
         faithful, wide, wlse, _ = case.oracle(orc, s, append)
-        assert rel(got[s], wide) < tol, (s, rel(got[s], wide))
-        assert rel(got[s], faithful) < tol, (s, rel(got[s], faithful))
+        assert_close(got[s], wide, tol, ("float64 chain", s))
+        assert_close(got[s], faithful, tol + rel(faithful, wide), ("faithful chain", s),
+                     elementwise=False)
         assert np.max(np.abs(lse[s] - wlse)) < 1e-3 * max(1.0, float(np.max(np.abs(wlse))))
 
 
@@ -116,8 +137,8 @@ def test_config1_fixture(cuda, orc, fixtures):
                        torch.from_numpy(f["cfg1_k"][:, :, 0].copy()).to(cuda),
                        torch.from_numpy(f["cfg1_v"][:, :, 0].copy()).to(cuda), rope=rope)
     got = out.cpu().numpy()[0]
-    assert rel(got, f["cfg1_out"][0, :, 0]) < 1e-5
-    assert rel(got, f["cfg1_out_wide"][0, :, 0]) < 1e-5
+    assert_close(got, f["cfg1_out"][0, :, 0], 1e-5, "faithful chain", elementwise=False)
+    assert_close(got, f["cfg1_out_wide"][0, :, 0], 1e-5, "float64 chain")
     cache.advance(1, 0)
     k, v = cache.gather(0, 0)
     assert np.array_equal(bits(k.cpu().numpy()[:, 128]), bits(f["cfg1_k_row_after"][0]))
@@ -135,8 +156,8 @@ def test_f16_fixture(cuda, orc, fixtures):
                        torch.from_numpy(f["f16_k"][:, :, 0].copy()).to(cuda),
                        torch.from_numpy(f["f16_v"][:, :, 0].copy()).to(cuda))
     got = out.float().cpu().numpy()[0]
-    assert rel(got, f["f16_out"][0, :, 0]) < 2e-3
-    assert rel(got, f["f16_out_wide"][0, :, 0]) < 2e-3
+    assert_close(got, f["f16_out"][0, :, 0], 2e-3, "faithful chain", elementwise=False)
+    assert_close(got, f["f16_out_wide"][0, :, 0], 2e-3, "float64 chain")
 
 
 CASES = [
@@ -273,9 +294,10 @@ def test_decode_rejects_full_cache_without_mutation(cuda):
     assert case.cache.len(0) == 10 and case.cache.block_table(0) == before
 
 
-def test_config4_full_size_against_float64(cuda, orc):
+def test_config4_full_size_against_oracle(cuda, orc):
     """BASELINE config 4 at full size (F16, Hq 32, Hkv 8, D 128, 131072 cached + 1): the
-    fused kernel against the float64 oracle (threaded), plus the constant-V identity."""
+    fused kernel against the float64 oracle and the faithful F16 chain (both threaded),
+    plus the constant-V identity."""
     hq, hkv, d, n = 32, 8, 128, 131072
     g = torch.Generator(device=cuda).manual_seed(4)
     kd = torch.randn((hkv, n, d), generator=g, device=cuda).half()
@@ -291,10 +313,16 @@ def test_config4_full_size_against_float64(cuda, orc):
     kc = torch.cat([kd, kn[0][:, None]], 1)[None].cpu().numpy()
     vc = torch.cat([vd, vn[0][:, None]], 1)[None].cpu().numpy()
     import os
-    wide, wlse = orc.attention_core_wide(q[:, :, None].cpu().numpy(), kc, vc, n + 1, n,
-                                         threads=os.cpu_count() or 8)
-    assert rel(out.float().cpu().numpy(), wide[:, :, 0]) < 2e-3
+    threads = os.cpu_count() or 8
+    qn = q[:, :, None].cpu().numpy()
+    wide, wlse = orc.attention_core_wide(qn, kc, vc, n + 1, n, threads=threads)
+    got = out.float().cpu().numpy()
+    assert_close(got, wide[:, :, 0], 2e-3, "float64 chain")
     assert np.max(np.abs(lse.cpu().numpy() - wlse[:, :, 0])) < 1e-2
+    # and the reference's own chain with its F16 store points (scores, probabilities)
+    faithful = orc.attention_core(qn, kc, vc, n + 1, n, threads=threads)
+    assert_close(got, faithful[:, :, 0], 2e-3 + rel(faithful[:, :, 0], wide[:, :, 0]),
+                 "faithful chain", elementwise=False)
     # softmax weights sum to one: a constant V row gives back that constant
     cache2 = rb.PagedKvCache(1, 1, n + 1, hkv, d, dtype=torch.float16, block_size=16,
                              device=cuda)
@@ -304,3 +332,21 @@ def test_config4_full_size_against_float64(cuda, orc):
     cache2.advance(n, 0)
     out2 = cache2.decode(0, q, kn, const.expand(1, hkv, d).contiguous())
     assert float((out2.float() - const.float()).abs().max()) < 2e-3
+
+
+def test_config3_attention_full_batch(cuda, orc):
+    """BASELINE config 3's attention op at its real batch: 64 sequences with context lengths
+    U[256, 2048] (seeded as the bench draws them), Hq 15 / Hkv 5 / D 64, 16-token pages in a
+    random permutation, the split count the cache chooses from the actual lengths.  Every
+    sequence against the faithful and the float64 chain; every appended row bit-exact."""
+    gen = torch.Generator().manual_seed(1234)
+    lens = torch.randint(256, 2049, (64,), generator=gen).tolist()
+    case = Case(cuda, np.float16, 15, 5, 64, lens, block_size=16, seed=1234)
+    got, lse = case.gpu()
+    check(case, orc, got, lse)
+    case.cache.advance(1)
+    for s in range(case.B):
+        k, v = case.cache.gather(0, s)
+        _, _, _, kn = case.oracle(orc, s)
+        assert np.array_equal(bits(k.cpu().numpy()[:, lens[s]]), bits(kn))
+        assert np.array_equal(bits(v.cpu().numpy()[:, lens[s]]), bits(case.vn[s]))

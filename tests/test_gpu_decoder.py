@@ -334,3 +334,59 @@ def test_overlapped_decode_launch_matches_plain(cuda):
         _lib.call("tmllm_cache_decode", cache.handle, 0, base, base + hq * d * es,
                   base + (hq + hkv) * d * es, out.data_ptr(), None, hq, C.byref(opts),
                   stream(cuda))
+
+
+def _greedy_against_float32(cuda, preset, B, prompt_len, steps, seed, check_seqs):
+    """Whole-prompt prefill then `steps` greedy decode steps of a BASELINE model shape
+    (random-init weights N(0, 0.02)); every emitted token's logits against the float32
+    restatement run over the prompt plus the tokens emitted before it."""
+    from rustllm_b200.decoder import PRESETS
+    cfg = PRESETS[preset]
+    w = DecoderWeights(cfg, device=cuda, seed=seed)
+    prompts = torch.randint(0, cfg.vocab_size, (B, prompt_len),
+                            generator=torch.Generator().manual_seed(seed + 1))
+    dec = Decoder(cfg, w, B, device=cuda, max_seq_len=prompt_len + steps + 2,
+                  shuffle_seed=seed)
+    nxt = dec.prefill(prompts.to(cuda))
+    logits, toks = [dec.logits.float().clone()], [nxt.clone()]
+    for _ in range(steps):
+        dec.ids.copy_(nxt)
+        dec.forward_step()
+        dec.cache.advance(1)
+        logits.append(dec.logits.float().clone())
+        nxt = dec.next_ids.clone()
+        toks.append(nxt)
+    assert dec.cache.lens() == [prompt_len + steps] * B
+    toks = torch.stack(toks)  # [steps + 1, B]
+    clear = 0
+    for s in check_seqs:
+        seq = torch.cat([prompts[s].to(cuda), toks[:-1, s].long()])
+        want = reference_forward(cfg, w, seq)[prompt_len - 1:]  # row t: token t's logits
+        for t in range(steps + 1):
+            got, ref = logits[t][s], want[t]
+            err = float((got - ref).abs().max())
+            # the reference's own model-level bound (F16 model vs F32 model, absolute per
+            # logit: src/model/transformer.rs:576-597) and a norm-relative one
+            assert err < 0.2, (s, t, err)
+            assert rel(got, ref) < 3e-2, (s, t, rel(got, ref))
+            top = ref.topk(2).values
+            if float(top[0] - top[1]) > 2 * err:  # the float32 model's choice is clear
+                assert int(toks[t, s]) == int(ref.argmax()), (s, t)
+                clear += 1
+            if t < 2:  # the first greedy tokens are identical in any case
+                assert int(toks[t, s]) == int(ref.argmax()), (s, t)
+    return clear
+
+
+def test_decoder_config2_shape_greedy_tokens(cuda):
+    """BASELINE config 2's model (SmolLM2-135M shape: 30 layers, hidden 576, 9 / 3 heads,
+    vocab 49152), batch 1, a 32-token prompt, then 8 greedy tokens."""
+    assert _greedy_against_float32(cuda, "smollm2-135m", 1, 32, 8, 21, [0]) >= 5
+
+
+def test_decoder_config5_shape_greedy_tokens(cuda):
+    """BASELINE config 5's model (TinyStories-110M shape: 12 layers, dim 768, 12 heads MHA,
+    vocab 32000), 16 prompts x 512 tokens through the tensor-core prefill, then 4 greedy
+    tokens for every sequence, all 16 checked."""
+    assert _greedy_against_float32(cuda, "tinystories-110m", 16, 512, 4, 31,
+                                   list(range(16))) >= 40
