@@ -255,7 +255,7 @@ def run_ours(args) -> None:
 
     torch.manual_seed(1234 + rank)
     cached = args.cached
-    overlap = world == 1 and not args.no_overlap
+    overlap = (world == 1 or args.exchange == "p2p") and not args.no_overlap
     sp = SequenceSplitAttention(cached, HQ, HKV, D, dtype=torch.float16, block_size=BS,
                                 shuffle_seed=77 + rank, device=dev, variant=args.variant,
                                 num_splits=args.splits, exchange=args.exchange,
@@ -299,10 +299,12 @@ def run_ours(args) -> None:
         dist.barrier()
     profile_region(True)
     wall0 = time.time()
+    h0 = time.perf_counter()
     t_start.record(stream)
     for _ in range(args.steps):
         sp.step(q, kn, vn, out)
     t_end.record(stream)
+    host_us = (time.perf_counter() - h0) * 1e6 / args.steps  # host submission per step
     torch.cuda.synchronize()
     profile_region(False)
     wall1 = time.time()
@@ -326,7 +328,34 @@ def run_ours(args) -> None:
         dist.barrier()
     ms_total = t_start.elapsed_time(t_end)
     k_ms = sum(a.elapsed_time(b) for a, b in kev) / n_k
+    # per-rank timeline (N > 1): this rank's share attended alone (the same fused kernel
+    # without the exchange, consecutive launches overlapped), against the exchanged step
+    local_ms = None
+    if world > 1:
+        lo = torch.empty((1, HQ, D), dtype=torch.float32, device=dev)
+        ll = torch.empty((1, HQ), dtype=torch.float32, device=dev)
+        kwl = dict(out=lo, lse=ll, overlap=not args.no_overlap, num_splits=args.splits,
+                   variant=args.variant)
+        for _ in range(20):
+            sp.cache.decode(0, q, kn if sp.owner else None, vn if sp.owner else None, **kwl)
+        l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_l = min(args.steps, 2000)
+        l0.record(stream)
+        for _ in range(n_l):
+            sp.cache.decode(0, q, kn if sp.owner else None, vn if sp.owner else None, **kwl)
+        l1.record(stream)
+        torch.cuda.synchronize()
+        local_ms = l0.elapsed_time(l1) / n_l
+        dist.barrier()
     clocks = sampler.stop(wall0, wall1) if sampler else None
+    per_rank = None
+    if world > 1:
+        mine = torch.tensor([ms_total / args.steps * 1e3, local_ms * 1e3, host_us],
+                            dtype=torch.float64, device=dev)
+        allr = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allr, mine)
+        per_rank = [{"rank": r, "step_us": float(x[0]), "local_attention_us": float(x[1]),
+                     "host_submit_us": float(x[2])} for r, x in enumerate(allr)]
     t = torch.tensor([ms_total, k_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -416,6 +445,8 @@ def run_ours(args) -> None:
                     "d2h_bytes_per_step": d2h},
             "clocks": clocks,
         }
+        if per_rank is not None:
+            line["per_rank"] = per_rank
         if cached != CACHED:
             line["config"]["cached"] = cached
             line["config"]["workload"] += f" (reduced to {cached} cached for a capture)"
@@ -564,7 +595,9 @@ def run_decoder(args) -> None:
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                          "peak_source": peaks["source"], "traffic": None,
-                         "scope": "whole decode step on rank 0: weights + K/V read per step"},
+                         "scope": "whole decode step on rank 0: weights + K/V read per step",
+                         "floor_ms_per_step": step_bytes / (peaks["hbm_gbs"] * 1e9) * 1e3,
+                         "bytes_per_step": step_bytes},
             "clocks": clocks,
             # this package's kernels a step launches (cuBLAS GEMMs not counted): embedding;
             # a layer's projections + attention (fused: 4 + 1; else norm x2, SwiGLU,

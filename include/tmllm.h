@@ -276,9 +276,10 @@ typedef struct tmllm_decode_opts {
  * queued before it on the stream (programmatic dependent launch).  The lengths, block table
  * and cached K/V are read before that work has finished, so the caller promises it does not
  * write them; q, k_new and v_new are read, and anything is written, only after it has
- * finished.  Ignored by the CUDA-core kernels (always launched plainly), with the cross-GPU
- * exchange, and by tmllm_cache_decode on a call that assigns a new block (the table update
- * it queues must finish first). */
+ * finished.  With the cross-GPU exchange (tmllm_gqa_decode_exchange) the same holds on
+ * every rank: a step's prologue may run while the previous step exchanges.  Ignored by the
+ * CUDA-core kernels (always launched plainly) and by tmllm_cache_decode on a call that
+ * assigns a new block (the table update it queues must finish first). */
 #define TMLLM_DECODE_OVERLAP 1
 
 /* Bytes of scratch tmllm_gqa_decode needs for `num_splits` splits (0 = enough for any

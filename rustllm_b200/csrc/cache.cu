@@ -23,6 +23,7 @@ size_t decode_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int
 int32_t decode_auto_splits(int64_t B, int64_t Hkv, int64_t max_len);
 int32_t decode_auto_splits_lens(const int64_t* lens, int64_t B, int64_t Hkv, int64_t hint,
                                 int per_sm);
+int decode_resident_ctas(int dtype, int head_dim, int variant, int group);
 int prefill_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, const void* v_new,
                  const int32_t* q_start, int32_t rows_per_seq, int32_t max_rows,
                  int32_t total_rows, void* out, int32_t q_heads, const tmllm_decode_opts* opts,
@@ -496,11 +497,10 @@ int tmllm_cache_decode(tmllm_cache* cache, int32_t layer, const void* q, const v
     }
     int32_t splits = o.num_splits;
     if (splits <= 0) {
-        // resident CTAs per SM of the kernel that will run: the tensor-core decode keeps
-        // four per SM at head_dim 64, every other configuration two
+        // resident CTAs per SM of the kernel that will run
         const int G = q_heads / cache->cfg.num_kv_heads;
-        const int per_sm = (cache->cfg.dtype == TMLLM_F16 && cache->cfg.head_dim == 64 &&
-                            o.variant != 1 && G <= 16) ? 4 : 2;
+        const int per_sm = decode_resident_ctas(cache->cfg.dtype, cache->cfg.head_dim,
+                                                o.variant, G);
         std::vector<int64_t> lens(cache->h_lens.begin(), cache->h_lens.end());
         if (append)
             for (auto& x : lens) ++x;

@@ -28,6 +28,13 @@ namespace tmllm {
 namespace {
 
 constexpr int kDecodeThreads = 128;
+// Ring depth (16-position sub-tiles per warp) of the head_dim-64 tensor-core kernel and the
+// CTAs per SM its shared memory and registers allow.
+#ifndef TMLLM_D64_STAGES
+#define TMLLM_D64_STAGES 3
+#endif
+constexpr int kD64Stages = TMLLM_D64_STAGES;
+constexpr int kD64MinBlocks = kD64Stages <= 3 ? 4 : (kD64Stages == 4 ? 3 : 2);
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -637,7 +644,7 @@ struct MmaCfg {
 // head-major form (whose M = 16 rows carry only G real query heads): at short contexts the
 // loop is bound by a warp's per-sub-tile chain, not by memory bandwidth.
 template <int D, int STAGES, bool PT>
-__global__ void __launch_bounds__(kDecodeThreads, D == 64 ? 4 : 2) decode_mma_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(kDecodeThreads, D == 64 ? kD64MinBlocks : 2) decode_mma_kernel(const DecodeArgs a) {
     using Cfg = MmaCfg<D, STAGES>;
     static_assert(!PT || D == 64, "the positions-major form is instantiated for D = 64");
     constexpr int C = Cfg::C, ROW = Cfg::ROW, SUBB = Cfg::SUBB, QROW = Cfg::QROW;
@@ -1444,8 +1451,9 @@ int launch_decode(int dtype, int D, int variant, const DecodeArgs& a, dim3 grid,
                   bool* done) {
     *done = true;
     if (dtype == TMLLM_F16 && a.group <= 16 && variant != 1) {
-        if (D == 64 && a.group <= 8 && a.ex == nullptr) return launch_mma<64, 3, true>(a, grid, s);
-        if (D == 64) return launch_mma<64, 3>(a, grid, s);
+        if (D == 64 && a.group <= 8 && a.ex == nullptr)
+            return launch_mma<64, kD64Stages, true>(a, grid, s);
+        if (D == 64) return launch_mma<64, kD64Stages>(a, grid, s);
         if (D == 128) return launch_mma<128, 3>(a, grid, s);
     }
     if (dtype == TMLLM_F16 && a.group <= 8) {
@@ -1602,8 +1610,10 @@ int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
         return fail(TMLLM_INVALID_SHAPE, "sequence strides of q / k_new must cover a sequence");
     a.q_stride = o.q_seq_stride > 0 ? o.q_seq_stride : static_cast<int64_t>(q_heads) * D;
     a.kv_stride = o.kv_seq_stride > 0 ? o.kv_seq_stride : static_cast<int64_t>(Hkv) * D;
-    // the overlapped launch is for the single-GPU tensor-core kernel (not the exchange)
-    a.overlap = (o.flags & TMLLM_DECODE_OVERLAP) && !ex ? 1 : 0;
+    // the overlapped launch applies to the tensor-core kernel (the CUDA-core kernels always
+    // launch plainly); with the exchange it lets a step's prologue run under the previous
+    // step's exchange, whose cells alternate by step parity
+    a.overlap = (o.flags & TMLLM_DECODE_OVERLAP) ? 1 : 0;
     a.clear_tickets = clear_tickets ? 1 : 0;
     if (ex && !(mma_shape && o.variant != 1))
         return fail(TMLLM_INVALID_ARGUMENT,
@@ -1665,6 +1675,12 @@ int32_t decode_auto_splits(int64_t B, int64_t Hkv, int64_t max_len) {
 }
 
 int32_t decode_auto_splits_bound(int64_t B, int64_t Hkv) { return auto_splits_bound(B, Hkv); }
+
+// Resident CTAs per SM of the decode kernel that runs for this configuration.
+int decode_resident_ctas(int dtype, int head_dim, int variant, int group) {
+    if (dtype == TMLLM_F16 && head_dim == 64 && variant != 1 && group <= 16) return kD64MinBlocks;
+    return 2;
+}
 
 // Split count for a batch whose lengths the host knows (the cache runtime): the largest count
 // whose CTAs -- ceil(len / chunk) per sequence and KV head, chunk as decode_impl_ex derives

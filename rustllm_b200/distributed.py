@@ -132,8 +132,9 @@ class SequenceSplitAttention:
         self.recv = torch.zeros((self.world, width), dtype=torch.float32, device=self.device)
         self.global_len = total_cached
         self.kw = {"variant": variant, "num_splits": num_splits}
-        # one GPU: consecutive steps may overlap (TMLLM_DECODE_OVERLAP); the caller promises
-        # that nothing between two steps writes this rank's cache
+        # consecutive steps may overlap (TMLLM_DECODE_OVERLAP): one GPU, or the in-kernel
+        # exchange; the caller promises that nothing between two steps writes this rank's
+        # cache
         self.overlap = overlap
         if exchange not in ("p2p", "nccl"):
             raise ValueError(f"unknown exchange {exchange!r}")
@@ -184,28 +185,36 @@ class SequenceSplitAttention:
         lengths are kept between steps and refreshed by ``fill`` / ``advance``."""
         if self._kv is None:
             self._kv = self.cache.view(0)
-            self._opts = DecodeOpts(num_splits=self.kw["num_splits"], variant=self.kw["variant"])
+            self._opts = DecodeOpts(num_splits=self.kw["num_splits"], variant=self.kw["variant"],
+                                    flags=_lib.DECODE_OVERLAP if self.overlap else 0)
             self._fn = _lib.load().tmllm_gqa_decode_exchange
             self._local_len = self.cache.len(0)
             self._reserved = self._local_len
+            self._key = None
         if self.owner and self._reserved < self._local_len + 1:
             self.cache.reserve(0, 1)
             self._reserved = self._local_len + 1
-        o = self._opts
-        o.out_f32 = int(out.dtype == torch.float32)
-        o.rope_pos_offset = self.global_len - self._local_len
-        o.max_len_hint = self._local_len + 1
-        if rope is not None:
-            cos, sin = rope
-            o.rope_cos, o.rope_sin, o.rope_len = cos.data_ptr(), sin.data_ptr(), cos.shape[0]
-        else:
-            o.rope_cos = o.rope_sin = None
-            o.rope_len = 0
+            self._key = None  # the reservation is a kernel ahead of this launch
         own = self.owner
-        rc = self._fn(C.byref(self._kv), q.data_ptr(), k_new.data_ptr() if own else None,
-                      v_new.data_ptr() if own else None, out.data_ptr(), None, self.hq,
-                      C.byref(o), self.ws.ptr, self.ws.nbytes, self.peer.handle,
-                      stream_ptr(self.device))
+        key = (q.data_ptr(), k_new.data_ptr() if own else None,
+               v_new.data_ptr() if own else None, out.data_ptr(), out.dtype,
+               None if rope is None else (rope[0].data_ptr(), rope[1].data_ptr()),
+               self._local_len, self.global_len, stream_ptr(self.device))
+        if key != self._key:  # arguments rebuilt only when something changed
+            o = self._opts
+            o.out_f32 = int(out.dtype == torch.float32)
+            o.rope_pos_offset = self.global_len - self._local_len
+            o.max_len_hint = self._local_len + 1
+            if rope is not None:
+                cos, sin = rope
+                o.rope_cos, o.rope_sin, o.rope_len = cos.data_ptr(), sin.data_ptr(), cos.shape[0]
+            else:
+                o.rope_cos = o.rope_sin = None
+                o.rope_len = 0
+            self._args = (C.byref(self._kv), key[0], key[1], key[2], key[3], None, self.hq,
+                          C.byref(o), self.ws.ptr, self.ws.nbytes, self.peer.handle, key[-1])
+            self._key = key
+        rc = self._fn(*self._args)
         if rc:
             _lib.check(rc)
         return out
