@@ -513,7 +513,10 @@ def run_decoder(args) -> None:
     gen = torch.Generator().manual_seed(1234)
     if args.workload == "cfg3":
         ctx = torch.randint(256, 2049, (total_seqs,), generator=gen).tolist()
-        mine = shard_sequences(total_seqs, rank, world)  # batch sharding, no collective
+        # batch sharding, no collective; --shard-of M runs rank 0's share of an M-way shard
+        # on this one GPU (a rank's work alone, for exploring the per-rank step)
+        ways = args.shard_of if (args.shard_of and world == 1) else world
+        mine = shard_sequences(total_seqs, rank, ways)
         scaling = "strong"
     else:
         ctx = [prompt] * total_seqs
@@ -573,7 +576,8 @@ def run_decoder(args) -> None:
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t[0])
-    tokens = (total_seqs if args.workload == "cfg3" else B * world) * steps
+    tokens = (total_seqs if args.workload == "cfg3" and not args.shard_of
+              else B * world) * steps
     tok_s = tokens / (ms * 1e-3)
     # step bytes on this rank: every weight once + the K/V each sequence reads
     e = 2
@@ -588,7 +592,9 @@ def run_decoder(args) -> None:
             "warmup": args.warmup, "ms_per_step": ms / steps, "higher_is_better": True,
             "scaling": scaling, "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (random-init weights N(0,0.02), random token ids, seeded)",
-            "config": {"workload": desc, "preset": preset, "sequences": total_seqs,
+            "config": {"workload": desc + (f" (rank 0's share of a {args.shard_of}-way "
+                                           f"shard: {B} sequences)" if args.shard_of else ""),
+                       "preset": preset, "sequences": total_seqs,
                        "parallelism": (f"batch-shard{world}" if args.workload == "cfg3"
                                        else f"replicas{world}") if world > 1 else "1gpu",
                        "graph": "one CUDA graph per decode step"},
@@ -1262,6 +1268,8 @@ def main() -> None:
                     help="ncu DRAM bytes per launch of the decode kernel, if measured anew")
     ap.add_argument("--settle", type=int, default=SETTLE_STEPS,
                     help="untimed steps after the warm-up, before the timed region")
+    ap.add_argument("--shard-of", type=int, default=0,
+                    help="cfg3 on one GPU: run only rank 0's share of this many batch shards")
     ap.add_argument("--no-overlap", action="store_true",
                     help="config 4 on one GPU: launch consecutive steps without "
                          "programmatic dependent launch")
