@@ -559,9 +559,13 @@ __device__ __forceinline__ bool wait_cell(const uint2* p, unsigned step,
 // rank's buffer as their cells turn to this step (waiting at most ex->timeout_ns), and
 // merge everything by log-sum-exp into `out`/`lse`.  Slots alternate by step parity, so a
 // rank one step ahead never overwrites cells another rank is still reading.
+// The reads are batched so their round trips overlap: first every other rank's lse of the
+// group's rows, one cell per thread, then each thread's output cells of all ranks as one
+// burst of independent loads (only cells not yet at this step are polled again).
+// `scratch` is >= (kMaxRanks + 2) * 16 floats of free shared memory.
 template <typename T>
 __device__ void exchange_tail(const DecodeArgs& a, const float* fin, const float* flse, int G,
-                              int D, int64_t row0, int* flag_s) {
+                              int D, int64_t row0, int* flag_s, float* scratch) {
     const ExchangeArgs* ex = a.ex;
     const int tid = threadIdx.x, world = ex->world, rank = ex->rank;
     const int64_t rows = ex->rows;
@@ -574,42 +578,85 @@ __device__ void exchange_tail(const DecodeArgs& a, const float* fin, const float
         for (int i = tid; i < G * D; i += kDecodeThreads) st_cell(dst + i, fin[i], step);
         if (tid < G) st_cell(ex->recv_lse[p] + mine + tid, flse[tid], step);
     }
+    float* wgt = scratch;                    // [kMaxRanks][16] merge weights e^(lse_p - M_g)
+    float* den = scratch + kMaxRanks * 16;   // [16] their sums
+    float* mx = den + 16;                    // [16] M_g
     if (tid == 0) *flag_s = 0;
     __syncthreads();
     const unsigned long long deadline = global_ns() + ex->timeout_ns;
     bool ok = true;
-    for (int idx = tid; idx < G * D; idx += kDecodeThreads) {
-        const int g = idx / D;
-        const int64_t row = row0 + g;
-        float M = flse[g];
-        float lp[kMaxRanks];
+    // (1) every rank's lse of the group's rows, one cell per thread
+    for (int c = tid; c < world * G; c += kDecodeThreads) {
+        const int p = c / G, g = c - p * G;
+        float v = flse[g];
+        if (p != rank) {
+            const uint2* cp = ex->recv_lse[rank] + (par + p) * rows + row0 + g;
+            const uint2 cell = ld_cell(cp);
+            if (cell.y == step) v = __uint_as_float(cell.x);
+            else if (!wait_cell(cp, step, deadline, &v)) ok = false;
+        }
+        wgt[p * 16 + g] = v;
+    }
+    if (!ok) *flag_s = 1;
+    __syncthreads();
+    if (tid < G) {
+        float M = -INFINITY;
+        for (int p = 0; p < world; ++p) M = fmaxf(M, wgt[p * 16 + tid]);
+        float dsum = 0.f;
         for (int p = 0; p < world; ++p) {
-            if (p == rank) {
-                lp[p] = flse[g];
-                continue;
+            const float w = (M == -INFINITY) ? 0.f : __expf(wgt[p * 16 + tid] - M);
+            wgt[p * 16 + tid] = w;
+            dsum += w;
+        }
+        den[tid] = dsum;
+        mx[tid] = M;
+    }
+    __syncthreads();
+    ok = !*flag_s;
+    // (2) the output cells: KB outputs of this thread x every other rank, loaded at once
+    constexpr int KB = 4;
+    for (int base = tid; base < G * D; base += KB * kDecodeThreads) {
+        uint2 cell[KB][kMaxRanks];
+#pragma unroll
+        for (int k = 0; k < KB; ++k) {
+            const int idx = base + k * kDecodeThreads;
+#pragma unroll
+            for (int p = 0; p < kMaxRanks; ++p) {
+                cell[k][p] = make_uint2(0u, step);
+                if (ok && idx < G * D && p < world && p != rank)
+                    cell[k][p] = ld_cell(ex->recv_o[rank] + ((par + p) * rows + row0) * D + idx);
             }
-            float v = -INFINITY;
-            if (ok) ok = wait_cell(ex->recv_lse[rank] + (par + p) * rows + row, step, deadline, &v);
-            lp[p] = v;
-            M = fmaxf(M, v);
         }
-        float num = 0.f, den = 0.f;
-        for (int p = 0; p < world; ++p) {
-            const float w = (M == -INFINITY) ? 0.f : __expf(lp[p] - M);
-            float o = fin[idx];
-            if (p != rank && ok)
-                ok = wait_cell(ex->recv_o[rank] + ((par + p) * rows + row0) * D + idx, step,
-                               deadline, &o);
-            num += w * o;
-            den += w;
+#pragma unroll
+        for (int k = 0; k < KB; ++k) {
+            const int idx = base + k * kDecodeThreads;
+            if (idx >= G * D) break;
+            const int g = idx / D, d = idx - g * D;
+            float num = 0.f;
+#pragma unroll
+            for (int p = 0; p < kMaxRanks; ++p) {
+                if (p >= world) break;
+                float o = fin[idx];
+                if (p != rank) {
+                    if (cell[k][p].y == step) {
+                        o = __uint_as_float(cell[k][p].x);
+                    } else if (ok) {
+                        ok = wait_cell(ex->recv_o[rank] + ((par + p) * rows + row0) * D + idx,
+                                       step, deadline, &o);
+                    }
+                }
+                num += wgt[p * 16 + g] * o;
+            }
+            const float dn = den[g];
+            const float ov = (!ok || !(dn > 0.f)) ? 0.f : num / dn;
+            const int64_t row = row0 + g;
+            if (a.out_f32)
+                static_cast<float*>(a.out)[row * D + d] = ov;
+            else
+                static_cast<T*>(a.out)[row * D + d] = from_f32<T>(ov);
+            if (d == 0 && a.lse)
+                a.lse[row] = (!ok || !(dn > 0.f)) ? -INFINITY : mx[g] + logf(dn);
         }
-        const float ov = (!ok || !(den > 0.f)) ? 0.f : num / den;
-        if (a.out_f32)
-            static_cast<float*>(a.out)[row * D + (idx - g * D)] = ov;
-        else
-            static_cast<T*>(a.out)[row * D + (idx - g * D)] = from_f32<T>(ov);
-        if (idx - g * D == 0 && a.lse)
-            a.lse[row] = (!ok || !(den > 0.f)) ? -INFINITY : M + logf(den);
     }
     if (!ok) {
         atomicExch(ex->status, TMLLM_TIMEOUT);
@@ -1107,9 +1154,12 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? kD64MinBlocks : 2) d
         }
     }
     if (splits_b == 1) {
-        if (a.ex) {
-            __syncthreads();
-            exchange_tail<__half>(a, fin, flse, G, D, qh0, flag_s);
+        if constexpr (!PT) {  // the positions-major form never runs with the exchange
+            if (a.ex) {
+                __syncthreads();
+                exchange_tail<__half>(a, fin, flse, G, D, qh0, flag_s,
+                                      reinterpret_cast<float*>(smem));
+            }
         }
         return;
     }
@@ -1193,9 +1243,12 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? kD64MinBlocks : 2) d
         if (d == 0 && a.lse) a.lse[qh0 + g] = lv;
     }
     if (tid == 0) a.counters[static_cast<int64_t>(b) * a.kv_heads + kvh] = 0;
-    if (a.ex) {
-        __syncthreads();
-        exchange_tail<__half>(a, fin, flse, G, D, qh0, flag_s);
+    if constexpr (!PT) {
+        if (a.ex) {  // the rings are free: their start is the exchange's scratch
+            __syncthreads();
+            exchange_tail<__half>(a, fin, flse, G, D, qh0, flag_s,
+                                  reinterpret_cast<float*>(smem));
+        }
     }
 }
 
