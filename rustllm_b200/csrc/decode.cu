@@ -1399,6 +1399,41 @@ __global__ void merge_lse_kernel(const float* __restrict__ po, const float* __re
     if (threadIdx.x == 0 && out_lse) out_lse[r] = den > 0.f ? M + logf(den) : -INFINITY;
 }
 
+// The same merge with one warp per row and 16-byte loads (parts 16-byte aligned, D and the
+// part stride multiples of 4 floats, at most 32 parts): lane p holds part p's lse, the
+// weights travel by shuffle, and each lane accumulates 4 consecutive dims of every part.
+template <typename OutT>
+__global__ void __launch_bounds__(128) merge_lse_vec_kernel(
+    const float* __restrict__ po, const float* __restrict__ pl, int n, int rows, int D,
+    int64_t os, int64_t ls, OutT* __restrict__ out, float* __restrict__ out_lse) {
+    const int r = blockIdx.x * 4 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;  // warp-uniform
+    const float lp = lane < n ? pl[lane * ls + r] : -INFINITY;
+    const float M = warp_max(lp);
+    const float w = (M == -INFINITY || lane >= n) ? 0.f : expf(lp - M);
+    const float den = warp_sum(w);
+    for (int d4 = lane; d4 < D / 4; d4 += 32) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (int p = 0; p < n; ++p) {
+            const float wp = __shfl_sync(0xffffffffu, w, p);
+            const float4 v = __ldg(reinterpret_cast<const float4*>(
+                po + p * os + static_cast<int64_t>(r) * D + 4 * d4));
+            acc.x += wp * v.x;
+            acc.y += wp * v.y;
+            acc.z += wp * v.z;
+            acc.w += wp * v.w;
+        }
+        OutT* o = out + static_cast<int64_t>(r) * D + 4 * d4;
+        o[0] = from_f32<OutT>(den > 0.f ? acc.x / den : 0.f);
+        o[1] = from_f32<OutT>(den > 0.f ? acc.y / den : 0.f);
+        o[2] = from_f32<OutT>(den > 0.f ? acc.z / den : 0.f);
+        o[3] = from_f32<OutT>(den > 0.f ? acc.w / den : 0.f);
+    }
+    if (lane == 0 && out_lse) out_lse[r] = den > 0.f ? M + logf(den) : -INFINITY;
+}
+
 // ---- launch plumbing -------------------------------------------------------------------
 
 // Opts `fn` into `bytes` of dynamic shared memory on the current device, once per device
@@ -1819,6 +1854,19 @@ int tmllm_merge_lse(const float* parts_o, const float* parts_lse, int32_t num_pa
     if (os < static_cast<int64_t>(rows) * head_dim || ls < rows)
         return fail(TMLLM_INVALID_SHAPE, "merge strides overlap the parts");
     auto s = reinterpret_cast<cudaStream_t>(stream);
+    if (num_parts <= 32 && head_dim % 4 == 0 && os % 4 == 0 && aligned16(parts_o)) {
+        const unsigned blocks = static_cast<unsigned>((rows + 3) / 4);
+        if (out_dtype == TMLLM_F16)
+            merge_lse_vec_kernel<__half><<<blocks, 128, 0, s>>>(
+                parts_o, parts_lse, num_parts, rows, head_dim, os, ls, static_cast<__half*>(out),
+                out_lse);
+        else
+            merge_lse_vec_kernel<float><<<blocks, 128, 0, s>>>(
+                parts_o, parts_lse, num_parts, rows, head_dim, os, ls, static_cast<float*>(out),
+                out_lse);
+        TMLLM_LAUNCH_TRY();
+        return TMLLM_OK;
+    }
     const int threads = head_dim >= 128 ? 128 : 64;
     if (out_dtype == TMLLM_F16)
         merge_lse_kernel<__half><<<rows, threads, 0, s>>>(parts_o, parts_lse, num_parts, rows,

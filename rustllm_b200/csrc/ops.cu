@@ -169,6 +169,29 @@ __global__ void scale_mask_kernel(const T* __restrict__ in, T* __restrict__ out,
     }
 }
 
+// The same with one 16-byte chunk per thread (key_len a multiple of the chunk's elements,
+// 16-byte aligned tensors): the row of a chunk is found once, not per element.
+template <typename T>
+__global__ void scale_mask_vec_kernel(const T* __restrict__ in, T* __restrict__ out,
+                                      float scale, int64_t query_len, int64_t key_len,
+                                      int64_t start, int64_t chunks) {
+    constexpr int EPC = 16 / sizeof(T);
+    const int64_t cpr = key_len / EPC;  // chunks per row
+    for (int64_t id = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; id < chunks;
+         id += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t row = id / cpr;
+        const int64_t key0 = (id - row * cpr) * EPC;
+        const int64_t lim = start + row % query_len;  // keys > lim are masked
+        uint4 raw = __ldg(reinterpret_cast<const uint4*>(in) + id);
+        T* e = reinterpret_cast<T*>(&raw);
+#pragma unroll
+        for (int k = 0; k < EPC; ++k)
+            e[k] = key0 + k > lim ? from_f32<T>(-INFINITY)
+                                  : from_f32<T>(__fmul_rn(to_f32<T>(e[k]), scale));
+        reinterpret_cast<uint4*>(out)[id] = raw;
+    }
+}
+
 // kernels/softmax.metal: one 256-thread block per row; element t, t+256, ... folded by
 // thread t, then a halving tree over the 256 partials (the reference's order).
 template <typename T, bool kZeroMaskedRow>
@@ -406,6 +429,20 @@ int tmllm_attention_scale_mask(tmllm_dtype dtype, const void* in, void* out, siz
     if (!in || !out) return fail(TMLLM_INVALID_ARGUMENT, "null tensor pointer");
     auto s = reinterpret_cast<cudaStream_t>(stream);
     int64_t total = static_cast<int64_t>(numel);
+    const int64_t epc = dtype == TMLLM_F16 ? 8 : 4;
+    if (static_cast<int64_t>(key_len) % epc == 0 && aligned16(in) && aligned16(out)) {
+        const int64_t chunks = total / epc;
+        if (dtype == TMLLM_F16)
+            scale_mask_vec_kernel<__half><<<grid_for(chunks), kThreads, 0, s>>>(
+                static_cast<const __half*>(in), static_cast<__half*>(out), scale, query_len,
+                key_len, query_start_pos, chunks);
+        else
+            scale_mask_vec_kernel<float><<<grid_for(chunks), kThreads, 0, s>>>(
+                static_cast<const float*>(in), static_cast<float*>(out), scale, query_len,
+                key_len, query_start_pos, chunks);
+        TMLLM_LAUNCH_TRY();
+        return TMLLM_OK;
+    }
     if (dtype == TMLLM_F16)
         scale_mask_kernel<__half><<<grid_for(total), kThreads, 0, s>>>(
             static_cast<const __half*>(in), static_cast<__half*>(out), scale, query_len, key_len,

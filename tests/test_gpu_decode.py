@@ -274,16 +274,27 @@ def test_raw_entry_point_over_caller_tensors(cuda, orc):
     assert np.array_equal(bits(k_ar[blk, :, off].cpu().numpy()), bits(kn[0]))
 
 
-def test_merge_lse_kernel(cuda, orc):
-    rng = np.random.default_rng(13)
-    n, rows, d = 5, 32, 128
+@pytest.mark.parametrize("n,rows,d,out_dtype", [
+    (5, 32, 128, torch.float32),   # warp per row, 16-byte loads
+    (8, 37, 64, torch.float16),    # rows not a multiple of the 4 rows of a block, F16 out
+    (33, 9, 128, torch.float32),   # more parts than a warp's lanes: one block per row
+    (3, 10, 66, torch.float32),    # D not a multiple of 4 floats: one block per row
+])
+def test_merge_lse_kernel(cuda, orc, n, rows, d, out_dtype):
+    rng = np.random.default_rng(13 + n + d)
     po = rng.standard_normal((n, rows, d)).astype(np.float32)
     pl = (rng.standard_normal((n, rows)) * 3).astype(np.float32)
+    pl[0, 1] = -np.inf  # a part that saw no key
+    pl[:, 2] = -np.inf  # a row no part saw: zeros and -inf
     want, wlse = orc.merge_lse(po, pl)
     lse = torch.empty(rows, dtype=torch.float32, device=cuda)
-    got = rb.merge_lse(torch.from_numpy(po).to(cuda), torch.from_numpy(pl).to(cuda), out_lse=lse)
-    assert rel(got.cpu().numpy(), want) < 1e-5
-    assert np.max(np.abs(lse.cpu().numpy() - wlse)) < 1e-4
+    got = rb.merge_lse(torch.from_numpy(po).to(cuda), torch.from_numpy(pl).to(cuda),
+                       out_dtype=out_dtype, out_lse=lse)
+    tol = 1e-5 if out_dtype == torch.float32 else 2e-3
+    finite = np.isfinite(wlse)
+    assert rel(got.float().cpu().numpy()[finite], want[finite]) < tol
+    assert np.max(np.abs(lse.cpu().numpy()[finite] - wlse[finite])) < 1e-4
+    assert not got.float()[2].any() and lse[2].item() == -np.inf
 
 
 def test_decode_rejects_full_cache_without_mutation(cuda):

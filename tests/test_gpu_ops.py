@@ -104,10 +104,12 @@ def test_gqa_qk_pv_bit_exact(cuda, orc, dtype):
 @pytest.mark.parametrize("dtype", DT)
 def test_scale_mask_and_bmm_bit_exact(cuda, orc, dtype):
     rng = np.random.default_rng(5)
-    s = rnd(rng, (2, 3, 4, 9), dtype) * 5
-    for start in (0, 3, 5):
-        got = n(rb.attention_scale_mask(t(s, cuda), 0.125, start))
-        assert np.array_equal(bits(got), bits(orc.attention_scale_mask(s, 0.125, start)))
+    # key lengths that are not (9) and are (16, 40) whole 16-byte chunks: both kernels
+    for shape in ((2, 3, 4, 9), (2, 3, 4, 16), (1, 2, 5, 40)):
+        s = rnd(rng, shape, dtype) * 5
+        for start in (0, 3, shape[-1] - shape[-2]):
+            got = n(rb.attention_scale_mask(t(s, cuda), 0.125, start))
+            assert np.array_equal(bits(got), bits(orc.attention_scale_mask(s, 0.125, start)))
     a, bm = rnd(rng, (3, 5, 7), dtype), rnd(rng, (3, 7, 11), dtype)
     assert np.array_equal(bits(n(rb.batched_matmul(t(a, cuda), t(bm, cuda)))),
                           bits(orc.batched_matmul(a, bm)))
