@@ -1176,7 +1176,23 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? kD64MinBlocks : 2) d
     float* lsp = wts + static_cast<int64_t>(nsplit) * 16;  // [splits_b][16]
     float* Ms = lsp + static_cast<int64_t>(nsplit) * 16;
     float* dens = Ms + 16;
-    // all (m, l) pairs of this (sequence, KV head) in one parallel round trip
+    // Each thread merges 4 consecutive dims of one head.  When all partial outputs fit in
+    // the free rings they are staged there with one burst of cp.async, issued before the
+    // (m, l) pairs are read, so both travel in one L2 round trip and the merge weights are
+    // computed while the outputs are in flight; otherwise they are read with one 16-byte
+    // L2 load per split.
+    const int64_t stride4 = static_cast<int64_t>(G) * D / 4;
+    const float4* src0 = reinterpret_cast<const float4*>(a.part_o + pbase * D);
+    const size_t stage_bytes = static_cast<size_t>(splits_b) * stride4 * 16;
+    const size_t stage_off = static_cast<size_t>(2 * nsplit * 16 + 32) * 4;
+    const bool staged = stage_off + stage_bytes <= static_cast<size_t>(Cfg::OFF_FIN);
+    float4* stage = reinterpret_cast<float4*>(smem + ((stage_off + 15) & ~static_cast<size_t>(15)));
+    if (staged) {
+        for (int64_t i = tid; i < splits_b * stride4; i += kDecodeThreads)
+            cp_async16(stage + i, src0 + i, 16);
+        cp_async_commit();
+    }
+    // all (m, l) pairs of this (sequence, KV head)
     for (int i = tid; i < splits_b * G; i += kDecodeThreads) {
         const int s2 = i / G, g = i - s2 * G;
         const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml) + pbase + i);
@@ -1196,23 +1212,8 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? kD64MinBlocks : 2) d
         Ms[tid] = M;
         dens[tid] = dsum;
     }
+    if (staged) cp_async_wait<0>();
     __syncthreads();
-    // each thread merges 4 consecutive dims of one head.  When all partial outputs fit in
-    // the free rings they are staged there with one burst of cp.async (a single L2 round
-    // trip); otherwise they are read with one 16-byte L2 load per split.
-    const int64_t stride4 = static_cast<int64_t>(G) * D / 4;
-    const float4* src0 = reinterpret_cast<const float4*>(a.part_o + pbase * D);
-    const size_t stage_bytes = static_cast<size_t>(splits_b) * stride4 * 16;
-    const size_t stage_off = static_cast<size_t>(2 * nsplit * 16 + 32) * 4;
-    const bool staged = stage_off + stage_bytes <= static_cast<size_t>(Cfg::OFF_FIN);
-    float4* stage = reinterpret_cast<float4*>(smem + ((stage_off + 15) & ~static_cast<size_t>(15)));
-    if (staged) {
-        for (int64_t i = tid; i < splits_b * stride4; i += kDecodeThreads)
-            cp_async16(stage + i, src0 + i, 16);
-        cp_async_commit();
-        cp_async_wait<0>();
-        __syncthreads();
-    }
     for (int idx = tid; idx < stride4; idx += kDecodeThreads) {
         const int g = idx / (D / 4), d = (idx - g * (D / 4)) * 4;
         float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
