@@ -35,6 +35,14 @@ constexpr int kDecodeThreads = 128;
 #endif
 constexpr int kD64Stages = TMLLM_D64_STAGES;
 constexpr int kD64MinBlocks = kD64Stages <= 3 ? 4 : (kD64Stages == 4 ? 3 : 2);
+// The positions-major kernel (head_dim 64, up to 8 query heads per KV head) consumes 32
+// positions (two 16-position sub-tiles) per softmax update; its ring holds this many such
+// items per warp.
+#ifndef TMLLM_D64_PT_STAGES
+#define TMLLM_D64_PT_STAGES 2
+#endif
+constexpr int kD64PtStages = TMLLM_D64_PT_STAGES;
+constexpr int kD64PtMinBlocks = kD64PtStages <= 2 ? 3 : 2;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -664,13 +672,14 @@ __device__ void exchange_tail(const DecodeArgs& a, const float* fin, const float
     }
 }
 
-template <int D, int STAGES>
+template <int D, int STAGES, int PS = 1>
 struct MmaCfg {
     static constexpr int C = D / 8;         // 16-byte chunks per row
     static constexpr int ROW = D * 2;       // bytes per row
     static constexpr int SUB = 16;          // positions per warp sub-tile
     static constexpr int SUBB = SUB * ROW;  // bytes of one K (or V) sub-tile
-    static constexpr int WARP_RING = STAGES * 2 * SUBB;
+    // a ring stage holds one item of PS sub-tiles: K sub-tiles, then V sub-tiles
+    static constexpr int WARP_RING = STAGES * 2 * SUBB * PS;
     static constexpr int QROW = D + 8;      // padded q row (halves)
     static constexpr int OFF_Q = 4 * WARP_RING;
     static constexpr int OFF_ST = OFF_Q + 16 * QROW * 2;  // m, l per warp x row + flag
@@ -691,8 +700,10 @@ struct MmaCfg {
 // head-major form (whose M = 16 rows carry only G real query heads): at short contexts the
 // loop is bound by a warp's per-sub-tile chain, not by memory bandwidth.
 template <int D, int STAGES, bool PT>
-__global__ void __launch_bounds__(kDecodeThreads, D == 64 ? kD64MinBlocks : 2) decode_mma_kernel(const DecodeArgs a) {
-    using Cfg = MmaCfg<D, STAGES>;
+__global__ void __launch_bounds__(kDecodeThreads, D == 64 ? (PT ? kD64PtMinBlocks : kD64MinBlocks) : 2)
+    decode_mma_kernel(const DecodeArgs a) {
+    constexpr int PS = PT ? 2 : 1;  // 16-position sub-tiles per item (one softmax update)
+    using Cfg = MmaCfg<D, STAGES, PS>;
     static_assert(!PT || D == 64, "the positions-major form is instantiated for D = 64");
     constexpr int C = Cfg::C, ROW = Cfg::ROW, SUBB = Cfg::SUBB, QROW = Cfg::QROW;
     constexpr int KS = D / 16;  // k-steps of QK
@@ -717,7 +728,10 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? kD64MinBlocks : 2) d
     // ahead of this one does not write; q, k_new and v_new are read after its completion.
     const bool whole_blocks = (a.block_size % 16) == 0;
     const int t0 = split * a.chunk;
-    // Block-table entry of this warp's sub-tile j (with whole blocks a sub-tile lies in one
+    // A warp takes items warp, warp + 4, ... of the chunk; item j holds PS sub-tiles, so
+    // sub-tile s of this warp (item s / PS, part s % PS) starts at position
+    // t0 + ((warp + 4 (s / PS)) PS + s % PS) 16.
+    // Block-table entry of this warp's sub-tile s (with whole blocks a sub-tile lies in one
     // block; out-of-table positions give -1).  At D = 64 (short sub-tiles, where a table
     // read per sub-tile left the ring waiting at short contexts) the entries sit 32 at a
     // time in the lanes: lane l holds the entry of sub-tile jb + l (`cur`) and of
@@ -725,9 +739,11 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? kD64MinBlocks : 2) d
     // on a table read; the first two batches depend on the chunk only and are read
     // together with the length.  At D = 128 the entry is read at issue (measured 1.5 %
     // faster there: fewer registers on the critical loop).
-    auto entry = [&](int j) -> int64_t {  // j may run past the chunk: 64-bit position
-        return whole_blocks ? block_of(a, b, static_cast<int64_t>(t0) + (warp + 4 * j) * 16)
-                            : -1;
+    auto sub_pos = [&](int sidx) -> int64_t {  // may run past the chunk: 64-bit position
+        return static_cast<int64_t>(t0) + ((warp + 4 * (sidx / PS)) * PS + sidx % PS) * 16;
+    };
+    auto entry = [&](int sidx) -> int64_t {
+        return whole_blocks ? block_of(a, b, sub_pos(sidx)) : -1;
     };
     constexpr bool kLaneTable = D == 64;
     int64_t cur = -1, nxt = -1;
@@ -743,14 +759,14 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? kD64MinBlocks : 2) d
     if (splits_b > nsplit) splits_b = nsplit;
     if (split >= splits_b) return;
     const int t1 = (split == splits_b - 1) ? L : min(L, t0 + a.chunk);
-    const int nsub = t1 > t0 ? (t1 - t0 + 15) / 16 : 0;
+    const int nitem = t1 > t0 ? (t1 - t0 + 16 * PS - 1) / (16 * PS) : 0;
     const bool owns_new = has_new && cached >= t0 && cached < t1;
     const int half = D / 2;
     const int qpos = cached + a.rope_off;
 
-    // ---- this warp's cp.async ring: sub-tiles warp, warp+4, ... of the chunk
+    // ---- this warp's cp.async ring: items warp, warp+4, ... of the chunk
     unsigned char* ring = smem + warp * Cfg::WARP_RING;
-    const int nmine = nsub > warp ? (nsub - warp + 3) / 4 : 0;
+    const int nmine = nitem > warp ? (nitem - warp + 3) / 4 : 0;
     const unsigned char* kbase = static_cast<const unsigned char*>(a.k_cache);
     const unsigned char* vbase = static_cast<const unsigned char*>(a.v_cache);
     const int lc = lane % C, lr0 = lane / C;
@@ -760,22 +776,20 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? kD64MinBlocks : 2) d
         const int r = lr0 + k * Cfg::RSTEP;
         dst_off[k] = r * ROW + swz<C>(r, lc) * 16;
     }
-    // called with warp-uniform j = 0, 1, 2, ... < nmine
+    // called with warp-uniform sub-tile indices 0, 1, 2, ... (items < nmine)
     int jb = 0;
-    auto sub_block = [&](int j) -> int64_t {
+    auto sub_block = [&](int sidx) -> int64_t {
         if (!kLaneTable)
-            return whole_blocks && j < nmine ? block_of(a, b, t0 + (warp + 4 * j) * 16) : -1;
-        if (j >= jb + 32) {
+            return whole_blocks && sidx / PS < nmine ? block_of(a, b, sub_pos(sidx)) : -1;
+        if (sidx >= jb + 32) {
             jb += 32;
             cur = nxt;
             nxt = entry(jb + 32 + lane);
         }
-        return __shfl_sync(0xffffffffu, cur, j - jb);
+        return __shfl_sync(0xffffffffu, cur, sidx - jb);
     };
-    auto load_sub = [&](int j, int stage, int64_t blk) {
-        unsigned char* ks = ring + stage * 2 * SUBB;
-        unsigned char* vs = ks + SUBB;
-        const int base = t0 + (warp + 4 * j) * 16;
+    // one 16-position sub-tile starting at `base` into ks / vs
+    auto load_sub = [&](int base, unsigned char* ks, unsigned char* vs, int64_t blk) {
         int64_t row0 = -1;  // arena row of position `base` when the sub-tile is one block
         if (whole_blocks) {
             if (blk >= 0)
@@ -819,9 +833,17 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? kD64MinBlocks : 2) d
             cp_async16(vs + dst_off[k], vsrc, bytes);
         }
     };
+    // item j (its PS sub-tiles) into ring stage `stage`
+    auto load_item = [&](int j, int stage) {
+        unsigned char* kst = ring + stage * 2 * PS * SUBB;
+#pragma unroll
+        for (int k = 0; k < PS; ++k)
+            load_sub(t0 + ((warp + 4 * j) * PS + k) * 16, kst + k * SUBB,
+                     kst + (PS + k) * SUBB, sub_block(j * PS + k));
+    };
 #pragma unroll
     for (int s = 0; s < STAGES - 1; ++s) {
-        if (s < nmine) load_sub(s, s, sub_block(s));
+        if (s < nmine) load_item(s, s);
         cp_async_commit();
     }
     if (a.overlap) grid_dependency_wait();  // q, k_new, v_new come from the kernel ahead
@@ -904,60 +926,80 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? kD64MinBlocks : 2) d
         __syncwarp();
         {
             const int nt = it + STAGES - 1;
-            if (nt < nmine) load_sub(nt, nt % STAGES, sub_block(nt));
+            if (nt < nmine) load_item(nt, nt % STAGES);
             cp_async_commit();
         }
-        unsigned char* ks = ring + (it % STAGES) * 2 * SUBB;
-        unsigned char* vs = ks + SUBB;
-        const int base = t0 + (warp + 4 * it) * 16;
-        if (owns_new && cached >= base && cached < base + 16) {
-            const int r = cached - base;
+        unsigned char* kst = ring + (it % STAGES) * 2 * PS * SUBB;  // K sub-tiles of the item
+        unsigned char* vst = kst + PS * SUBB;                        // then its V sub-tiles
+        const int base = t0 + (warp + 4 * it) * 16 * PS;
+        if (owns_new && cached >= base && cached < base + 16 * PS) {
+            const int rr = cached - base, kk = rr >> 4, r = rr & 15;
             if (lane < C) {
-                *reinterpret_cast<uint4*>(ks + r * ROW + swz<C>(r, lane) * 16) =
+                *reinterpret_cast<uint4*>(kst + kk * SUBB + r * ROW + swz<C>(r, lane) * 16) =
                     reinterpret_cast<const uint4*>(knew_s)[lane];
-                *reinterpret_cast<uint4*>(vs + r * ROW + swz<C>(r, lane) * 16) =
+                *reinterpret_cast<uint4*>(vst + kk * SUBB + r * ROW + swz<C>(r, lane) * 16) =
                     reinterpret_cast<const uint4*>(vnew_s)[lane];
             }
             __syncwarp();
         }
         if constexpr (PT) {
-            // S^T = K Q^T: A = K rows (positions) by ldmatrix, B = Q^T from registers; even
-            // and odd k-steps in separate accumulators.  st[e]: positions g4 (e < 2) and
-            // g4 + 8, heads 2t4 + (e & 1).
-            float st[4] = {0.f, 0.f, 0.f, 0.f}, sx[4] = {0.f, 0.f, 0.f, 0.f};
+            // S^T = K Q^T per sub-tile: A = K rows (positions) by ldmatrix, B = Q^T from
+            // registers; even and odd k-steps in separate accumulators, the PS sub-tiles'
+            // chains independent.  st[k][e]: sub-tile k, positions g4 (e < 2) and g4 + 8,
+            // heads 2t4 + (e & 1).
+            float st[PS][4], sx[PS][4];
+#pragma unroll
+            for (int k = 0; k < PS; ++k)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) st[k][e] = sx[k][e] = 0.f;
             {
                 const int mi = lane >> 3, r = (mi & 1) * 8 + (lane & 7);
-                const uint32_t rbase = smem_u32(ks + r * ROW);
 #pragma unroll
                 for (int kstep = 0; kstep < KS; ++kstep) {
-                    const int c = kstep * 2 + (mi >> 1);
-                    uint32_t a0, a1, a2, a3;
-                    ldsm_x4(rbase + swz<C>(r, c) * 16, a0, a1, a2, a3);
-                    mma16816((kstep & 1) ? sx : st, a0, a1, a2, a3, qa[kstep][0], qa[kstep][1]);
+#pragma unroll
+                    for (int k = 0; k < PS; ++k) {
+                        const uint32_t rbase = smem_u32(kst + k * SUBB + r * ROW);
+                        const int c = kstep * 2 + (mi >> 1);
+                        uint32_t a0, a1, a2, a3;
+                        ldsm_x4(rbase + swz<C>(r, c) * 16, a0, a1, a2, a3);
+                        mma16816((kstep & 1) ? sx[k] : st[k], a0, a1, a2, a3, qa[kstep][0],
+                                 qa[kstep][1]);
+                    }
                 }
             }
-            const bool full = base + 16 <= t1;
+            const bool full = base + 16 * PS <= t1;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                float v = (st[e] + sx[e]) * a.scale_log2;
-                if (!full && base + g4 + (e >= 2 ? 8 : 0) >= t1) v = -INFINITY;
-                st[e] = v;
-            }
-            // online softmax per head over the 16 positions (8 lanes of equal t4 x 2 rows)
+            for (int k = 0; k < PS; ++k)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    float v = (st[k][e] + sx[k][e]) * a.scale_log2;
+                    if (!full && base + 16 * k + g4 + (e >= 2 ? 8 : 0) >= t1) v = -INFINITY;
+                    st[k][e] = v;
+                }
+            // one online-softmax update per head over the item's 16 PS positions (8 lanes of
+            // equal t4 x 2 rows x PS sub-tiles)
             float alpha[2];
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                float mx = fmaxf(st[h], st[2 + h]);
+                float mx = fmaxf(st[0][h], st[0][2 + h]);
+#pragma unroll
+                for (int k = 1; k < PS; ++k) mx = fmaxf(mx, fmaxf(st[k][h], st[k][2 + h]));
                 mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
                 mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
                 mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
                 const float m_new = fmaxf(m_r[h], mx);
                 const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
                 alpha[h] = fast_exp2(m_r[h] - m_use);
-                const float p0 = fast_exp2(st[h] - m_use), p1 = fast_exp2(st[2 + h] - m_use);
-                st[h] = p0;
-                st[2 + h] = p1;
-                l_r[h] = l_r[h] * alpha[h] + (p0 + p1);
+                float sum = 0.f;
+#pragma unroll
+                for (int k = 0; k < PS; ++k) {
+                    const float p0 = fast_exp2(st[k][h] - m_use);
+                    const float p1 = fast_exp2(st[k][2 + h] - m_use);
+                    st[k][h] = p0;
+                    st[k][2 + h] = p1;
+                    sum += p0 + p1;
+                }
+                l_r[h] = l_r[h] * alpha[h] + sum;
                 m_r[h] = m_new;
             }
             if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
@@ -969,25 +1011,35 @@ __global__ void __launch_bounds__(kDecodeThreads, D == 64 ? kD64MinBlocks : 2) d
                     o[mt][3] *= alpha[1];
                 }
             }
-            // P^T as the B operand: the 8 x 8 blocks (positions 0-7 | 8-15) x heads of the
-            // accumulator layout, transposed across the warp
-            uint32_t pb0, pb1;
-            const uint32_t pk0 = pack_half2(st[0], st[1]), pk1 = pack_half2(st[2], st[3]);
-            asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(pb0) : "r"(pk0));
-            asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(pb1) : "r"(pk1));
-            // O^T += V^T P^T: A = V^T (dims x positions) by ldmatrix.trans of the V rows
+            // P^T of each sub-tile as a B operand: the 8 x 8 blocks (positions 0-7 | 8-15) x
+            // heads of the accumulator layout, transposed across the warp
+            uint32_t pb[PS][2];
+#pragma unroll
+            for (int k = 0; k < PS; ++k) {
+                const uint32_t pk0 = pack_half2(st[k][0], st[k][1]);
+                const uint32_t pk1 = pack_half2(st[k][2], st[k][3]);
+                asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(pb[k][0]) : "r"(pk0));
+                asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(pb[k][1]) : "r"(pk1));
+            }
+            // O^T += V^T P^T over the item's sub-tiles: A = V^T (dims x positions) by
+            // ldmatrix.trans of the V rows
             {
                 const int mi = lane >> 3, r = (mi >> 1) * 8 + (lane & 7);
-                const uint32_t rbase = smem_u32(vs + r * ROW);
 #pragma unroll
                 for (int mt = 0; mt < NO; ++mt) {
-                    const int c = mt * 2 + (mi & 1);
-                    uint32_t a0, a1, a2, a3;
-                    ldsm_x4_t(rbase + swz<C>(r, c) * 16, a0, a1, a2, a3);
-                    mma16816(o[mt], a0, a1, a2, a3, pb0, pb1);
+#pragma unroll
+                    for (int k = 0; k < PS; ++k) {
+                        const uint32_t rbase = smem_u32(vst + k * SUBB + r * ROW);
+                        const int c = mt * 2 + (mi & 1);
+                        uint32_t a0, a1, a2, a3;
+                        ldsm_x4_t(rbase + swz<C>(r, c) * 16, a0, a1, a2, a3);
+                        mma16816(o[mt], a0, a1, a2, a3, pb[k][0], pb[k][1]);
+                    }
                 }
             }
         } else {
+            unsigned char* ks = kst;  // PS = 1: the item is one sub-tile
+            unsigned char* vs = vst;
             // S = Q K^T: two n-tiles of 8 positions, even/odd k-steps in separate accumulators
             float sc[2][4], sx[2][4];
     #pragma unroll
@@ -1499,7 +1551,7 @@ int launch_tiled(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
 
 template <int D, int STAGES, bool PT = false>
 int launch_mma(const DecodeArgs& a, dim3 grid, cudaStream_t s) {
-    using Cfg = MmaCfg<D, STAGES>;
+    using Cfg = MmaCfg<D, STAGES, PT ? 2 : 1>;
     auto* fn = decode_mma_kernel<D, STAGES, PT>;
     const size_t bytes = static_cast<size_t>(Cfg::BYTES);
     if ((2 * static_cast<size_t>(grid.z) + 2) * 16 * 4 > static_cast<size_t>(Cfg::OFF_FIN))
@@ -1541,7 +1593,7 @@ int launch_decode(int dtype, int D, int variant, const DecodeArgs& a, dim3 grid,
     *done = true;
     if (dtype == TMLLM_F16 && a.group <= 16 && variant != 1) {
         if (D == 64 && a.group <= 8 && a.ex == nullptr)
-            return launch_mma<64, kD64Stages, true>(a, grid, s);
+            return launch_mma<64, kD64PtStages, true>(a, grid, s);
         if (D == 64) return launch_mma<64, kD64Stages>(a, grid, s);
         if (D == 128) return launch_mma<128, 3>(a, grid, s);
     }
@@ -1767,6 +1819,7 @@ int32_t decode_auto_splits_bound(int64_t B, int64_t Hkv) { return auto_splits_bo
 
 // Resident CTAs per SM of the decode kernel that runs for this configuration.
 int decode_resident_ctas(int dtype, int head_dim, int variant, int group) {
+    if (dtype == TMLLM_F16 && head_dim == 64 && variant != 1 && group <= 8) return kD64PtMinBlocks;
     if (dtype == TMLLM_F16 && head_dim == 64 && variant != 1 && group <= 16) return kD64MinBlocks;
     return 2;
 }
