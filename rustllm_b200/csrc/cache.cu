@@ -21,8 +21,13 @@ int decode_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, cons
                 cudaStream_t stream);
 size_t decode_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t splits);
 int32_t decode_auto_splits(int64_t B, int64_t Hkv, int64_t max_len);
-int32_t decode_auto_splits_lens(const int64_t* lens, int64_t B, int64_t Hkv, int64_t hint,
-                                int per_sm);
+int64_t decode_auto_chunk_lens(const int64_t* lens, int64_t B, int64_t Hkv, int64_t hint,
+                               int per_sm);
+int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
+                   const void* v_new, void* out, float* lse, int32_t q_heads,
+                   const tmllm_decode_opts* opts, void* workspace, size_t workspace_bytes,
+                   int64_t max_len_hint, const ExchangeArgs* ex, uint32_t epoch,
+                   bool clear_tickets, cudaStream_t stream, int64_t chunk_override = 0);
 int decode_resident_ctas(int dtype, int head_dim, int variant, int group);
 int prefill_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, const void* v_new,
                  const int32_t* q_start, int32_t rows_per_seq, int32_t max_rows,
@@ -495,18 +500,25 @@ int tmllm_cache_decode(tmllm_cache* cache, int32_t layer, const void* q, const v
                 return fail_position(pos, 1, o.rope_len);  // rope.rs:121-127
         }
     }
+    // a caller that knows lengths will grow (a captured graph replayed for several steps)
+    // may ask for splits sized for the longest length it will see
+    const int64_t hint = std::max<int64_t>(max_len, o.max_len_hint);
     int32_t splits = o.num_splits;
+    int64_t chunk = 0;
     if (splits <= 0) {
-        // resident CTAs per SM of the kernel that will run
+        // positions per split from every sequence's length and the resident CTAs per SM of
+        // the kernel that will run; the split count follows from the longest length
         const int G = q_heads / cache->cfg.num_kv_heads;
         const int per_sm = decode_resident_ctas(cache->cfg.dtype, cache->cfg.head_dim,
                                                 o.variant, G);
         std::vector<int64_t> lens(cache->h_lens.begin(), cache->h_lens.end());
         if (append)
             for (auto& x : lens) ++x;
-        splits = decode_auto_splits_lens(lens.data(), cache->cfg.num_seqs,
-                                         cache->cfg.num_kv_heads,
-                                         std::max<int64_t>(max_len, o.max_len_hint), per_sm);
+        chunk = decode_auto_chunk_lens(lens.data(), cache->cfg.num_seqs,
+                                       cache->cfg.num_kv_heads, hint, per_sm);
+        int64_t s2 = (hint + chunk - 1) / chunk;
+        if (s2 > 1024) s2 = 1024;
+        splits = static_cast<int32_t>(s2 < 1 ? 1 : s2);
     }
     o.num_splits = splits;
     const size_t need = decode_workspace_bytes(cache->cfg.num_seqs, q_heads,
@@ -530,11 +542,8 @@ int tmllm_cache_decode(tmllm_cache* cache, int32_t layer, const void* q, const v
     // ahead of the decode, which an overlapped launch would read before that kernel ends:
     // such a call launches plainly.
     if (need_total > 0) o.flags &= ~TMLLM_DECODE_OVERLAP;
-    // a caller that knows lengths will grow (a captured graph replayed for several steps)
-    // may ask for splits sized for the longest length it will see
-    const int64_t hint = std::max<int64_t>(max_len, o.max_len_hint);
-    return decode_impl(&view, q, k_new, v_new, out, lse, q_heads, &o, cache->ws, cache->ws_bytes,
-                       hint, s);
+    return decode_impl_ex(&view, q, k_new, v_new, out, lse, q_heads, &o, cache->ws,
+                          cache->ws_bytes, hint, nullptr, 0, false, s, chunk);
 }
 
 int tmllm_cache_prefill(tmllm_cache* cache, int32_t layer, const void* q, const void* k_new,

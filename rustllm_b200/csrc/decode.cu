@@ -1643,7 +1643,7 @@ int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
                    const void* v_new, void* out, float* lse, int32_t q_heads,
                    const tmllm_decode_opts* opts, void* workspace, size_t workspace_bytes,
                    int64_t max_len_hint, const ExchangeArgs* ex, uint32_t epoch,
-                   bool clear_tickets, cudaStream_t stream);
+                   bool clear_tickets, cudaStream_t stream, int64_t chunk_override = 0);
 
 int decode_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, const void* v_new,
                 void* out, float* lse, int32_t q_heads, const tmllm_decode_opts* opts,
@@ -1656,12 +1656,14 @@ int decode_impl(const tmllm_paged_kv* kv, const void* q, const void* k_new, cons
 // `ex` (device-resident) makes the launch finish a sequence split across GPUs: the final
 // rows are exchanged with every rank and merged (tensor-core kernel only).  With
 // `clear_tickets` the split tickets in the workspace are zeroed on `stream` right before
-// the launch (only when the call passed every check and uses splits).
+// the launch (only when the call passed every check and uses splits).  `chunk_override`
+// > 0 sets the positions per split directly (rounded up to 128; the split count follows
+// from the longest length), instead of deriving them from opts->num_splits.
 int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
                    const void* v_new, void* out, float* lse, int32_t q_heads,
                    const tmllm_decode_opts* opts, void* workspace, size_t workspace_bytes,
                    int64_t max_len_hint, const ExchangeArgs* ex, uint32_t epoch,
-                   bool clear_tickets, cudaStream_t stream) {
+                   bool clear_tickets, cudaStream_t stream, int64_t chunk_override) {
     if (!kv) return fail(TMLLM_INVALID_ARGUMENT, "null paged KV descriptor");
     if (!valid_dtype(kv->dtype)) return fail(TMLLM_UNSUPPORTED_DTYPE, "unknown cache dtype");
     const int D = kv->head_dim, Hkv = kv->num_kv_heads, B = kv->num_seqs;
@@ -1709,6 +1711,13 @@ int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
     int32_t splits = o.num_splits > 0 ? o.num_splits : auto_splits(B, Hkv, hint);
     if (splits > 1024) splits = 1024;
     int64_t chunk = (hint + splits - 1) / splits;
+    if (chunk_override > 0) {
+        chunk = chunk_override;
+        int64_t s2 = (hint + ((chunk + 127) / 128) * 128 - 1) / (((chunk + 127) / 128) * 128);
+        if (s2 < 1) s2 = 1;
+        if (s2 > 1024) s2 = 1024;
+        splits = static_cast<int32_t>(s2);
+    }
     chunk = ((chunk + 127) / 128) * 128;
     if (chunk < 128) chunk = 128;
     if (chunk > INT32_MAX) chunk = INT32_MAX;
@@ -1829,6 +1838,41 @@ int decode_resident_ctas(int dtype, int head_dim, int variant, int group) {
 // it from `hint` -- still fit one wave of resident CTAs (`per_sm` per SM), so the long
 // sequences of a mixed batch are cut without pushing work into a second wave.  The CTA
 // count grows with the split count, so the largest fitting count is found by bisection.
+// Positions per split for a batch whose lengths the host knows: the smallest multiple of
+// 128 whose CTAs -- ceil(len / chunk) per sequence and KV head -- fit one wave of resident
+// CTAs (`per_sm` per SM), so only the sequences longer than the chunk are cut and no work
+// spills into a second wave.  The same floors as the split-count choice below: never under
+// 256 positions, and >= 1024 once one CTA per (sequence, KV head) covers every SM.  Finer
+// than choosing a split count (chunk = ceil(longest / s)): 64 sequences of 256-2048
+// positions x 5 KV heads at 3 CTAs per SM fit chunks of 1408 (435 CTAs), where 2 splits
+// (chunks of 1152) would need a second wave.  Returns the chunk, or the longest length
+// rounded up when even one chunk per sequence overflows the wave.
+int64_t decode_auto_chunk_lens(const int64_t* lens, int64_t B, int64_t Hkv, int64_t hint,
+                               int per_sm) {
+    const int64_t slots = static_cast<int64_t>(device_sm_count()) * per_sm;
+    if (hint < 1) hint = 1;
+    auto ctas = [&](int64_t chunk) {
+        int64_t n = 0;
+        for (int64_t b = 0; b < B; ++b) {
+            const int64_t L = lens[b] > 0 ? lens[b] : 1;
+            n += (L + chunk - 1) / chunk;
+        }
+        return n * Hkv;
+    };
+    int64_t hi = (hint + 127) / 128;  // in units of 128 positions
+    int64_t lo = 2;                   // never under 256 positions
+    if (B * Hkv >= static_cast<int64_t>(device_sm_count())) lo = 8;  // >= 1024
+    if (hint > 1024 * 128 * 1024) lo = (hint / 1024 + 127) / 128;    // at most 1024 splits
+    if (lo > hi) lo = hi;
+    if (ctas(hi * 128) > slots) return hi * 128;
+    while (lo < hi) {  // smallest k in [lo, hi] with ctas(128 k) <= slots
+        const int64_t mid = (lo + hi) / 2;
+        if (ctas(mid * 128) <= slots) hi = mid;
+        else lo = mid + 1;
+    }
+    return lo * 128;
+}
+
 int32_t decode_auto_splits_lens(const int64_t* lens, int64_t B, int64_t Hkv, int64_t hint,
                                 int per_sm) {
     const int64_t slots = static_cast<int64_t>(device_sm_count()) * per_sm;

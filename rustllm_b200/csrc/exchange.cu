@@ -13,7 +13,7 @@ int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
                    const void* v_new, void* out, float* lse, int32_t q_heads,
                    const tmllm_decode_opts* opts, void* workspace, size_t workspace_bytes,
                    int64_t max_len_hint, const ExchangeArgs* ex, uint32_t epoch,
-                   bool clear_tickets, cudaStream_t stream);
+                   bool clear_tickets, cudaStream_t stream, int64_t chunk_override = 0);
 }
 
 using namespace tmllm;
