@@ -371,39 +371,73 @@ def run_ours(args) -> None:
 
     # e2e through the public API with host buffers: the step's q, k_new and v_new live in
     # one pinned host buffer (one host-to-device copy per step, views on the device side);
-    # out comes back to pinned host memory
+    # out comes back to pinned host memory.  Two forms, both with every copy inside the
+    # timed region: serial (copy in, kernel, copy out on one stream) and pipelined, as a
+    # serving loop runs it: two device buffer sets, the next step's input copy on a copy
+    # stream while this step's kernel runs, this step's read-back on a third stream while
+    # the next kernel runs.
     nq, nk = HQ * D, HKV * D
-    hin = torch.randn((nq + 2 * nk,)).half().pin_memory()
-    hout = torch.empty((1, HQ, D), dtype=torch.float16).pin_memory()
-    din = torch.empty((nq + 2 * nk,), dtype=torch.float16, device=dev)
-    dq = din[:nq].view(1, HQ, D)
-    dk = din[nq:nq + nk].view(1, HKV, D)
-    dv = din[nq + nk:].view(1, HKV, D)
+    hin = [torch.randn((nq + 2 * nk,)).half().pin_memory() for _ in range(2)]
+    hout = [torch.empty((1, HQ, D), dtype=torch.float16).pin_memory() for _ in range(2)]
+    din = [torch.empty((nq + 2 * nk,), dtype=torch.float16, device=dev) for _ in range(2)]
+    dout = [out] + [torch.empty_like(out)]
+    views = [(x[:nq].view(1, HQ, D), x[nq:nq + nk].view(1, HKV, D),
+              x[nq + nk:].view(1, HKV, D)) for x in din]
     e_steps = max(1, min(args.steps, 2000))
+    s_in = torch.cuda.Stream(device=dev)
+    s_out = torch.cuda.Stream(device=dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]    # input copy into set b done
+    ev_k = [torch.cuda.Event() for _ in range(2)]     # kernel that read set b done
+    ev_out = [torch.cuda.Event() for _ in range(2)]   # read-back of set b done
+    for b in range(2):
+        ev_k[b].record(stream)
+        ev_out[b].record(stream)
 
-    def e2e_step():
-        din.copy_(hin, non_blocking=True)
-        sp.step(dq, dk, dv, out)
-        hout.copy_(out, non_blocking=True)
+    def e2e_serial():
+        din[0].copy_(hin[0], non_blocking=True)
+        sp.step(*views[0], dout[0])
+        hout[0].copy_(dout[0], non_blocking=True)
 
-    for _ in range(3):
-        e2e_step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e_steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_tok_s = 1000.0 * e_steps / float(te[0])
-    h2d = hin.numel() * 2
-    d2h = hout.numel() * 2
+    def e2e_pipelined(i):
+        b = i & 1
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_k[b])             # the kernel that last read set b is done
+            din[b].copy_(hin[b], non_blocking=True)
+            ev_in[b].record(s_in)
+        stream.wait_event(ev_in[b])
+        stream.wait_event(ev_out[b])             # set b's previous result is on the host
+        sp.step(*views[b], dout[b])
+        ev_k[b].record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_k[b])
+            hout[b].copy_(dout[b], non_blocking=True)
+            ev_out[b].record(s_out)
+
+    def timed_e2e(fn, pipelined):
+        for i in range(3):
+            fn(i) if pipelined else fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(e_steps):
+            fn(i) if pipelined else fn()
+        if pipelined:
+            stream.wait_event(ev_out[0])
+            stream.wait_event(ev_out[1])
+        e1.record(stream)
+        torch.cuda.synchronize()
+        te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        return 1000.0 * e_steps / float(te[0])
+
+    e2e_serial_tok_s = timed_e2e(e2e_serial, False)
+    e2e_tok_s = timed_e2e(e2e_pipelined, True)
+    h2d = hin[0].numel() * 2
+    d2h = hout[0].numel() * 2
 
     if rank == 0:
         peaks = load_peaks()
@@ -442,7 +476,8 @@ def run_ours(args) -> None:
                          "kernel_ms": k_ms, "kernel_ms_single_launch_events": k_ms_events,
                          "bytes_per_launch": launch_bytes},
             "e2e": {"value": e2e_tok_s, "unit": "tok/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
+                    "d2h_bytes_per_step": d2h, "form": "pipelined (2 buffer sets, 3 streams)",
+                    "serial_value": e2e_serial_tok_s},
             "clocks": clocks,
         }
         if per_rank is not None:
