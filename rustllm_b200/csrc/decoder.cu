@@ -405,8 +405,10 @@ __global__ void __launch_bounds__(kLinThreads) linear_kernel(const LinearArgs a)
                        ok ? 16 : 0);
         }
     };
-    // weights first (constant through a decode step), then wait for the previous kernel
-    const int pro = min(S - 1, nkt);
+    // weights first (constant through a decode step), then wait for the previous kernel;
+    // a K chunk that fits the ring is loaded whole here, so none of its weight loads waits
+    // for the previous kernel
+    const int pro = nkt <= S ? nkt : S - 1;
     for (int t = 0; t < pro; ++t) load_w(t, t);
     grid_dependency_wait();
     for (int t = 0; t < pro; ++t) load_x(t, t);
@@ -475,7 +477,7 @@ __global__ void __launch_bounds__(kLinThreads) linear_kernel(const LinearArgs a)
         __syncthreads();
         {
             const int tn = t + S - 1;
-            if (tn < nkt) {
+            if (tn >= pro && tn < nkt) {
                 load_w(tn, tn % S);
                 load_x(tn, tn % S);
             }
@@ -563,14 +565,21 @@ __global__ void __launch_bounds__(kLinThreads) linear_kernel(const LinearArgs a)
     const int m0 = split * rbr;
     const int mine = max(0, min(a.M, m0 + rbr) - m0);
     const float* src = ps;
+    // this thread's first output chunk: its residual is loaded now, so the load overlaps
+    // the exchange of the partial rows (the residual may alias out: this CTA alone writes
+    // these rows and columns, later)
+    uint4 resid0 = make_uint4(0, 0, 0, 0);
+    if (a.resid && (tid >> 3) < mine && n0 + (tid & 7) * 8 < a.N)
+        resid0 = *reinterpret_cast<const uint4*>(
+            a.resid + static_cast<int64_t>(m0 + (tid >> 3)) * a.ldr + n0 + (tid & 7) * 8);
     if (splits > 1) {
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // ps, for the copy engine
         __syncthreads();
         asm volatile("barrier.cluster.wait;" ::: "memory");  // every receive barrier is initialised
-        if (tid == 0) {
-            for (int r = 0; r < splits; ++r) {
-                const int b0 = r * rbr, b1 = min(a.M, b0 + rbr);
-                if (b1 <= b0) continue;
+        if (tid < splits) {  // thread r pushes band r to its owner, the copies issued in parallel
+            const int r = tid;
+            const int b0 = r * rbr, b1 = min(a.M, b0 + rbr);
+            if (b1 > b0) {
                 uint32_t dst, bar;
                 asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
                              : "=r"(dst)
@@ -651,7 +660,9 @@ __global__ void __launch_bounds__(kLinThreads) linear_kernel(const LinearArgs a)
             if (a.resid) {
                 float r[8];
                 Chunk<__half>::unpack(
-                    *reinterpret_cast<const uint4*>(a.resid + static_cast<int64_t>(m) * a.ldr + col), r);
+                    q == tid ? resid0
+                             : *reinterpret_cast<const uint4*>(a.resid + static_cast<int64_t>(m) * a.ldr + col),
+                    r);
 #pragma unroll
                 for (int e = 0; e < 8; ++e) y[e] = __fadd_rn(y[e], r[e]);
             }
@@ -673,30 +684,50 @@ __global__ void __launch_bounds__(kLinThreads) linear_kernel(const LinearArgs a)
             if (src != nullptr && c == 0 && (q >> 3) < mine) a.stats_out[tile * kLinRows + m] = sq;
         }
     }
-    if (splits > 1 && tid == 0)  // the pushed rows have left this CTA's shared memory
+    if (splits > 1 && tid < splits)  // the pushed rows have left this CTA's shared memory
         asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
 struct LinearPlan {
     int tiles, splits, kchunk;
 };
+// Dynamic shared memory of a launch: the ring, and with a split K the receive buffer of
+// the rows a CTA finishes (every split's partial band).
+template <int NW>
+size_t linear_smem_bytes(int splits, int rows) {
+    const int rbr = (rows + splits - 1) / splits;
+    return LinCfg<NW>::OFF_RB +
+           (splits > 1 ? static_cast<size_t>(splits) * rbr * LinCfg<NW>::PSTRIDE * 4 : 0);
+}
+
 // K splits so that the grid fills the SMs once (three CTAs an SM, less an eighth for the
 // packing of clusters), in chunks of whole 64-deep tiles, at most one cluster (8) per
-// column tile.  The plan depends on the shape only, so a row's result is the same in
-// every batch.
+// column tile, and never more CTAs than one wave holds at the largest batch (64 rows: the
+// receive buffer, and so the CTAs an SM holds, depends on the rows; B200 has 228 KB of
+// shared memory an SM, 1 KB of it reserved per CTA).  The plan depends on the shape only,
+// so a row's result is the same in every batch.
+template <int NW>
 LinearPlan plan_linear(int64_t k, int64_t n) {
+    constexpr int64_t kSmemPerSm = 233472, kSmemReserved = 1024;
     LinearPlan p{};
     p.tiles = static_cast<int>((n + kLinCols - 1) / kLinCols);
-    const int64_t target = static_cast<int64_t>(device_sm_count()) * 3 * 7 / 8;
+    const int64_t sms = device_sm_count();
+    const int64_t target = sms * 3 * 7 / 8;
     int64_t sp = target / p.tiles;
     const int64_t kt = (k + kLinK - 1) / kLinK;
     if (sp > kt) sp = kt;
     if (sp > kLinMaxSplits) sp = kLinMaxSplits;
     if (sp < 1) sp = 1;
-    int64_t chunk = (k + sp - 1) / sp;
-    chunk = ((chunk + kLinK - 1) / kLinK) * kLinK;
-    p.kchunk = static_cast<int>(chunk);
-    p.splits = static_cast<int>((k + chunk - 1) / chunk);
+    for (;; --sp) {
+        int64_t chunk = (k + sp - 1) / sp;
+        chunk = ((chunk + kLinK - 1) / kLinK) * kLinK;
+        p.kchunk = static_cast<int>(chunk);
+        p.splits = static_cast<int>((k + chunk - 1) / chunk);
+        const int64_t per_sm =
+            kSmemPerSm / (static_cast<int64_t>(linear_smem_bytes<NW>(p.splits, kLinRows)) +
+                          kSmemReserved);
+        if (sp == 1 || static_cast<int64_t>(p.tiles) * p.splits <= sms * per_sm) break;
+    }
     return p;
 }
 
@@ -713,13 +744,10 @@ int launch_linear(const LinearArgs& a, const LinearPlan& p, bool overlap, cudaSt
                                             static_cast<int>(LinCfg<NW>::SMEM_MAX)));
         opted.fetch_or(bit, std::memory_order_relaxed);
     }
-    const int rbr = (a.M + p.splits - 1) / p.splits;  // rows a CTA finishes
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(p.tiles), static_cast<unsigned>(p.splits));
     cfg.blockDim = dim3(kLinThreads);
-    cfg.dynamicSmemBytes =
-        LinCfg<NW>::OFF_RB +
-        (p.splits > 1 ? static_cast<size_t>(p.splits) * rbr * LinCfg<NW>::PSTRIDE * 4 : 0);
+    cfg.dynamicSmemBytes = linear_smem_bytes<NW>(p.splits, a.M);
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -876,7 +904,7 @@ int tmllm_linear(const void* x, int64_t ldx, const void* norm_weight, const floa
     if (norm_weight && (!std::isfinite(eps) || eps <= 0.0f))
         return fail(TMLLM_INVALID_SHAPE, "RMSNorm epsilon must be positive, got %g",
                     static_cast<double>(eps));
-    const LinearPlan p = plan_linear(k, n);
+    const LinearPlan p = swiglu ? plan_linear<2>(k, n) : plan_linear<1>(k, n);
     LinearArgs a{};
     a.x = static_cast<const __half*>(x);
     a.norm_w = static_cast<const __half*>(norm_weight);
