@@ -1252,11 +1252,12 @@ def run_kernel_survey(args) -> None:
                              (hid, 2560, True, "gate/up + SwiGLU 960x5120"),
                              (2560, 960, False, "down 2560x960")]:
         w = (rnd(kk, 2 * nn if sw else nn) / 30).to(H)
-        xin = rnd(8, kk)
-        outl = torch.empty((8, nn), dtype=H, device=dev)
-        timed(f"projection 8 rows, {what}", "linear_kernel",
-              lambda w=w, xin=xin, outl=outl, sw=sw: linear(xin, w, out=outl, swiglu=sw),
-              w.numel() * 2 + 8 * (kk + nn) * 2)
+        for rows, kern in ((8, "gemv_kernel"), (64, "linear_kernel")):
+            xin = rnd(rows, kk)
+            outl = torch.empty((rows, nn), dtype=H, device=dev)
+            timed(f"projection {rows} rows, {what}", kern,
+                  lambda w=w, xin=xin, outl=outl, sw=sw: linear(xin, w, out=outl, swiglu=sw),
+                  w.numel() * 2 + rows * (kk + nn) * 2)
     torch.cuda.empty_cache()
 
     # ---- op-level API kernels (ops.cu)

@@ -201,15 +201,19 @@ int tmllm_swiglu(tmllm_dtype dtype, const void* gate_up, void* out, size_t rows,
  *   residual != NULL (swiglu = 0 only): out = half(residual + half(x · W))
  *     (kernels/vector_add.metal:15-21); residual may alias out;
  *   stats_out != NULL: receives the row statistics of out (tmllm_linear_stats_bytes(n)
- *     bytes of device memory), for a later call that RMS-normalises out (its k = this n,
- *     the same rows).
+ *     bytes of 16-byte aligned device memory: one partial sum of squares per 16 columns
+ *     and row), for a
+ *     later call that RMS-normalises out (its k = this n, the same rows).
  * rows <= 64; k and n multiples of 8; ldx / ldw / ldo / ldr are row strides in elements,
  * multiples of 8, and x, w, out, residual and norm_weight are 16-byte aligned.
  * flags: TMLLM_LINEAR_OVERLAP lets the launch overlap the tail of the work queued before it
  * on `stream` (programmatic dependent launch): w is read before that work has finished, so
  * the caller promises that it does not write w; x, residual, stats_in and norm_weight are
- * read only after it has finished.  The result does not depend on `rows` beyond the row
- * itself: a row computed alone equals the same row in any batch. */
+ * read only after it has finished.  Up to 16 rows and 17-64 rows run two different forms
+ * (one CTA per 16 columns over the whole k; K split over a thread-block cluster); within
+ * each range the result does not depend on `rows` beyond the row itself: a row computed
+ * alone equals the same row in any batch of at most 16 rows, and any two batches of 17-64
+ * rows agree on a common row bit for bit. */
 #define TMLLM_LINEAR_OVERLAP 1u
 size_t tmllm_linear_stats_bytes(int32_t n);
 /* Reads and clears the status word of tmllm_linear's kernels: TMLLM_TIMEOUT when a bounded

@@ -45,17 +45,18 @@ def inputs(dev, rows, k, n, seed, *, swiglu=False):
 
 @pytest.mark.parametrize("rows", [1, 7, 16, 33, 64])
 @pytest.mark.parametrize("k,n", [(576, 960), (4096, 512), (200, 136), (1536, 576),
-                                 (768, 32000)])
+                                 (768, 32000), (7200, 64)])
 def test_plain_projection(cuda, rows, k, n):
-    """Unsplit (many column tiles) and split-K (few tiles, long K) plans; K and N that are
-    not multiples of the 64-wide tiles."""
+    """Up to 16 rows: one CTA per 16 columns over the whole K (and the cluster form where
+    the weight slice exceeds shared memory, K 7200); above: unsplit (many column tiles) and
+    split-K (few tiles, long K) plans; K and N that are not multiples of the tiles."""
     _, x, w = inputs(cuda, rows, k, n, rows * 7 + k)
     got = linear(x, w)
     assert rel(got, reference(x, w)) < 2e-3
     assert linear_status() == 0
 
 
-@pytest.mark.parametrize("rows", [1, 5, 64])
+@pytest.mark.parametrize("rows", [1, 5, 12, 64])
 @pytest.mark.parametrize("k,n", [(576, 960), (2048, 256)])
 def test_norm_fused_into_projection(cuda, rows, k, n):
     g, x, w = inputs(cuda, rows, k, n, 3 + rows)
@@ -64,7 +65,7 @@ def test_norm_fused_into_projection(cuda, rows, k, n):
     assert rel(got, reference(x, w, norm=nw, eps=1e-5)) < 2e-3
 
 
-@pytest.mark.parametrize("rows", [1, 24, 64])
+@pytest.mark.parametrize("rows", [1, 9, 24, 64])
 @pytest.mark.parametrize("k,n", [(576, 1536), (960, 2560), (4096, 256)])
 def test_norm_and_swiglu(cuda, rows, k, n):
     g, x, w = inputs(cuda, rows, k, n, 11 + rows, swiglu=True)
@@ -74,7 +75,7 @@ def test_norm_and_swiglu(cuda, rows, k, n):
     assert rel(got, reference(x, w, norm=nw, swiglu=True)) < 2e-3
 
 
-@pytest.mark.parametrize("rows", [1, 64])
+@pytest.mark.parametrize("rows", [1, 13, 64])
 @pytest.mark.parametrize("k,n", [(1536, 576), (4096, 1024)])
 def test_residual_in_place(cuda, rows, k, n):
     """out aliases the residual (the decoder's residual stream x += x_in · W)."""
@@ -85,16 +86,17 @@ def test_residual_in_place(cuda, rows, k, n):
     assert rel(r, want) < 2e-3
 
 
+@pytest.mark.parametrize("rows", [16, 40])
 @pytest.mark.parametrize("overlap", [False, True])
-def test_strided_rows_and_repeat_calls_are_identical(cuda, overlap):
+def test_strided_rows_and_repeat_calls_are_identical(cuda, overlap, rows):
     """Row strides wider than a row (x a column slice, out a column slice); repeated calls
     (split K over a cluster) give bit-identical results, with and without the overlapped
     launch."""
     g = torch.Generator(device=cuda).manual_seed(9)
-    big = torch.randn((16, 1024), generator=g, device=cuda).to(H)
+    big = torch.randn((rows, 1024), generator=g, device=cuda).to(H)
     x = big[:, 256:256 + 512]
     w = (torch.randn((512, 256), generator=g, device=cuda) / 23).to(H)
-    out = torch.zeros((16, 384), dtype=H, device=cuda)
+    out = torch.zeros((rows, 384), dtype=H, device=cuda)
     linear(x, w, out=out[:, 64:320], overlap=overlap)
     first = out.clone()
     assert rel(out[:, 64:320], reference(x.contiguous(), w)) < 2e-3
@@ -104,11 +106,12 @@ def test_strided_rows_and_repeat_calls_are_identical(cuda, overlap):
         assert torch.equal(out, first)
 
 
-def test_overlapped_chain_reads_the_previous_result(cuda):
+@pytest.mark.parametrize("rows", [8, 24])
+def test_overlapped_chain_reads_the_previous_result(cuda, rows):
     """A chain of overlapped projections where each reads (and adds into) the rows the
     previous one wrote: the same as the chain launched without overlap."""
     g = torch.Generator(device=cuda).manual_seed(31)
-    x0 = torch.randn((8, 512), generator=g, device=cuda).to(H)
+    x0 = torch.randn((rows, 512), generator=g, device=cuda).to(H)
     ws = [(torch.randn((512, 512), generator=g, device=cuda) / 23).to(H) for _ in range(6)]
     nw = (1 + 0.1 * torch.randn(512, generator=g, device=cuda)).to(H)
     res = []
@@ -125,7 +128,7 @@ def test_overlapped_chain_reads_the_previous_result(cuda):
     assert torch.equal(res[0], res[1])
 
 
-@pytest.mark.parametrize("rows", [1, 19, 64])
+@pytest.mark.parametrize("rows", [1, 11, 19, 64])
 def test_row_statistics_chain(cuda, rows):
     """A residual projection writes the row statistics of its output; the norm-fused
     projection that reads them equals one that recomputes them from the rows, and the
@@ -149,14 +152,20 @@ def test_row_statistics_chain(cuda, rows):
 
 
 def test_rows_do_not_interact(cuda):
-    """Row r of a 64-row call equals the same row computed alone, bit for bit (the split
-    plan depends on the shape only)."""
+    """Row r of a 16-row call equals the same row computed alone, and row r of a 64-row
+    call equals the same row in a 17-row call, bit for bit (each form's summation order
+    depends on the shape only).  The two forms agree within F32 rounding."""
     g, x, w = inputs(cuda, 64, 960, 2560, 4, swiglu=True)
     nw = (1 + 0.1 * torch.randn(960, generator=g, device=cuda)).to(H)
-    full = linear(x, w, norm_weight=nw, swiglu=True)
-    for r in (0, 17, 63):
+    small = linear(x[:16].contiguous(), w, norm_weight=nw, swiglu=True)
+    for r in (0, 7, 15):
         one = linear(x[r:r + 1].contiguous(), w, norm_weight=nw, swiglu=True)
-        assert torch.equal(one[0], full[r])
+        assert torch.equal(one[0], small[r])
+    full = linear(x, w, norm_weight=nw, swiglu=True)
+    for r in (17, 40, 63):
+        part = linear(x[r - 16:r + 1].contiguous(), w, norm_weight=nw, swiglu=True)
+        assert torch.equal(part[16], full[r])
+    assert rel(full[:16], small) < 2e-3
 
 
 def test_rejects_bad_arguments(cuda):
