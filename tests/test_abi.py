@@ -169,7 +169,7 @@ def test_linear_host_validation():
     assert lin(norm=p, eps=0.0) == 2 and lin(norm=p, eps=float("nan")) == 2
     assert b"epsilon" in lib.tmllm_last_error()
     assert lib.tmllm_linear_stats_bytes(960) == 60 * 64 * 4   # one partial per 16 columns
-    assert lib.tmllm_linear_stats_bytes(1000) == 16 * 64 * 4
+    assert lib.tmllm_linear_stats_bytes(1000) == 63 * 64 * 4
     assert lib.tmllm_linear_stats_bytes(0) == 0
 
 
