@@ -642,8 +642,10 @@ def run_decoder(args) -> None:
             "clocks": clocks,
             # this package's kernels a step launches (cuBLAS GEMMs not counted): embedding;
             # a layer's projections + attention (fused: 4 + 1; else norm x2, SwiGLU,
-            # attention); final norm, argmax; the length advance outside the graph
-            "gpu_launches": steps * (1 + cfg.num_layers * (5 if dec.fused else 4) + 2 + 1),
+            # attention); the head (fused: norm + head + argmax in one; else final norm,
+            # argmax); the length advance outside the graph
+            "gpu_launches": steps * (1 + cfg.num_layers * (5 if dec.fused else 4) +
+                                     (1 if dec.head else 2) + 1),
         }
         if prefill_ms is not None:
             line["prefill"] = {"ms": prefill_ms, "tok_s": B * prompt / (prefill_ms * 1e-3),

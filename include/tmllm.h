@@ -232,6 +232,29 @@ int tmllm_linear(const void* x, int64_t ldx, const void* norm_weight, const floa
 int tmllm_argmax(tmllm_dtype dtype, const void* logits, int32_t* ids, size_t rows, size_t vocab,
                  tmllm_stream stream);
 
+/* Replaces the tail of a decode step in one launch: the final RmsNorm and the lm_head Linear
+ * of Transformer::forward_with_cache_encode (src/model/transformer/cache.rs:72-77, i.e.
+ * kernels/rmsnorm.metal:71-126 then Linear::forward_encode, src/nn/linear.rs:141-149) and,
+ * optionally, the greedy pick of src/generation/sampler.rs:79-88 on the result.
+ *   logits [rows, n] = half(xn · W), W [k, n] row-major F16, F32 accumulation, where
+ *     x' = half(x + residual) when residual != NULL (kernels/vector_add.metal), else x, and
+ *     xn = half(x' * rsqrt(mean(x'^2) + eps) * norm_weight) row by row (bit-identical to
+ *     tmllm_add_rmsnorm), or xn = x' when norm_weight is NULL;
+ *   ids != NULL: ids[r] = the pick of tmllm_argmax over the stored F16 logits of row r
+ *     (the last of equal finite maxima under total order, -1 without a finite logit).
+ * The argmax needs `workspace`: tmllm_lm_head_workspace_bytes() bytes of 8-byte aligned
+ * device memory, zeroed once before its first use; every call leaves it zeroed again, so
+ * one workspace serves any number of calls that do not run concurrently on the GPU.
+ * rows <= 64 (with rows x k small enough for the rows to sit in shared memory: k <= 1344
+ * at 64 rows); k and n multiples of 8; ldx / ldr / ldw / ld_logits multiples of 8 and x,
+ * residual, w, logits and norm_weight 16-byte aligned.  flags: TMLLM_LINEAR_OVERLAP as for
+ * tmllm_linear (w may be read before the work queued ahead on `stream` has finished). */
+size_t tmllm_lm_head_workspace_bytes(void);
+int tmllm_lm_head(const void* x, int64_t ldx, const void* residual, int64_t ldr,
+                  const void* norm_weight, float eps, const void* w, int64_t ldw, void* logits,
+                  int64_t ld_logits, int32_t* ids, void* workspace, int32_t rows, int32_t k,
+                  int32_t n, uint32_t flags, tmllm_stream stream);
+
 /* ---------------------------------------------------------------------------------- */
 /* Fused paged decode attention (the hot path)                                         */
 /* ---------------------------------------------------------------------------------- */

@@ -178,6 +178,9 @@ _PROTOS = {
     "tmllm_linear_status": (C.c_int, [vp]),
     "tmllm_linear": (C.c_int, [vp, i64, vp, vp, C.c_float, vp, i64, vp, i64, vp, i64, vp, i32,
                                i32, i32, i32, C.c_uint32, vp]),
+    "tmllm_lm_head_workspace_bytes": (sz, []),
+    "tmllm_lm_head": (C.c_int, [vp, i64, vp, i64, vp, C.c_float, vp, i64, vp, i64, vp, vp, i32,
+                                i32, i32, C.c_uint32, vp]),
     "tmllm_decode_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
     "tmllm_decode_workspace_init": (C.c_int, [vp, sz, vp]),
     "tmllm_decode_auto_splits": (i32, [i32, i32, i64]),

@@ -9,6 +9,7 @@
 #include <cmath>
 
 #include "common.cuh"
+#include "tc.cuh"
 
 
 namespace tmllm {
@@ -1077,6 +1078,428 @@ int launch_gemv(const LinearArgs& a, bool overlap, cudaStream_t s) {
     return TMLLM_OK;
 }
 
+// ---- Vocabulary head of a decode step: final RMSNorm, x · W_head, greedy argmax ----------
+// The last three stages of the reference's cached forward (transformer/cache.rs:72-77: the
+// final RmsNorm, the lm_head Linear; then greedy_from_slice, generation/sampler.rs:79-88) as
+// one kernel.  The head weight is the largest tensor a decode step reads (K x vocab halves,
+// 57-94 MB for the BASELINE models) and every other operand is tiny, so the kernel is a
+// weight stream.  Column tiles of 4 x WN columns (64 with up to 32 rows, 128 above) are dealt
+// to persistent CTAs in equal numbers (the grid is the tile count over the tiles a CTA must
+// take, so no CTA runs a lone extra round at a fraction of the bandwidth).  Each CTA moves
+// its tiles through a ring of 16 KB stages (128 or 64 weight rows) that runs ahead across
+// tile boundaries, as deep as shared memory allows (two CTAs an SM with 4-12 stages each
+// where the rows leave room, else one with 3-12): a producer warp fills a stage with one or
+// two TMA tensor loads (64-column boxes in the 128-byte swizzle, so the eight rows of an
+// ldmatrix.trans tile fall into different banks; boxes reaching past K or N are zero-filled
+// by the copy engine) completing on the stage's full barrier, as soon as the four MMA warps
+// have released the slot on its empty barrier.  The rows (<= 64) sit in shared memory for
+// the whole
+// kernel, RMS-normalised in place once (the arithmetic of add_rmsnorm_warp_kernel, so the
+// normed rows equal tmllm_add_rmsnorm's bit for bit).  Warp w multiplies the rows by columns
+// [w*WN, (w+1)*WN) of a tile on the warp-level tensor cores (mma.sync m16n8k16, F16 in, F32
+// accumulate), one 16-row tile of rows per m-tile.  The epilogue stores the F16 logits and
+// keeps, per row, the best (value, index) key of the stored values (argmax_key: finite
+// values under total order, the last maximum wins); each CTA folds its keys into a per-row
+// 64-bit maximum in the caller's workspace, and the CTA that takes the last ticket turns
+// those maxima into token ids (-1 for a row without a finite logit) and resets the
+// workspace to zero for the next call.  Stage waits are bounded (TMLLM_TIMEOUT in the
+// status word tmllm_linear_status reads).
+constexpr int kHeadConsumers = 4;                     // MMA warps
+constexpr int kHeadThreads = 32 * (kHeadConsumers + 1);  // + one TMA producer warp
+constexpr int kHeadMaxRows = 64;
+constexpr int kHeadMinStages = 3, kHeadMaxStages = 12;
+constexpr int kHeadOffBest = 0;                                    // [4 warps][64] keys
+constexpr int kHeadOffBar = kHeadOffBest + 4 * kHeadMaxRows * 8;   // full and empty barriers
+constexpr int kHeadOffFlag = kHeadOffBar + 2 * kHeadMaxStages * 8;  // last-CTA / abort flags
+constexpr int kHeadOffX = kHeadOffFlag + 64;                       // the rows, then the ring
+constexpr int kHeadStage = 16384;                                  // bytes of one stage
+constexpr int kHeadSmemMax = 227 * 1024;
+constexpr int kHeadSmemPair = 113 * 1024;  // two CTAs an SM
+
+struct HeadArgs {
+    const __half* x;
+    const __half* norm_w;  // null: the rows are used as they are
+    const __half* resid;   // null: no residual add before the norm
+    const __half* w;
+    __half* logits;
+    int32_t* ids;                // null: no argmax
+    unsigned long long* best;    // [64] per-row keys (zero between calls)
+    unsigned int* ticket;        // CTAs finished (zero between calls)
+    int64_t ldx, ldr, ldw, ldo;
+    int M, K, N, stages;
+    float eps;
+};
+
+// columns a warp owns: 16 with up to two 16-row tiles of rows, else 32 (more products per
+// weight fragment, fewer reloads of the row fragments)
+__host__ __device__ constexpr int head_wn(int mt) { return mt <= 2 ? 16 : 32; }
+// weight rows of one stage (16 KB of weight: one or two 128-byte-wide panels)
+__host__ __device__ constexpr int head_krows(int mt) { return kHeadStage / (8 * head_wn(mt)); }
+// bytes of one staged input row: K rounded up to a whole stage, plus 16 so that the eight
+// rows of an ldmatrix tile fall into different banks
+__host__ __device__ inline int head_xstride(int mt, int K) {
+    const int kr = head_krows(mt);
+    return ((K + kr - 1) / kr) * kr * 2 + 16;
+}
+// the rows, the norm weight (K rounded up to a stage), then the ring on a 1024-byte
+// boundary (the swizzle pattern's period): up to 1008 bytes of padding
+size_t head_smem_bytes(int M, int K, int stages) {
+    const int mt = (M + 15) / 16;
+    const int kr = head_krows(mt);
+    return static_cast<size_t>(kHeadOffX) + static_cast<size_t>(mt) * 16 * head_xstride(mt, K) +
+           static_cast<size_t>((K + kr - 1) / kr) * kr * 2 + 1024 +
+           static_cast<size_t>(stages) * kHeadStage;
+}
+// ring depth: as deep as fits with two CTAs an SM (each in half of the shared memory) when
+// that leaves at least four stages, else with one CTA an SM (measured: two CTAs with a few
+// stages each stream the weight faster than one CTA with twice the stages in flight);
+// 0 when not even the shallowest ring fits
+int head_stages(int M, int K) {
+    for (int per_sm : {2, 1}) {
+        const size_t budget = per_sm == 2 ? kHeadSmemPair : kHeadSmemMax;
+        int st = kHeadMaxStages;
+        while (st >= kHeadMinStages && head_smem_bytes(M, K, st) > budget) --st;
+        if (st >= (per_sm == 2 ? 4 : kHeadMinStages)) return st;
+    }
+    return 0;
+}
+
+template <int MT>
+__global__ void __launch_bounds__(kHeadThreads)
+    head_kernel(const __grid_constant__ CUtensorMap wmap, const HeadArgs a) {
+    constexpr int WN = head_wn(MT), TC = 4 * WN;  // columns a warp / a tile owns
+    constexpr int KR = head_krows(MT);            // weight rows per stage
+    constexpr int PANEL = KR * 128;               // bytes of one 64-column panel of a stage
+    constexpr int NB = WN / 16;                   // ldmatrix.x4.trans per k16 step and warp
+    constexpr int CT = kHeadConsumers * 32;       // threads of the consumer warps
+    extern __shared__ __align__(128) unsigned char smem[];
+    unsigned long long* best_s = reinterpret_cast<unsigned long long*>(smem + kHeadOffBest);
+    volatile int* flags_s = reinterpret_cast<volatile int*>(smem + kHeadOffFlag);  // last, abort
+    unsigned char* xs = smem + kHeadOffX;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int K = a.K, M = a.M, N = a.N, S = a.stages;
+    const int ks = (K + KR - 1) / KR;  // ring stages per tile
+    const int kp = ks * KR;
+    const int xstride = head_xstride(MT, K);
+    unsigned char* nws = xs + MT * 16 * xstride;  // [kp] norm weight
+    const uint32_t ring_u = (lin_smem(nws + kp * 2) + 1023u) & ~1023u;
+    const uint32_t full0 = lin_smem(smem + kHeadOffBar);  // [S] stage landed (TMA bytes)
+    const uint32_t empty0 = full0 + 8 * kHeadMaxStages;   // [S] stage read by every consumer
+    const int ntiles = (N + TC - 1) / TC;
+    const int G = static_cast<int>(gridDim.x), cta = static_cast<int>(blockIdx.x);
+    const int nmine = cta < ntiles ? (ntiles - 1 - cta) / G + 1 : 0;
+    const int total = nmine * ks;  // ring stages of this CTA
+    if (tid == 0) {
+        for (int i = 0; i < S; ++i) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(full0 + 8 * i), "r"(1)
+                         : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(empty0 + 8 * i),
+                         "r"(kHeadConsumers)
+                         : "memory");
+        }
+        flags_s[0] = 0;
+        flags_s[1] = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    launch_dependents();
+
+    if (warp == kHeadConsumers) {
+        // ===== producer (one lane): stage q = weight rows [kk*KR, +KR) of tile q / ks, one
+        // 64-column box per panel (the bytes of every box count, zero-filled ones included),
+        // into slot q % S once the consumers have released that slot's previous stage.  The
+        // weight is constant, so none of this waits for the kernel ahead.
+        if (lane == 0) {
+            int q = 0;
+            for (; q < total; ++q) {
+                const int kk = q % ks, slot = q % S;
+                if (q >= S && !lin_wait(empty0 + 8 * slot, static_cast<uint32_t>(((q / S) - 1) & 1))) {
+                    flags_s[1] = 1;
+                    break;
+                }
+                if (flags_s[1]) break;
+                const int n0 = (cta + (q / ks) * G) * TC;
+                const uint32_t bar = full0 + 8 * slot;
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+                             "r"(static_cast<uint32_t>(kHeadStage))
+                             : "memory");
+#pragma unroll
+                for (int p = 0; p < TC / 64; ++p)
+                    tma_load_2d(ring_u + slot * kHeadStage + p * PANEL, &wmap, n0 + 64 * p,
+                                kk * KR, bar);
+            }
+            // on an abort, wait (bounded) for the stages in flight, so no copy lands after
+            // the CTA has exited
+            for (int r = q - S; r < q; ++r)
+                if (r >= 0) lin_wait(full0 + 8 * (r % S), static_cast<uint32_t>((r / S) & 1));
+        }
+    } else {
+        // ===== consumers (warps 0-3)
+        if (a.norm_w)  // constant: staged before the dependency wait
+            for (int c = tid; c < kp / 8; c += CT)
+                cp_async16(nws + c * 16, c * 8 < K ? a.norm_w + c * 8 : a.norm_w, c * 8 < K ? 16 : 0);
+        cp_async_commit();
+        grid_dependency_wait();  // the rows are current from here on
+        // the rows, zero-filled to whole 16-row tiles and whole stages
+        const int cpx = kp / 8;  // 16-byte chunks per staged row
+        for (int i = tid; i < MT * 16 * cpx; i += CT) {
+            const int m = i / cpx, c = i - m * cpx;
+            const bool ok = m < M && c * 8 < K;
+            cp_async16(xs + m * xstride + c * 16,
+                       ok ? a.x + static_cast<int64_t>(m) * a.ldx + c * 8 : a.x, ok ? 16 : 0);
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+        asm volatile("bar.sync 1, %0;" ::"n"(CT) : "memory");
+        if (a.norm_w || a.resid) {
+            // row m on warp m % 4, as add_rmsnorm_warp_kernel does one row: the residual
+            // added with the sum rounded to F16 (kernels/vector_add.metal), lane sums chunks
+            // lane, lane + 32, ... in order, then the shuffle tree; the row is rewritten as
+            // half(x * inv * w).  A warp's rows advance together, chunk by chunk, so their
+            // loads and sums overlap.
+            constexpr int RPW = MT * 16 / kHeadConsumers;  // rows per warp at most
+            const int nr = (M - warp + kHeadConsumers - 1) / kHeadConsumers;  // this warp's
+            float ss[RPW];
+#pragma unroll
+            for (int j = 0; j < RPW; ++j) ss[j] = 0.f;
+            for (int c = lane; c < K / 8; c += 32) {
+                uint4 rv[RPW];
+                if (a.resid) {
+#pragma unroll
+                    for (int j = 0; j < RPW; ++j)
+                        if (j < nr)
+                            rv[j] = __ldg(reinterpret_cast<const uint4*>(
+                                              a.resid + static_cast<int64_t>(warp + kHeadConsumers * j) * a.ldr) +
+                                          c);
+                }
+#pragma unroll
+                for (int j = 0; j < RPW; ++j) {
+                    if (j >= nr) break;
+                    unsigned char* row = xs + (warp + kHeadConsumers * j) * xstride;
+                    float f[8];
+                    Chunk<__half>::unpack(*reinterpret_cast<const uint4*>(row + c * 16), f);
+                    if (a.resid) {
+                        float r8[8];
+                        Chunk<__half>::unpack(rv[j], r8);
+                        uint4 sv;
+                        __half2* sh = reinterpret_cast<__half2*>(&sv);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] = round_store<__half>(__fadd_rn(f[e], r8[e]));
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) sh[e] = __floats2half2_rn(f[2 * e], f[2 * e + 1]);
+                        *reinterpret_cast<uint4*>(row + c * 16) = sv;
+                    }
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) ss[j] = fmaf(f[e], f[e], ss[j]);
+                }
+            }
+            if (a.norm_w) {
+                float inv[RPW];
+#pragma unroll
+                for (int j = 0; j < RPW; ++j)
+                    inv[j] = j < nr ? rsqrtf(warp_sum(ss[j]) / static_cast<float>(K) + a.eps) : 0.f;
+                for (int c = lane; c < K / 8; c += 32) {
+                    float w8[8];
+                    Chunk<__half>::unpack(*reinterpret_cast<const uint4*>(nws + c * 16), w8);
+#pragma unroll
+                    for (int j = 0; j < RPW; ++j) {
+                        if (j >= nr) break;
+                        unsigned char* row = xs + (warp + kHeadConsumers * j) * xstride;
+                        float f[8];
+                        Chunk<__half>::unpack(*reinterpret_cast<const uint4*>(row + c * 16), f);
+                        uint4 y;
+                        __half2* yh = reinterpret_cast<__half2*>(&y);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            yh[e] = __floats2half2_rn(f[2 * e] * inv[j] * w8[2 * e],
+                                                      f[2 * e + 1] * inv[j] * w8[2 * e + 1]);
+                        *reinterpret_cast<uint4*>(row + c * 16) = y;
+                    }
+                }
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(CT) : "memory");
+        }
+
+        const int g = lane >> 2, t = lane & 3;
+        float acc[MT][2 * NB][4];
+        unsigned long long bk[MT][2];  // best key of rows g and g + 8 of each m-tile
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) bk[mt][0] = bk[mt][1] = 0ull;
+        const uint32_t xs_u = lin_smem(xs);
+        // ldmatrix addresses of this lane: A (rows) matrix lane/8 = (row half, k half);
+        // B (weight, transposed) matrix lane/8 = (k half, column half): column chunk
+        // bch + 2p of a stage lives in panel chunk/8 at chunk (chunk % 8) ^ (row % 8)
+        const int arow = (lane & 7) + ((lane >> 3) & 1) * 8, acol = (lane >> 4) * 8;
+        const int bch = warp * (WN / 8) + (lane >> 4);
+        for (int q = 0; q < total; ++q) {
+            const int kk = q % ks, slot = q % S;
+            const bool ok = lin_wait(full0 + 8 * slot, static_cast<uint32_t>((q / S) & 1));
+            if (!__all_sync(0xffffffffu, ok) || flags_s[1]) {
+                flags_s[1] = 1;
+                break;
+            }
+            if (kk == 0) {
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                    for (int nt = 0; nt < 2 * NB; ++nt)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) acc[mt][nt][e] = 0.f;
+            }
+            const uint32_t st = ring_u + slot * kHeadStage;
+            const int nk = (min(KR, K - kk * KR) + 15) / 16;  // k16 steps holding rows < K
+#pragma unroll 4
+            for (int s16 = 0; s16 < nk; ++s16) {
+                uint32_t af[MT][4];
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+                    ldsm_x4(xs_u + (mt * 16 + arow) * xstride + (kk * KR + s16 * 16 + acol) * 2,
+                            af[mt][0], af[mt][1], af[mt][2], af[mt][3]);
+                const int r = s16 * 16 + arow;
+#pragma unroll
+                for (int p = 0; p < NB; ++p) {
+                    const int ch = bch + 2 * p;
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4_t(st + (ch >> 3) * PANEL + r * 128 + (((ch & 7) ^ (r & 7)) << 4), b0,
+                              b1, b2, b3);
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) {
+                        mma16816(acc[mt][2 * p], af[mt][0], af[mt][1], af[mt][2], af[mt][3], b0, b1);
+                        mma16816(acc[mt][2 * p + 1], af[mt][0], af[mt][1], af[mt][2], af[mt][3], b2,
+                                 b3);
+                    }
+                }
+            }
+            // this warp is done with the slot (its shared-memory reads are complete once
+            // the fragments are in registers)
+            __syncwarp();
+            if (lane == 0)
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(empty0 + 8 * slot)
+                             : "memory");
+            if (kk == ks - 1) {
+                // the tile is complete: F16 logits out, the best key of the stored values kept
+                const int n0 = (cta + (q / ks) * G) * TC + warp * WN;
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const int m = mt * 16 + g + 8 * hh;
+#pragma unroll
+                        for (int nt = 0; nt < 2 * NB; ++nt) {
+                            const int col = n0 + nt * 8 + 2 * t;
+                            const __half2 hv =
+                                __floats2half2_rn(acc[mt][nt][2 * hh], acc[mt][nt][2 * hh + 1]);
+                            if (m < M && col < N) {
+                                *reinterpret_cast<__half2*>(a.logits + static_cast<int64_t>(m) * a.ldo +
+                                                            col) = hv;
+                                const float2 f = __half22float2(hv);
+                                const unsigned long long k0 = argmax_key(f.x, col);
+                                const unsigned long long k1 = argmax_key(f.y, col + 1);
+                                const unsigned long long kb = k1 > k0 ? k1 : k0;
+                                bk[mt][hh] = kb > bk[mt][hh] ? kb : bk[mt][hh];
+                            }
+                        }
+                    }
+            }
+        }
+        if (a.ids) {
+            // per row: the four lanes of a row group, then the four warps, then every CTA
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    unsigned long long k = bk[mt][hh];
+#pragma unroll
+                    for (int o = 1; o <= 2; o <<= 1) {
+                        const unsigned long long v = __shfl_xor_sync(0xffffffffu, k, o);
+                        k = v > k ? v : k;
+                    }
+                    if (t == 0) best_s[warp * kHeadMaxRows + mt * 16 + g + 8 * hh] = k;
+                }
+        }
+    }
+    if (!a.ids) return;
+    __syncthreads();
+    if (tid < M) {
+        unsigned long long k = best_s[tid];
+#pragma unroll
+        for (int w = 1; w < kHeadConsumers; ++w) {
+            const unsigned long long v = best_s[w * kHeadMaxRows + tid];
+            k = v > k ? v : k;
+        }
+        if (k) atomicMax(a.best + tid, k);
+    }
+    // the ticket is taken with release and acquire semantics at device scope: the barrier
+    // orders this CTA's maxima before thread 0's release, and the last CTA's acquire before
+    // its reads of every CTA's maxima.  A CTA that gave up on a wait (recorded in the
+    // status word) still takes its ticket, so later calls start from a zeroed workspace.
+    __syncthreads();
+    if (tid == 0) {
+        unsigned int t;
+        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(t) : "l"(a.ticket)
+                     : "memory");
+        flags_s[0] = t == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!flags_s[0]) return;
+    if (tid < M) {  // every CTA's maxima are in: read and clear them
+        const unsigned long long k = atomicExch(a.best + tid, 0ull);
+        a.ids[tid] = k ? static_cast<int32_t>(k & 0xffffffffull) : -1;
+    }
+    if (tid == 0) atomicExch(a.ticket, 0u);
+}
+
+template <int MT>
+int launch_head(const HeadArgs& a, bool overlap, cudaStream_t s) {
+    const size_t smem = head_smem_bytes(a.M, a.K, a.stages);
+    // the weight as K rows of N halves, boxes of 64 columns x one stage's rows; the map of
+    // the last call is kept per thread (a decode loop calls with one head weight)
+    struct MapKey {
+        const void* w;
+        int64_t n, k, ldw;
+        int kr;
+    };
+    thread_local MapKey key{nullptr, 0, 0, 0, 0};
+    thread_local CUtensorMap wmap;
+    const MapKey want{a.w, a.N, a.K, a.ldw, head_krows(MT)};
+    if (key.w != want.w || key.n != want.n || key.k != want.k || key.ldw != want.ldw ||
+        key.kr != want.kr) {
+        if (int st = make_map(&wmap, a.w, a.N, a.K, a.ldw * 2, head_krows(MT))) return st;
+        key = want;
+    }
+    static std::atomic<uint64_t> opted{0};
+    int dev = 0;
+    TMLLM_CUDA_TRY(cudaGetDevice(&dev));
+    const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
+    if (!bit || !(opted.load(std::memory_order_relaxed) & bit)) {
+        TMLLM_CUDA_TRY(cudaFuncSetAttribute(head_kernel<MT>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            kHeadSmemMax));
+        opted.fetch_or(bit, std::memory_order_relaxed);
+    }
+    int per_sm = 0;
+    TMLLM_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, head_kernel<MT>,
+                                                                 kHeadThreads, smem));
+    if (per_sm < 1) per_sm = 1;
+    // equal shares: every CTA takes `rounds` tiles (the last few one fewer)
+    const int64_t ntiles = (a.N + 4 * head_wn(MT) - 1) / (4 * head_wn(MT));
+    const int64_t slots = static_cast<int64_t>(device_sm_count()) * per_sm;
+    const int64_t rounds = (ntiles + slots - 1) / slots;
+    const int64_t grid = (ntiles + rounds - 1) / rounds;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(kHeadThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = overlap ? 1 : 0;
+    TMLLM_CUDA_TRY(cudaLaunchKernelEx(&cfg, head_kernel<MT>, wmap, a));
+    return TMLLM_OK;
+}
+
 int check_dtype(int dtype) {
     if (!valid_dtype(dtype)) return fail(TMLLM_UNSUPPORTED_DTYPE, "unknown dtype %d", dtype);
     return TMLLM_OK;
@@ -1271,6 +1694,76 @@ int tmllm_argmax(tmllm_dtype dtype, const void* logits, int32_t* ids, size_t row
     else
         argmax_kernel<float><<<static_cast<unsigned>(rows), 1024, 0, s>>>(
             static_cast<const float*>(logits), ids, static_cast<int64_t>(vocab), vec);
+    TMLLM_LAUNCH_TRY();
+    return TMLLM_OK;
+}
+
+size_t tmllm_lm_head_workspace_bytes(void) { return 1024; }
+
+int tmllm_lm_head(const void* x, int64_t ldx, const void* residual, int64_t ldr,
+                  const void* norm_weight, float eps, const void* w, int64_t ldw, void* logits,
+                  int64_t ld_logits, int32_t* ids, void* workspace, int32_t rows, int32_t k,
+                  int32_t n, uint32_t flags, tmllm_stream stream) {
+    clear_error();
+    if (rows <= 0 || k <= 0 || n <= 0)
+        return fail(TMLLM_INVALID_SHAPE, "lm_head dimensions must be positive");
+    if (rows > kHeadMaxRows)
+        return fail(TMLLM_INVALID_SHAPE, "tmllm_lm_head takes at most %d rows, got %d",
+                    kHeadMaxRows, rows);
+    if (flags & ~static_cast<uint32_t>(TMLLM_LINEAR_OVERLAP))
+        return fail(TMLLM_INVALID_ARGUMENT, "unknown lm_head flags 0x%x", flags);
+    if (!x || !w || !logits) return fail(TMLLM_INVALID_ARGUMENT, "null tensor pointer");
+    if (ids && !workspace)
+        return fail(TMLLM_INVALID_ARGUMENT, "the argmax needs the lm_head workspace");
+    if (k % 8 || n % 8)
+        return fail(TMLLM_INVALID_SHAPE, "lm_head K and N must be multiples of 8 (got %d, %d)",
+                    k, n);
+    if (ldx < k || ldw < n || ld_logits < n || (residual && ldr < k))
+        return fail(TMLLM_INVALID_SHAPE, "row strides must cover a row");
+    if (!aligned16(x) || !aligned16(w) || !aligned16(logits) ||
+        (norm_weight && !aligned16(norm_weight)) || (residual && !aligned16(residual)) ||
+        ldx % 8 || ldw % 8 || ld_logits % 8 || (residual && ldr % 8))
+        return fail(TMLLM_INVALID_ARGUMENT,
+                    "x, the residual, w, logits and the norm weight need 16-byte aligned rows");
+    if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 7u))
+        return fail(TMLLM_INVALID_ARGUMENT, "the lm_head workspace needs 8-byte alignment");
+    if (norm_weight && (!std::isfinite(eps) || eps <= 0.0f))
+        return fail(TMLLM_INVALID_SHAPE, "RMSNorm epsilon must be positive, got %g",
+                    static_cast<double>(eps));
+    const int stages = head_stages(rows, k);
+    if (stages == 0)
+        return fail(TMLLM_INVALID_SHAPE,
+                    "lm_head rows x K too large for shared memory (%d x %d)", rows, k);
+    HeadArgs a{};
+    a.x = static_cast<const __half*>(x);
+    a.norm_w = static_cast<const __half*>(norm_weight);
+    a.resid = static_cast<const __half*>(residual);
+    a.ldr = ldr;
+    a.w = static_cast<const __half*>(w);
+    a.logits = static_cast<__half*>(logits);
+    a.ids = ids;
+    a.best = static_cast<unsigned long long*>(workspace);
+    a.ticket = workspace ? reinterpret_cast<unsigned int*>(static_cast<unsigned char*>(workspace) +
+                                                           kHeadMaxRows * 8)
+                         : nullptr;
+    a.ldx = ldx;
+    a.ldw = ldw;
+    a.ldo = ld_logits;
+    a.M = rows;
+    a.K = k;
+    a.N = n;
+    a.stages = stages;
+    a.eps = eps;
+    auto s = reinterpret_cast<cudaStream_t>(stream);
+    const bool overlap = (flags & TMLLM_LINEAR_OVERLAP) != 0;
+    int rc;
+    switch ((rows + 15) / 16) {
+        case 1: rc = launch_head<1>(a, overlap, s); break;
+        case 2: rc = launch_head<2>(a, overlap, s); break;
+        case 3: rc = launch_head<3>(a, overlap, s); break;
+        default: rc = launch_head<4>(a, overlap, s); break;
+    }
+    if (rc != TMLLM_OK) return rc;
     TMLLM_LAUNCH_TRY();
     return TMLLM_OK;
 }

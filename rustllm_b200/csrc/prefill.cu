@@ -850,6 +850,8 @@ __global__ void __launch_bounds__(128) prefill_generic_kernel(const PrefillArgs 
 }
 
 // ---- host ----------------------------------------------------------------------------
+}  // namespace
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -874,7 +876,7 @@ EncodeTiledFn encode_tiled() {
 // or 32 F32 columns) x box_rows rows with the 128-byte swizzle (the layout the tensor-core
 // descriptors read).
 int make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t rows, int64_t row_bytes,
-             int box_rows, bool f32 = false) {
+             int box_rows, bool f32) {
     EncodeTiledFn enc = encode_tiled();
     if (!enc) return fail(TMLLM_DEVICE_ERROR, "cuTensorMapEncodeTiled is not available");
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
@@ -891,6 +893,8 @@ int make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t rows, in
                     static_cast<int>(r));
     return TMLLM_OK;
 }
+
+namespace {
 
 template <int D>
 int launch_tc(const PrefillArgs& a, int64_t arena_rows, int max_rows, cudaStream_t s) {

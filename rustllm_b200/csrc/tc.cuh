@@ -9,6 +9,14 @@
 
 namespace tmllm {
 
+// Host: a 2-D tensor map over `rows` rows of `inner` elements, `row_bytes` apart, with
+// boxes of 128 bytes (64 F16 or 32 F32 columns) x box_rows rows in the 128-byte swizzle
+// (chunk c of box row r at chunk c ^ (r % 8); the layout the tensor-core descriptors and
+// the swizzled ldmatrix reads expect).  The encoder is the driver's cuTensorMapEncodeTiled,
+// fetched at run time.  Returns a tmllm status.
+int make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t rows, int64_t row_bytes,
+             int box_rows, bool f32 = false);
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

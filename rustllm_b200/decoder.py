@@ -17,7 +17,8 @@ into the projection that produces it, so a layer is five launches:
       -> [down + residual -> x]
 
 Prompts and larger batches use plain cuBLAS GEMMs (torch.matmul) between the norm, SwiGLU
-and attention kernels.  Weights keep the reference's [in, out] layout
+and attention kernels.  With up to 16 sequences (F16) the step ends in one launch: the final
+RMSNorm, the vocabulary head and the greedy pick (``lm_head``, tmllm_lm_head).  Weights keep the reference's [in, out] layout
 (src/nn/linear.rs:26-27); Q, K, V and gate/up are concatenated along `out` so each
 pair/triple is one projection, and the attention reads q, k, v in place from the fused
 output through per-sequence strides.  A whole step is captured into one CUDA graph
@@ -157,6 +158,73 @@ def linear(x: torch.Tensor, w: torch.Tensor, *, norm_weight: torch.Tensor | None
          stats_out.data_ptr() if stats_out is not None else None, rows, k, n, int(swiglu),
          LINEAR_OVERLAP if overlap else 0, stream_ptr(x.device))
     return out
+
+
+HEAD_MAX_ROWS = 64
+HEAD_STEP_MAX_ROWS = 16  # decode steps of up to this many sequences use lm_head
+_HEAD_SMEM_MAX = 227 * 1024
+
+
+def head_fits(rows: int, k: int, n: int) -> bool:
+    """Whether ``lm_head`` takes these sizes: at most 64 rows whose staged copy (in 16-row
+    tiles; K rounded up to a whole stage of 128 weight rows with up to 32 rows, 64 above,
+    plus a 16-byte pad per row) and the norm weight fit beside the shallowest weight ring
+    (three 16 KB stages on a 1024-byte boundary) in shared memory, K and N in whole 16-byte
+    chunks."""
+    mt = (rows + 15) // 16
+    kr = 128 if mt <= 2 else 64  # weight rows a stage
+    kp = (k + kr - 1) // kr * kr
+    smem = 4 * 64 * 8 + 2 * 12 * 8 + 64 + mt * 16 * (2 * kp + 16) + 2 * kp + 1024 + 3 * 16384
+    return 0 < rows <= HEAD_MAX_ROWS and k % 8 == 0 and n % 8 == 0 and smem <= _HEAD_SMEM_MAX
+
+
+def head_workspace(*, device=None) -> torch.Tensor:
+    """Zeroed device workspace for the argmax of ``lm_head`` (each call leaves it zeroed)."""
+    nbytes = int(_lib.load().tmllm_lm_head_workspace_bytes())
+    return torch.zeros(nbytes // 8, dtype=torch.int64, device=device)
+
+
+def lm_head(x: torch.Tensor, w: torch.Tensor, *, norm_weight: torch.Tensor | None = None,
+            eps: float = 1e-5, residual: torch.Tensor | None = None,
+            logits: torch.Tensor | None = None, ids: torch.Tensor | None = None,
+            workspace: torch.Tensor | None = None, overlap: bool = False) -> torch.Tensor:
+    """The end of a decode step in one launch (transformer/cache.rs:72-77 and
+    generation/sampler.rs:79-88): logits [rows <= 64, n] = half(rmsnorm(x [+ residual]) · w)
+    for F16 x [rows, k] and w [k, n]; with ``ids`` (int32 [rows]) also the greedy token of
+    every row, as ``tmllm_argmax`` picks it from the stored logits (``workspace`` from
+    ``head_workspace``).  ``overlap`` as for ``linear``."""
+    if x.dim() != 2 or w.dim() != 2:
+        raise _lib.ModelFormat(f"Linear expects rank-2 input, got {tuple(x.shape)}")
+    given = [t for t in (x, w, norm_weight, residual, logits, ids, workspace) if t is not None]
+    if any(not t.is_cuda or t.device != x.device for t in given):
+        raise _lib.InvalidArgument("lm_head tensors must live on one CUDA device")
+    rows, k = x.shape
+    if w.shape[0] != k:
+        raise _lib.ModelFormat(f"Linear input feature mismatch: expected {w.shape[0]}, got {k}")
+    if x.dtype != torch.float16 or w.dtype != torch.float16:
+        raise _lib.UnsupportedDType(f"lm_head takes F16 input and weight, got {x.dtype}, {w.dtype}")
+    if residual is not None and (residual.shape != x.shape or residual.dtype != x.dtype):
+        raise _lib.ShapeMismatch("lm_head residual must match x", left=list(x.shape),
+                                 right=list(residual.shape))
+    if x.stride(1) != 1 or w.stride(1) != 1 or (residual is not None and residual.stride(1) != 1):
+        raise _lib.NonContiguousTensor("lm_head needs unit column stride")
+    n = w.shape[1]
+    if logits is None:
+        logits = torch.empty((rows, n), dtype=x.dtype, device=x.device)
+    if ids is not None:
+        if ids.dtype != torch.int32 or ids.numel() < rows or not ids.is_contiguous():
+            raise _lib.InvalidArgument("lm_head ids must be a contiguous int32 buffer of rows")
+        if workspace is None:
+            raise _lib.InvalidArgument("lm_head argmax needs a head_workspace buffer")
+    call("tmllm_lm_head", x.data_ptr(), x.stride(0),
+         residual.data_ptr() if residual is not None else None,
+         residual.stride(0) if residual is not None else 0,
+         norm_weight.data_ptr() if norm_weight is not None else None, eps, w.data_ptr(),
+         w.stride(0), logits.data_ptr(), logits.stride(0),
+         ids.data_ptr() if ids is not None else None,
+         workspace.data_ptr() if workspace is not None else None, rows, k, n,
+         LINEAR_OVERLAP if overlap else 0, stream_ptr(x.device))
+    return logits
 
 
 class DecoderWeights:
@@ -305,6 +373,26 @@ class Decoder:
                       all(k % 8 == 0 and n % 8 == 0 for k, n in shapes))
         if self.fused:
             self.stats = linear_stats(h, device=self.device)  # row statistics of x
+        # final norm + vocabulary head + greedy pick in one kernel (F16); measured faster
+        # than the library GEMM with the separate norm and argmax up to 16 rows
+        self.head = (self.dtype == torch.float16 and B <= HEAD_STEP_MAX_ROWS and
+                     head_fits(B, h, cfg.vocab_size))
+        if self.head:
+            self.head_ws = head_workspace(device=self.device)
+
+    def _head(self, residual) -> None:
+        """logits and next_ids from the residual stream x (+ residual): final RMSNorm,
+        lm_head and greedy argmax (transformer/cache.rs:72-77, sampler.rs:79-88)."""
+        cfg, w = self.cfg, self.w
+        if self.head:
+            lm_head(self.x, w.lm_head, norm_weight=w.final_norm, eps=cfg.rms_norm_eps,
+                    residual=residual, logits=self.logits, ids=self.next_ids,
+                    workspace=self.head_ws, overlap=True)
+            return
+        self._norm(self.x, residual, w.final_norm, self.hn, None)
+        torch.matmul(self.hn, w.lm_head, out=self.logits)
+        call("tmllm_argmax", self.dt, self.logits.data_ptr(), self.next_ids.data_ptr(), self.B,
+             cfg.vocab_size, stream_ptr(self.device))
 
     # -- pieces ------------------------------------------------------------------------
     def _norm(self, x, residual, weight, out, sum_out):
@@ -362,11 +450,7 @@ class Decoder:
                 self._linear(self.x, L["wgu"], self.act, norm=L["mlp_norm"], stats_in=True,
                              swiglu=True)
                 self._linear(self.act, L["wd"], self.x, residual=self.x)
-            # the vocabulary-wide head streams best as a cuBLAS GEMM (wide tiles)
-            self._norm(self.x, None, w.final_norm, self.hn, None)
-            torch.matmul(self.hn, w.lm_head, out=self.logits)
-            call("tmllm_argmax", self.dt, self.logits.data_ptr(), self.next_ids.data_ptr(),
-                 self.B, cfg.vocab_size, stream_ptr(self.device))
+            self._head(None)
             return
         residual = None
         for li, L in enumerate(w.layers):
@@ -381,10 +465,7 @@ class Decoder:
                  cfg.intermediate_size, stream_ptr(self.device))
             torch.matmul(self.act, L["wd"], out=self.down)
             residual = self.down
-        self._norm(self.x, residual, w.final_norm, self.hn, None)
-        torch.matmul(self.hn, w.lm_head, out=self.logits)
-        call("tmllm_argmax", self.dt, self.logits.data_ptr(), self.next_ids.data_ptr(), self.B,
-             cfg.vocab_size, stream_ptr(self.device))
+        self._head(residual)
 
     # -- driving -----------------------------------------------------------------------
     def check_ids(self, ids: torch.Tensor) -> None:
@@ -435,10 +516,7 @@ class Decoder:
         # only each prompt's last row reaches the head
         last = torch.arange(S - 1, T, S, device=self.device)
         self.x.copy_(x.index_select(0, last))
-        self._norm(self.x, down.index_select(0, last), w.final_norm, self.hn, None)
-        torch.matmul(self.hn, w.lm_head, out=self.logits)
-        call("tmllm_argmax", self.dt, self.logits.data_ptr(), self.next_ids.data_ptr(), self.B,
-             cfg.vocab_size, sp)
+        self._head(down.index_select(0, last))
         self.cache.advance(S)
         return self.next_ids.clone()
 

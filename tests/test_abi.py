@@ -173,6 +173,32 @@ def test_linear_host_validation():
     assert lib.tmllm_linear_stats_bytes(0) == 0
 
 
+def test_lm_head_host_validation():
+    """tmllm_lm_head rejects bad shapes, strides, alignment and a missing workspace on the
+    host, before any device work; its workspace is 1 KB."""
+    lib = _lib.load()
+    p = C.c_void_p(256)  # 16-byte aligned, never dereferenced
+
+    def head(x=p, ldx=64, res=None, ldr=0, norm=None, eps=1e-5, w=p, ldw=64, out=p, ldo=64,
+             ids=None, ws=None, rows=4, k=64, n=64, flags=0):
+        return lib.tmllm_lm_head(x, ldx, res, ldr, norm, eps, w, ldw, out, ldo, ids, ws, rows,
+                                 k, n, flags, None)
+    assert lib.tmllm_lm_head_workspace_bytes() == 1024
+    assert head(rows=0) == 2 and head(rows=65) == 2      # 1..64 rows
+    assert head(k=60, ldx=64) == 2 and head(n=60) == 2   # whole 16-byte chunks
+    assert head(flags=2) == 1                            # only TMLLM_LINEAR_OVERLAP
+    assert head(x=None) == 1 and head(out=None) == 1 and head(w=None) == 1
+    assert head(ids=p) == 1                              # the argmax needs the workspace
+    assert head(ids=p, ws=C.c_void_p(260)) == 1          # 8-byte aligned workspace
+    assert head(ldx=32) == 2 and head(ldo=32) == 2       # stride shorter than a row
+    assert head(res=p, ldr=32) == 2
+    assert head(x=C.c_void_p(258)) == 1 and head(res=C.c_void_p(264), ldr=64) == 1
+    assert head(ldw=68) == 1                             # row stride in whole chunks
+    assert head(norm=p, eps=0.0) == 2
+    assert head(rows=64, k=1408, ldx=1408) == 2          # rows too large for shared memory
+    assert b"shared memory" in lib.tmllm_last_error()
+
+
 def test_argmax_and_decode_flag_validation():
     lib = _lib.load()
     p = C.c_void_p(256)
