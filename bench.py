@@ -1069,7 +1069,7 @@ def run_kernel_survey(args) -> None:
 
     import rustllm_b200 as rb
     from rustllm_b200 import _lib
-    from rustllm_b200.decoder import linear
+    from rustllm_b200.decoder import head_workspace, linear, lm_head
 
     world, rank, local = dist_env()
     if rank != 0:
@@ -1250,6 +1250,22 @@ def run_kernel_survey(args) -> None:
           lambda: _lib.call("tmllm_argmax", 1, lg.data_ptr(), am.data_ptr(), 1024, voc, sp),
           1024 * voc * 2)
     del lg
+    # the decode-step head (final norm + lm_head + argmax): three weight copies in turn, so
+    # the weight is read from HBM as in a decode step
+    for rows, kk, nn, what in ((1, 576, 49152, "cfg2"), (16, 768, 32000, "cfg5")):
+        hw = [(rnd(kk, nn) / 30).to(H) for _ in range(3)]
+        hx, hnw = rnd(rows, kk), rnd(kk)
+        hlg = torch.empty((rows, nn), dtype=H, device=dev)
+        hid_ = torch.empty(rows, dtype=torch.int32, device=dev)
+        hws = head_workspace(device=dev)
+        turn = [0]
+
+        def head_call(hw=hw, hx=hx, hnw=hnw, hlg=hlg, hid_=hid_, hws=hws, turn=turn):
+            turn[0] += 1
+            lm_head(hx, hw[turn[0] % 3], norm_weight=hnw, logits=hlg, ids=hid_, workspace=hws)
+        timed(f"head {rows} rows, {kk}x{nn} ({what})", "head_kernel<1>", head_call,
+              kk * nn * 2 + rows * (kk + nn) * 2)
+        del hw
     for kk, nn, sw, what in [(hid, 1600, False, "QKV 960x1600"), (960, 960, False, "O 960x960"),
                              (hid, 2560, True, "gate/up + SwiGLU 960x5120"),
                              (2560, 960, False, "down 2560x960")]:

@@ -281,7 +281,9 @@ constexpr int kLinMaxSplits = 8;                 // portable cluster size
 constexpr int kLinSlab = kLinK * kLinCols * 2;  // one 64 x 64 F16 tile (weight or x)
 // the small-batch form below (gemv_kernel); row statistics hold one partial sum of squares
 // per 16 output columns and row: [ceil(N / 16)][64] floats
-constexpr int kGemvRows = 16;
+constexpr int kGemvRows = 16;      // rows the form below holds
+constexpr int kGemvUseRows = 8;    // rows it is used for: at 16 rows the cluster form measured
+                                   // faster (config 5 step 0.370 vs 0.386 ms)
 constexpr int kGemvCols = 16;
 constexpr int kGemvWarps = 16;
 constexpr int kGemvThreads = 32 * kGemvWarps;
@@ -808,7 +810,7 @@ int launch_linear(const LinearArgs& a, const LinearPlan& p, bool overlap, cudaSt
     return TMLLM_OK;
 }
 
-// ---- Projections of at most 16 rows (decode steps of up to 16 sequences) ----------------
+// ---- Projections of few rows (decode steps of up to 8 sequences) -------------------------
 // One CTA per 16 output columns (16 gate + 16 up columns with SwiGLU) over the whole K, no
 // split across CTAs.  The CTA's weight slice (K x 16 x NW halves, 18-80 KB for the BASELINE
 // models) is copied into shared memory before the dependency wait, so under programmatic
@@ -1663,7 +1665,7 @@ int tmllm_linear(const void* x, int64_t ldx, const void* norm_weight, const floa
     auto s = reinterpret_cast<cudaStream_t>(stream);
     const bool overlap = (flags & TMLLM_LINEAR_OVERLAP) != 0;
     int rc;
-    if (rows <= kGemvRows && (swiglu ? gemv_smem_bytes<2>(k, rows) : gemv_smem_bytes<1>(k, rows)) <=
+    if (rows <= kGemvUseRows && (swiglu ? gemv_smem_bytes<2>(k, rows) : gemv_smem_bytes<1>(k, rows)) <=
                                  static_cast<size_t>(kGemvSmemMax)) {
         rc = swiglu ? launch_gemv<2>(a, overlap, s) : launch_gemv<1>(a, overlap, s);
     } else {
