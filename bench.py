@@ -528,6 +528,82 @@ DECODER_WORKLOADS = {
 }
 
 
+def decoder_cpu_time(cfg, weights, lens, budget_s: float, threads: int):
+    """One decode token of the whole model on the host cores, per sequence, as the
+    reference's CPU-side chain would compute it: numpy float32 products over the F16 weights
+    with the reference's F16 storage points (normed rows, projections, residual sums, the
+    SwiGLU product, logits), RoPE and the faithful attention chain of the C oracle over the
+    sequence's cache (length from `lens`, random N(0,1) contents; `threads` host threads
+    for the attention), greedy argmax.  Sequences are taken in turn until the budget is
+    spent; returns (tokens, seconds, sample description)."""
+    import numpy as np
+
+    from oracle import oracle as orc
+    orc.build()
+    f32, f16 = np.float32, np.float16
+    hkv, d = cfg.num_kv_heads, cfg.head_dim
+    # the weights as host float32 (the conversion is not timed)
+    emb = weights.embedding.float().cpu().numpy()
+    layers = [{k: v.float().cpu().numpy() for k, v in L.items()} for L in weights.layers]
+    fnorm = weights.final_norm.float().cpu().numpy()
+    head = weights.lm_head.float().cpu().numpy()
+    rng = np.random.default_rng(77)
+    cos, sin = orc.rope_tables(d, max(lens) + 2, cfg.rope_theta)
+    sample_lens = lens[:8]  # up to eight sequences, an equal share of the budget each
+    tokens, t_total = 0, 0.0
+    for si, L in enumerate(sample_lens):
+        kc = [rng.standard_normal((1, hkv, L + 1, d), dtype=f32).astype(f16)
+              for _ in range(cfg.num_layers)]
+        vc = [rng.standard_normal((1, hkv, L + 1, d), dtype=f32).astype(f16)
+              for _ in range(cfg.num_layers)]
+        share_end = budget_s * (si + 1) / len(sample_lens)
+        while True:
+            t0 = time.perf_counter()
+            decoder_cpu_token(cfg, emb, layers, fnorm, head, kc, vc, L, cos, sin, rng, threads)
+            t_total += time.perf_counter() - t0
+            tokens += 1
+            if t_total >= share_end:
+                break
+    sample = (f"{tokens} decode tokens over {len(sample_lens)} sequence(s) of the workload's "
+              f"context lengths, one token at a time, all {cfg.num_layers} layers, attention "
+              f"on {threads} threads, time-boxed to {budget_s:.0f} s")
+    return tokens, t_total, sample
+
+
+def decoder_cpu_token(cfg, emb, layers, fnorm, head, kc, vc, L, cos, sin, rng, threads):
+    """The body of decoder_cpu_time: one token of one sequence at position L."""
+    import numpy as np
+
+    from oracle import oracle as orc
+    f32, f16 = np.float32, np.float16
+    hq, hkv, d = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+    inter, eps = cfg.intermediate_size, cfg.rms_norm_eps
+
+    def half(x):
+        return x.astype(f16).astype(f32)
+
+    def norm(x, w):
+        return half(x / np.sqrt((x * x).mean() + eps) * w)
+
+    x = half(emb[int(rng.integers(cfg.vocab_size))])
+    for li, W in enumerate(layers):
+        qkv = half(norm(x, W["attn_norm"]) @ W["wqkv"])
+        q = qkv[:hq * d].reshape(1, hq, 1, d).astype(f16)
+        kn = qkv[hq * d:(hq + hkv) * d].reshape(1, hkv, 1, d).astype(f16)
+        vn = qkv[(hq + hkv) * d:].reshape(1, hkv, 1, d).astype(f16)
+        q, kn = orc.rope(q, cos, sin, L), orc.rope(kn, cos, sin, L)
+        kc[li][:, :, L:L + 1] = kn
+        vc[li][:, :, L:L + 1] = vn
+        att = orc.attention_core(q, kc[li], vc[li], L + 1, L, threads=threads)
+        x = half(x + half(att.astype(f32).reshape(-1) @ W["wo"]))
+        gu = half(norm(x, W["mlp_norm"]) @ W["wgu"])
+        g, u = gu[:inter], gu[inter:]
+        act = half(g / (1.0 + np.exp(-g)) * u)
+        x = half(x + half(act @ W["wd"]))
+    logits = half(norm(x, fnorm) @ head)
+    return int(np.argmax(logits))
+
+
 def run_decoder(args) -> None:
     import torch
     import torch.distributed as dist
@@ -647,6 +723,12 @@ def run_decoder(args) -> None:
             "gpu_launches": steps * (1 + cfg.num_layers * (5 if dec.fused else 4) +
                                      (1 if dec.head else 2) + 1),
         }
+        if world == 1 and not args.no_cpu:
+            threads = os.cpu_count() or 1
+            lens = [ctx[s] + steps // 2 for s in mine]
+            n_tok, secs, sample = decoder_cpu_time(cfg, w, lens, args.cpu_budget, threads)
+            line["cpu_baseline"] = {"value": n_tok / secs, "unit": "tok/s", "cores": threads,
+                                    "kind": "port", "sample": sample}
         if prefill_ms is not None:
             line["prefill"] = {"ms": prefill_ms, "tok_s": B * prompt / (prefill_ms * 1e-3),
                                "scope": f"{B} prompts x {prompt} tokens, whole model (GEMMs "
