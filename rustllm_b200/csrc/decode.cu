@@ -1710,15 +1710,17 @@ int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
     if (hint > capacity) hint = capacity;
     int32_t splits = o.num_splits > 0 ? o.num_splits : auto_splits(B, Hkv, hint);
     if (splits > 1024) splits = 1024;
+    // positions per split: a multiple of 128 from a split count, a multiple of 32 (one
+    // positions-major item) when the caller chose the chunk from the sequence lengths
     int64_t chunk = (hint + splits - 1) / splits;
+    chunk = ((chunk + 127) / 128) * 128;
     if (chunk_override > 0) {
-        chunk = chunk_override;
-        int64_t s2 = (hint + ((chunk + 127) / 128) * 128 - 1) / (((chunk + 127) / 128) * 128);
+        chunk = ((chunk_override + 31) / 32) * 32;
+        int64_t s2 = (hint + chunk - 1) / chunk;
         if (s2 < 1) s2 = 1;
         if (s2 > 1024) s2 = 1024;
         splits = static_cast<int32_t>(s2);
     }
-    chunk = ((chunk + 127) / 128) * 128;
     if (chunk < 128) chunk = 128;
     if (chunk > INT32_MAX) chunk = INT32_MAX;
 
@@ -1839,14 +1841,14 @@ int decode_resident_ctas(int dtype, int head_dim, int variant, int group) {
 // sequences of a mixed batch are cut without pushing work into a second wave.  The CTA
 // count grows with the split count, so the largest fitting count is found by bisection.
 // Positions per split for a batch whose lengths the host knows: the smallest multiple of
-// 128 whose CTAs -- ceil(len / chunk) per sequence and KV head -- fit one wave of resident
+// 32 whose CTAs -- ceil(len / chunk) per sequence and KV head -- fit one wave of resident
 // CTAs (`per_sm` per SM), so only the sequences longer than the chunk are cut and no work
 // spills into a second wave.  The same floors as the split-count choice below: never under
 // 256 positions, and >= 1024 once one CTA per (sequence, KV head) covers every SM.  Finer
 // than choosing a split count (chunk = ceil(longest / s)): 64 sequences of 256-2048
-// positions x 5 KV heads at 3 CTAs per SM fit chunks of 1408 (435 CTAs), where 2 splits
-// (chunks of 1152) would need a second wave.  Returns the chunk, or the longest length
-// rounded up when even one chunk per sequence overflows the wave.
+// positions x 5 KV heads at 3 CTAs per SM fit chunks of 1440 (440 CTAs; 1536 in steps of
+// 128), where 2 splits (chunks of 1152) would need a second wave.  Returns the chunk, or
+// the longest length rounded up when even one chunk per sequence overflows the wave.
 int64_t decode_auto_chunk_lens(const int64_t* lens, int64_t B, int64_t Hkv, int64_t hint,
                                int per_sm) {
     const int64_t slots = static_cast<int64_t>(device_sm_count()) * per_sm;
@@ -1859,18 +1861,19 @@ int64_t decode_auto_chunk_lens(const int64_t* lens, int64_t B, int64_t Hkv, int6
         }
         return n * Hkv;
     };
-    int64_t hi = (hint + 127) / 128;  // in units of 128 positions
-    int64_t lo = 2;                   // never under 256 positions
-    if (B * Hkv >= static_cast<int64_t>(device_sm_count())) lo = 8;  // >= 1024
-    if (hint > 1024 * 128 * 1024) lo = (hint / 1024 + 127) / 128;    // at most 1024 splits
+    int64_t hi = (hint + 31) / 32;  // in units of 32 positions
+    int64_t lo = 8;                 // never under 256 positions
+    if (B * Hkv >= static_cast<int64_t>(device_sm_count())) lo = 32;  // >= 1024
+    const int64_t lo_splits = ((hint + 1023) / 1024 + 31) / 32;  // at most 1024 splits
+    if (lo < lo_splits) lo = lo_splits;
     if (lo > hi) lo = hi;
-    if (ctas(hi * 128) > slots) return hi * 128;
-    while (lo < hi) {  // smallest k in [lo, hi] with ctas(128 k) <= slots
+    if (ctas(hi * 32) > slots) return hi * 32;
+    while (lo < hi) {  // smallest k in [lo, hi] with ctas(32 k) <= slots
         const int64_t mid = (lo + hi) / 2;
-        if (ctas(mid * 128) <= slots) hi = mid;
+        if (ctas(mid * 32) <= slots) hi = mid;
         else lo = mid + 1;
     }
-    return lo * 128;
+    return lo * 32;
 }
 
 int32_t decode_auto_splits_lens(const int64_t* lens, int64_t B, int64_t Hkv, int64_t hint,
