@@ -248,7 +248,9 @@ int tmllm_argmax(tmllm_dtype dtype, const void* logits, int32_t* ids, size_t row
  * rows <= 64 (with rows x k small enough for the rows to sit in shared memory: k <= 1344
  * at 64 rows); k and n multiples of 8; ldx / ldr / ldw / ld_logits multiples of 8 and x,
  * residual, w, logits and norm_weight 16-byte aligned.  flags: TMLLM_LINEAR_OVERLAP as for
- * tmllm_linear (w may be read before the work queued ahead on `stream` has finished). */
+ * tmllm_linear (w may be read before the work queued ahead on `stream` has finished).  Its
+ * device-side waits are bounded: an expired one is reported by tmllm_linear_status (the
+ * outputs of that call are then undefined; the workspace is still left zeroed). */
 size_t tmllm_lm_head_workspace_bytes(void);
 int tmllm_lm_head(const void* x, int64_t ldx, const void* residual, int64_t ldr,
                   const void* norm_weight, float eps, const void* w, int64_t ldw, void* logits,
