@@ -54,7 +54,7 @@ CFG4_CONFIG = {"workload": "cfg4 long-context decode attention op (Llama-3-8B at
 # captured on: `roofline.traffic` is reported only while rustllm_b200/csrc/decode.cu still
 # has that SHA-256.
 NCU_TRAFFIC = {"bytes_per_launch": 537.5e6,
-               "decode_cu_sha256": "e0f83df1a927fbc3db71aa5fc4a6ca91d53e6457bcc5d43a6d2ae57e8170d495"}
+               "decode_cu_sha256": "7ceae295d2d81b3fba506620e6f933281e41c3f7b306a1bdbbc2e107034c7242"}
 # Untimed steps run between the warm-up and the timed region so the GPU's clocks have left
 # their idle state (the clock sampler's start-up pause idles the GPU for 0.4 s).
 SETTLE_STEPS = 2000

@@ -1710,10 +1710,11 @@ int decode_impl_ex(const tmllm_paged_kv* kv, const void* q, const void* k_new,
     if (hint > capacity) hint = capacity;
     int32_t splits = o.num_splits > 0 ? o.num_splits : auto_splits(B, Hkv, hint);
     if (splits > 1024) splits = 1024;
-    // positions per split: a multiple of 128 from a split count, a multiple of 32 (one
-    // positions-major item) when the caller chose the chunk from the sequence lengths
+    // positions per split: a multiple of 32 (one positions-major item), so the splits of a
+    // long sequence come out nearly equal (config 4 at 8 ranks: 37 x 448 instead of 33 x 512
+    // with 4 of the 37 CTAs a KV head idle)
     int64_t chunk = (hint + splits - 1) / splits;
-    chunk = ((chunk + 127) / 128) * 128;
+    chunk = ((chunk + 31) / 32) * 32;
     if (chunk_override > 0) {
         chunk = ((chunk_override + 31) / 32) * 32;
         int64_t s2 = (hint + chunk - 1) / chunk;
