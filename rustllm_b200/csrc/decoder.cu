@@ -1336,7 +1336,9 @@ __global__ void __launch_bounds__(kHeadThreads)
         for (int q = 0; q < total; ++q) {
             const int kk = q % ks, slot = q % S;
             const bool ok = lin_wait(full0 + 8 * slot, static_cast<uint32_t>((q / S) & 1));
-            if (!__all_sync(0xffffffffu, ok) || flags_s[1]) {
+            // one decision for the whole warp (the MMAs below are warp-collective): give up
+            // when any lane's wait expired or another warp has given up
+            if (!__all_sync(0xffffffffu, ok) || __any_sync(0xffffffffu, flags_s[1] != 0)) {
                 flags_s[1] = 1;
                 break;
             }
