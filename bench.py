@@ -1352,7 +1352,7 @@ def run_kernel_survey(args) -> None:
                              (hid, 2560, True, "gate/up + SwiGLU 960x5120"),
                              (2560, 960, False, "down 2560x960")]:
         w = (rnd(kk, 2 * nn if sw else nn) / 30).to(H)
-        for rows, kern in ((8, "gemv_kernel"), (64, "linear_kernel")):
+        for rows, kern in ((8, "linear_kernel"), (64, "linear_kernel")):
             xin = rnd(rows, kk)
             outl = torch.empty((rows, nn), dtype=H, device=dev)
             timed(f"projection {rows} rows, {what}", kern,

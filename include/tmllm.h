@@ -209,11 +209,9 @@ int tmllm_swiglu(tmllm_dtype dtype, const void* gate_up, void* out, size_t rows,
  * flags: TMLLM_LINEAR_OVERLAP lets the launch overlap the tail of the work queued before it
  * on `stream` (programmatic dependent launch): w is read before that work has finished, so
  * the caller promises that it does not write w; x, residual, stats_in and norm_weight are
- * read only after it has finished.  Up to 8 rows and 9-64 rows run two different forms
- * (one CTA per 16 columns over the whole k; K split over a thread-block cluster); within
- * each range the result does not depend on `rows` beyond the row itself: a row computed
- * alone equals the same row in any batch of at most 8 rows, and any two batches of 9-64
- * rows agree on a common row bit for bit. */
+ * read only after it has finished.  The summation order depends on k and n only, so the
+ * result does not depend on `rows` beyond the row itself: a row computed alone equals the
+ * same row in any batch, bit for bit. */
 #define TMLLM_LINEAR_OVERLAP 1u
 size_t tmllm_linear_stats_bytes(int32_t n);
 /* Reads and clears the status word of tmllm_linear's kernels: TMLLM_TIMEOUT when a bounded

@@ -279,17 +279,9 @@ constexpr int kLinK = 64;
 constexpr int kLinThreads = 128;
 constexpr int kLinMaxSplits = 8;                 // portable cluster size
 constexpr int kLinSlab = kLinK * kLinCols * 2;  // one 64 x 64 F16 tile (weight or x)
-// the small-batch form below (gemv_kernel); row statistics hold one partial sum of squares
-// per 16 output columns and row: [ceil(N / 16)][64] floats
-constexpr int kGemvRows = 16;      // rows the form below holds
-constexpr int kGemvUseRows = 8;    // rows it is used for: at 16 rows the cluster form measured
-                                   // faster (config 5 step 0.370 vs 0.386 ms)
-constexpr int kGemvCols = 16;
-constexpr int kGemvWarps = 16;
-constexpr int kGemvThreads = 32 * kGemvWarps;
-constexpr int kGemvOffInv = kGemvWarps * 2 * kGemvRows * kGemvCols * 4;  // after the partials
-constexpr int kGemvOffW = kGemvOffInv + 128;
-constexpr int kGemvSmemMax = 227 * 1024;
+// row statistics hold one partial sum of squares per 16 output columns and row:
+// [ceil(N / 16)][64] floats
+constexpr int kStatCols = 16;
 
 constexpr unsigned long long kLinWaitNs = 1000000000ull;  // bounded waits: 1 s
 
@@ -369,7 +361,7 @@ __device__ __forceinline__ void rows_inv_from_stats(const float* __restrict__ st
     while (gp < groups) gp <<= 1;
     const int P = min(32, THREADS / gp);
     const int grp = tid / P, part = tid % P;
-    const int kt = (K + kGemvCols - 1) / kGemvCols;
+    const int kt = (K + kStatCols - 1) / kStatCols;
     float s[4] = {0.f, 0.f, 0.f, 0.f};
     if (grp < groups) {
         for (int t0 = part; t0 < kt; t0 += 8 * P) {
@@ -729,7 +721,7 @@ __global__ void __launch_bounds__(kLinThreads) linear_kernel(const LinearArgs a)
         if (a.stats_out) {  // one partial per 16 columns: chunks 2j and 2j+1 of the row
             sq += __shfl_xor_sync(0xffffffffu, sq, 1);
             if (src != nullptr && (c & 1) == 0 && (q >> 3) < mine && col < a.N)
-                a.stats_out[(tile * (kLinCols / kGemvCols) + (c >> 1)) * kLinRows + m] = sq;
+                a.stats_out[(tile * (kLinCols / kStatCols) + (c >> 1)) * kLinRows + m] = sq;
         }
     }
     if (splits > 1 && tid < splits)  // the pushed rows have left this CTA's shared memory
@@ -807,276 +799,6 @@ int launch_linear(const LinearArgs& a, const LinearPlan& p, bool overlap, cudaSt
     cfg.attrs = attr;
     cfg.numAttrs = overlap ? 2 : 1;
     TMLLM_CUDA_TRY(cudaLaunchKernelEx(&cfg, linear_kernel<NW>, a));
-    return TMLLM_OK;
-}
-
-// ---- Projections of few rows (decode steps of up to 8 sequences) -------------------------
-// One CTA per 16 output columns (16 gate + 16 up columns with SwiGLU) over the whole K, no
-// split across CTAs.  The CTA's weight slice (K x 16 x NW halves, 18-80 KB for the BASELINE
-// models) is copied into shared memory before the dependency wait, so under programmatic
-// dependent launch it streams while the kernel ahead drains; after the wait only the rows
-// (from L2), the products and one reduction over the CTA's 16 warps remain.  The product is
-// computed transposed on the warp-level tensor cores: A = the weight slice (its 16 columns
-// are the M = 16 side of mma.m16n8k16), B = the rows (8 rows per n-tile, one or two tiles),
-// each warp a contiguous sixteenth of K (two accumulator sets, even and odd steps).  Inside each 16-deep step the K index is permuted
-// (slot 2t+j holds k = 4t+j, slot 8+2t+j holds k = 4t+2+j, j < 2) so that a lane's B
-// fragment is four consecutive elements of one row: a single 8-byte load, normalised in
-// registers (half(x * inv * w), the reference's rounding of the normed row); the weight
-// rows are staged in slot order so ldmatrix produces the matching A fragments.  The sum
-// over K runs in a fixed order (per warp, then warps 0..15), so results are identical run to
-// run and a row's result does not depend on the other rows of the call.
-
-// shared-memory row (slot) of weight row k: the permutation above within each 16-row step
-__host__ __device__ __forceinline__ int gemv_slot(int k) {
-    const int p = k & 15;
-    return (k & ~15) | ((p & 2) << 2) | ((p >> 2) << 1) | (p & 1);
-}
-// 16-byte chunk position of logical chunk c in slot row r (C = 2 * NW chunks a row): rows
-// are 32 * NW bytes, so the eight rows of an ldmatrix tile are spread over all 32 banks
-template <int NW>
-__device__ __forceinline__ int gemv_chunk(int r, int c) {
-    constexpr int C = 2 * NW, SHIFT = NW == 1 ? 2 : 1;  // 8 / C rows per 128 bytes
-    return c ^ ((r >> SHIFT) & (C - 1));
-}
-// shared memory: partials and 1/rms, the weight slice, the norm weight, then the rows (2k + 16 bytes each:
-// the 16-byte pad spreads the 8-byte B fragment reads of 8 rows over the banks)
-template <int NW>
-size_t gemv_smem_bytes(int k, int rows) {
-    const size_t kp = static_cast<size_t>((k + 15) / 16) * 16;
-    return static_cast<size_t>(kGemvOffW) + kp * 32 * NW + kp * 2 +
-           static_cast<size_t>(rows) * (2 * static_cast<size_t>(k) + 16);
-}
-
-template <int NW>
-__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const LinearArgs a) {
-    extern __shared__ __align__(128) unsigned char smem[];
-    float* red = reinterpret_cast<float*>(smem);                   // [warp][NW][16 m][16 n]
-    float* inv_s = reinterpret_cast<float*>(smem + kGemvOffInv);   // [16]
-    unsigned char* ws = smem + kGemvOffW;                          // [Kp slots][C chunks]
-    constexpr int C = 2 * NW;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n0 = blockIdx.x * kGemvCols;
-    const int K = a.K, M = a.M;
-    const int kp = (K + 15) & ~15;
-    const int xstride = 2 * K + 16;                                // bytes per staged row
-    unsigned char* nws = ws + kp * 16 * C;                         // [Kp] norm weight
-    unsigned char* xs = nws + kp * 2;                              // [M][K] (+ pad)
-    const bool norm = a.norm_w != nullptr;
-    launch_dependents();  // the next projection may start staging its weights
-
-    // the weight slice, in slot order (chunks past N or rows past K are zero-filled)
-    for (int i = tid; i < kp * C; i += kGemvThreads) {
-        const int k = i / C, c = i % C;
-        const int col = n0 + (c & 1) * 8;
-        const bool ok = k < K && col < a.N;
-        const __half* src = ok ? a.w + static_cast<int64_t>(k) * a.ldw + (c >> 1) * a.N + col : a.w;
-        const int r = gemv_slot(k);
-        cp_async16(ws + r * (16 * C) + (gemv_chunk<NW>(r, c) << 4), src, ok ? 16 : 0);
-    }
-    if (norm)  // the norm weight (constant too)
-        for (int c = tid; c < kp / 8; c += kGemvThreads)
-            cp_async16(nws + c * 16, c * 8 < K ? a.norm_w + c * 8 : a.norm_w, c * 8 < K ? 16 : 0);
-    cp_async_commit();
-    grid_dependency_wait();  // from here on the rows, statistics and residual are current
-
-    // the residual of this lane's output chunk (warp 0: row q/2, columns (q&1)*8..+7)
-    const int q = lane, qm = q >> 1, qcol = n0 + (q & 1) * 8;
-    const bool qlive = warp == 0 && qm < M && qcol < a.N;
-    uint4 resid = make_uint4(0, 0, 0, 0);
-    if (a.resid && qlive)
-        resid = __ldcg(reinterpret_cast<const uint4*>(a.resid + static_cast<int64_t>(qm) * a.ldr + qcol));
-    // the rows, all at once
-    for (int i = tid; i < M * (K / 8); i += kGemvThreads) {
-        const int m = i / (K / 8), c = i % (K / 8);
-        cp_async16(xs + m * xstride + c * 16, a.x + static_cast<int64_t>(m) * a.ldx + c * 8, 16);
-    }
-    cp_async_commit();
-    // 1/rms of every row: from the statistics the producing call wrote while the rows land,
-    // else from the staged rows (16 threads a row, a fixed reduction order)
-    if (norm && a.stats_in) rows_inv_from_stats<kGemvThreads>(a.stats_in, M, K, a.eps, inv_s);
-    cp_async_wait<0>();
-    __syncthreads();
-    if (norm && !a.stats_in) {
-        const int nm = tid >> 4, part = tid & 15;
-        float ss = 0.f;
-        if (nm < M) {
-            for (int c = part; c < K / 8; c += 16) {
-                float f[8];
-                Chunk<__half>::unpack(*reinterpret_cast<const uint4*>(xs + nm * xstride + c * 16), f);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
-            }
-        }
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        if (part == 0 && nm < M) inv_s[nm] = rsqrtf(ss / static_cast<float>(K) + a.eps);
-        __syncthreads();
-    }
-
-    // this warp's contiguous share of the 16-deep steps
-    const int steps = kp / 16;
-    const int per = (steps + kGemvWarps - 1) / kGemvWarps;
-    const int s0 = warp * per, s1 = min(steps, s0 + per);
-    const int g = lane >> 2, t = lane & 3;
-    const bool two = M > 8;  // a second 8-row tile
-    const float inv0 = norm && g < M ? inv_s[g] : 0.f;
-    const float inv1 = norm && g + 8 < M ? inv_s[g + 8] : 0.f;
-    const unsigned char* x0 = xs + g * xstride;
-    const unsigned char* x1 = xs + (g + 8) * xstride;
-    // two accumulator sets (even and odd steps), so consecutive products do not wait for
-    // each other; added in a fixed order at the end
-    float acc[2][NW][2][4];
-#pragma unroll
-    for (int z = 0; z < 2; ++z)
-#pragma unroll
-        for (int h = 0; h < NW; ++h)
-#pragma unroll
-            for (int b = 0; b < 2; ++b)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) acc[z][h][b][e] = 0.f;
-    // ldmatrix row of this lane: matrix lane/8 = (slot half, column half), row lane%8
-    const int lm = lane >> 3, lr = lane & 7;
-    // B fragment: four consecutive elements of one row, normalised and rounded to F16
-    auto frag = [&](const unsigned char* row, bool live, float inv, int kx, float4 nwv,
-                    uint32_t& b0, uint32_t& b1) {
-        uint2 v = make_uint2(0, 0);
-        if (live && kx < K) v = *reinterpret_cast<const uint2*>(row + kx * 2);
-        if (norm) {
-            const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
-            const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
-            b0 = pack_half2(f0.x * inv * nwv.x, f0.y * inv * nwv.y);
-            b1 = pack_half2(f1.x * inv * nwv.z, f1.y * inv * nwv.w);
-        } else {
-            b0 = v.x;
-            b1 = v.y;
-        }
-    };
-    auto step = [&](int s, float (&ac)[NW][2][4]) {
-        const int kx = s * 16 + 4 * t;
-        float4 nwv = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (norm) {
-            const uint2 nv = *reinterpret_cast<const uint2*>(nws + kx * 2);
-            const float2 n0f = __half22float2(*reinterpret_cast<const __half2*>(&nv.x));
-            const float2 n1f = __half22float2(*reinterpret_cast<const __half2*>(&nv.y));
-            nwv = make_float4(n0f.x, n0f.y, n1f.x, n1f.y);
-        }
-        uint32_t b[2][2];
-        frag(x0, g < M, inv0, kx, nwv, b[0][0], b[0][1]);
-        if (two) frag(x1, g + 8 < M, inv1, kx, nwv, b[1][0], b[1][1]);
-        const int r = s * 16 + (lm >> 1) * 8 + lr;
-#pragma unroll
-        for (int h = 0; h < NW; ++h) {
-            uint32_t a0, a1, a2, a3;
-            ldsm_x4_t(static_cast<uint32_t>(__cvta_generic_to_shared(
-                          ws + r * (16 * C) + (gemv_chunk<NW>(r, 2 * h + (lm & 1)) << 4))),
-                      a0, a1, a2, a3);
-            // matrices: (slots 0-7, columns 0-7), (slots 0-7, columns 8-15),
-            // (slots 8-15, columns 0-7), (slots 8-15, columns 8-15)
-            mma16816(ac[h][0], a0, a1, a2, a3, b[0][0], b[0][1]);
-            if (two) mma16816(ac[h][1], a0, a1, a2, a3, b[1][0], b[1][1]);
-        }
-    };
-    for (int s = s0; s < s1; s += 2) {
-        step(s, acc[0]);
-        if (s + 1 < s1) step(s + 1, acc[1]);
-    }
-#pragma unroll
-    for (int h = 0; h < NW; ++h)
-#pragma unroll
-        for (int b = 0; b < 2; ++b)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[0][h][b][e] += acc[1][h][b][e];
-    // this warp's partial: fragment e of tile b is column g (+8 for e >= 2), row
-    // b*8 + 2t + (e & 1)
-#pragma unroll
-    for (int h = 0; h < NW; ++h)
-#pragma unroll
-        for (int b = 0; b < 2; ++b)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int m = b * 8 + 2 * t + (e & 1), n = g + 8 * (e >> 1);
-                red[((warp * NW + h) * kGemvRows + m) * kGemvCols + n] = acc[0][h][b][e];
-            }
-    __syncthreads();
-    if (warp != 0) return;
-
-    // warp 0: lane q finishes row q/2, columns (q&1)*8..+7 (every warp's partial summed in
-    // warp order), with the residual added or SwiGLU applied, and the row's sum of squares
-    // over the CTA's 16 columns
-    float sq = 0.f;
-    if (qlive) {
-        float gsum[8], usum[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) gsum[e] = usum[e] = 0.f;
-#pragma unroll
-        for (int w = 0; w < kGemvWarps; ++w) {
-#pragma unroll
-            for (int h = 0; h < NW; ++h) {
-                const float4* p = reinterpret_cast<const float4*>(
-                    red + ((w * NW + h) * kGemvRows + qm) * kGemvCols + (q & 1) * 8);
-                const float4 lo = p[0], hi = p[1];
-                float* d = h == 0 ? gsum : usum;
-                d[0] += lo.x; d[1] += lo.y; d[2] += lo.z; d[3] += lo.w;
-                d[4] += hi.x; d[5] += hi.y; d[6] += hi.z; d[7] += hi.w;
-            }
-        }
-        float y[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const float gh = __half2float(__float2half_rn(gsum[e]));
-            if (NW == 1) {
-                y[e] = gh;
-            } else {
-                const float uh = __half2float(__float2half_rn(usum[e]));
-                y[e] = (gh / (1.0f + expf(-gh))) * uh;
-            }
-        }
-        if (a.resid) {
-            float r[8];
-            Chunk<__half>::unpack(resid, r);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) y[e] = __fadd_rn(y[e], r[e]);
-        }
-        uint4 o;
-        __half2* oh = reinterpret_cast<__half2*>(&o);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            oh[e] = __floats2half2_rn(y[2 * e], y[2 * e + 1]);
-            const float2 f = __half22float2(oh[e]);
-            sq = fmaf(f.x, f.x, sq);
-            sq = fmaf(f.y, f.y, sq);
-        }
-        *reinterpret_cast<uint4*>(a.out + static_cast<int64_t>(qm) * a.ldo + qcol) = o;
-    }
-    if (a.stats_out) {
-        sq += __shfl_xor_sync(0xffffffffu, sq, 1);
-        if ((q & 1) == 0 && qm < M) a.stats_out[blockIdx.x * kLinRows + qm] = sq;
-    }
-}
-
-template <int NW>
-int launch_gemv(const LinearArgs& a, bool overlap, cudaStream_t s) {
-    static std::atomic<uint64_t> opted{0};
-    int dev = 0;
-    TMLLM_CUDA_TRY(cudaGetDevice(&dev));
-    const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
-    if (!bit || !(opted.load(std::memory_order_relaxed) & bit)) {
-        TMLLM_CUDA_TRY(cudaFuncSetAttribute(gemv_kernel<NW>,
-                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            kGemvSmemMax));
-        opted.fetch_or(bit, std::memory_order_relaxed);
-    }
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(static_cast<unsigned>((a.N + kGemvCols - 1) / kGemvCols));
-    cfg.blockDim = dim3(kGemvThreads);
-    cfg.dynamicSmemBytes = gemv_smem_bytes<NW>(a.K, a.M);
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = overlap ? 1 : 0;
-    TMLLM_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_kernel<NW>, a));
     return TMLLM_OK;
 }
 
@@ -1612,7 +1334,7 @@ int tmllm_linear_status(int32_t* status) {
 
 size_t tmllm_linear_stats_bytes(int32_t n) {
     if (n <= 0) return 0;
-    return static_cast<size_t>((n + kGemvCols - 1) / kGemvCols) * kLinRows * sizeof(float);
+    return static_cast<size_t>((n + kStatCols - 1) / kStatCols) * kLinRows * sizeof(float);
 }
 
 int tmllm_linear(const void* x, int64_t ldx, const void* norm_weight, const float* stats_in,
@@ -1667,10 +1389,7 @@ int tmllm_linear(const void* x, int64_t ldx, const void* norm_weight, const floa
     auto s = reinterpret_cast<cudaStream_t>(stream);
     const bool overlap = (flags & TMLLM_LINEAR_OVERLAP) != 0;
     int rc;
-    if (rows <= kGemvUseRows && (swiglu ? gemv_smem_bytes<2>(k, rows) : gemv_smem_bytes<1>(k, rows)) <=
-                                 static_cast<size_t>(kGemvSmemMax)) {
-        rc = swiglu ? launch_gemv<2>(a, overlap, s) : launch_gemv<1>(a, overlap, s);
-    } else {
+    {
         const LinearPlan p = swiglu ? plan_linear<2>(k, n) : plan_linear<1>(k, n);
         a.kchunk = p.kchunk;
         rc = swiglu ? launch_linear<2>(a, p, overlap, s) : launch_linear<1>(a, p, overlap, s);
