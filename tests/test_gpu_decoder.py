@@ -239,14 +239,17 @@ def test_model_dir_round_trip_gives_identical_logits(cuda, tmp_path):
         DecoderWeights.from_weights(TINY, bad, device=cuda)
 
 
-def test_fused_step_matches_library_step(cuda):
+@pytest.mark.parametrize("batch", [4, 40])
+def test_fused_step_matches_library_step(cuda, batch):
     """The decode step with fused projections (tmllm_linear: norm, SwiGLU and residual adds
     folded in) gives the logits of the step built from cuBLAS GEMMs and the separate norm
-    and SwiGLU kernels."""
+    and SwiGLU kernels, for a few sequences (fused head too) and for a batch above 16 (the
+    cuBLAS head after fused projections)."""
     w = DecoderWeights(TINY, device=cuda, seed=13, std=0.08)
-    prompts = torch.randint(0, TINY.vocab_size, (4, 20), generator=torch.Generator().manual_seed(14))
-    a = Decoder(TINY, w, 4, device=cuda)
-    b = Decoder(TINY, w, 4, device=cuda)
+    prompts = torch.randint(0, TINY.vocab_size, (batch, 20),
+                            generator=torch.Generator().manual_seed(14))
+    a = Decoder(TINY, w, batch, device=cuda)
+    b = Decoder(TINY, w, batch, device=cuda)
     assert a.fused
     b.fused = False
     for dec in (a, b):
